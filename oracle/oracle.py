@@ -1,0 +1,212 @@
+"""ctypes front-end of the CPU checkers.  TEST INFRASTRUCTURE ONLY.
+
+* ``liboracle.so`` -- ftoracle.c, the C restatement of the reference path.
+* ``_ref/libftref.so`` -- the reference's own ``ft/src/cpu_backend.cpp``
+  compiled from its sources (oracle/Makefile), reached through ref_shim.cpp.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use
+this module; the product path never does.
+"""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = os.path.join(HERE, "liboracle.so")
+_REF = os.path.join(HERE, "_ref", "libftref.so")
+
+_f = C.c_float
+_i64 = C.c_int64
+_p = C.c_void_p
+
+
+def build():
+    """Compile liboracle.so (and _ref/libftref.so where the reference tree
+    exists) with oracle/Makefile."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _load(path):
+    lib = C.CDLL(path)
+    return lib
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB):
+            build()
+        _lib = _load(_LIB)
+        _lib.ftor_half_to_float.restype = _f
+        _lib.ftor_half_to_float.argtypes = [C.c_uint16]
+        _lib.ftor_float_to_half.restype = C.c_uint16
+        _lib.ftor_float_to_half.argtypes = [_f]
+        _lib.ftor_dot_row_f32.restype = _f
+        _lib.ftor_dot_row_f32.argtypes = [_p, _p, C.c_int, _i64]
+        _lib.ftor_dequant_row.argtypes = [_p, _p, C.c_int, _i64]
+        _lib.ftor_matmul.argtypes = [_p, _i64, _i64, _p, C.c_int, _i64, _i64, _p, C.c_int]
+        _lib.ftor_expert_chunk.argtypes = [_p, _p, _p, _p, _p, C.c_int, _i64, _i64, _i64,
+                                           _i64, _i64, C.c_int]
+        _lib.ftor_expert_ffn.argtypes = [_p, _p, _p, _p, _p, C.c_int, _i64, _i64, _i64,
+                                         _i64, _i64, C.c_int]
+        _lib.ftor_route_topk.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p]
+        _lib.ftor_moe_ffn.argtypes = [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
+                                      C.c_int, _p, C.c_int]
+        for fn in ("ftor_block_elems", "ftor_block_bytes", "ftor_row_bytes"):
+            getattr(_lib, fn).restype = _i64
+        _lib.ftor_row_bytes.argtypes = [C.c_int, _i64]
+    return _lib
+
+
+def have_ref():
+    return os.path.exists(_REF)
+
+
+def ref():
+    """The reference's own CPU code (None when _ref was never built)."""
+    global _ref
+    if _ref is None and have_ref():
+        r = _load(_REF)
+        r.ftref_half_to_float.restype = _f
+        r.ftref_half_to_float.argtypes = [C.c_uint16]
+        r.ftref_float_to_half.restype = C.c_uint16
+        r.ftref_float_to_half.argtypes = [_f]
+        r.ftref_dequant_row.argtypes = [_p, _p, C.c_uint32, _i64]
+        r.ftref_dot_row_f32.argtypes = [_p, _p, C.c_uint32, _i64, _p]
+        r.ftref_matmul.argtypes = [_p, _i64, _i64, _p, C.c_uint32, _i64, _p, C.c_int]
+        r.ftref_run_expert_chunk.argtypes = [_p, _p, _p, _p, _p, C.c_uint32, _i64, _i64, _i64,
+                                             C.c_size_t, C.c_size_t, C.c_int]
+        _ref = r
+    return _ref
+
+
+def _ptr(a):
+    return a.ctypes.data_as(_p)
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def _check(rc, what):
+    if rc != 0:
+        raise RuntimeError(f"{what} failed (rc={rc})")
+
+
+# ----------------------------------------------------------------- oracle
+
+def dequant_rows(w, dtype, k):
+    """Dequantize every row of ``w`` ``[n, row_bytes]`` -> fp32 ``[n, k]``."""
+    w = _c(w, np.uint8)
+    n = w.shape[0]
+    out = np.empty((n, k), dtype=np.float32)
+    for r in range(n):
+        _check(lib().ftor_dequant_row(_ptr(out[r]), _ptr(w[r]), dtype, k), "ftor_dequant_row")
+    return out
+
+
+def dot_row(x, wrow, dtype, k):
+    x = _c(x, np.float32)
+    wrow = _c(wrow, np.uint8)
+    return float(lib().ftor_dot_row_f32(_ptr(x), _ptr(wrow), dtype, k))
+
+
+def matmul(x, w, dtype, k, threads=1):
+    """Per-row semantics ``y[m][n] = dot(x_m, W_n)``; x fp32 ``[m, k]``."""
+    x = _c(x, np.float32).reshape(-1, k)
+    w = _c(w, np.uint8)
+    m, n = x.shape[0], w.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    _check(lib().ftor_matmul(_ptr(x), m, k, _ptr(w), dtype, n, w.shape[1], _ptr(y), threads),
+           "ftor_matmul")
+    return y
+
+
+def expert_chunk(x, out, gate, up, down, dtype, k, ic, threads=1):
+    """Reference-layout expert chunk (down rows = neurons); ``out`` += ..."""
+    x = _c(x, np.float32)
+    assert out.dtype == np.float32 and out.flags.c_contiguous
+    gate, up, down = (_c(a, np.uint8) for a in (gate, up, down))
+    m = x.shape[0]
+    _check(lib().ftor_expert_chunk(_ptr(x), _ptr(out), _ptr(gate), _ptr(up), _ptr(down), dtype,
+                                   m, k, ic, gate.shape[1], down.shape[1], threads),
+           "ftor_expert_chunk")
+    return out
+
+
+def expert_ffn(x, out, gate, up, down, dtype, k, n_ff, threads=1):
+    """Standard-layout expert FFN (down ``[k][n_ff]``); ``out`` += ..."""
+    x = _c(x, np.float32)
+    assert out.dtype == np.float32 and out.flags.c_contiguous
+    gate, up, down = (_c(a, np.uint8) for a in (gate, up, down))
+    m = x.shape[0]
+    _check(lib().ftor_expert_ffn(_ptr(x), _ptr(out), _ptr(gate), _ptr(up), _ptr(down), dtype,
+                                 m, k, n_ff, gate.shape[1], down.shape[1], threads),
+           "ftor_expert_ffn")
+    return out
+
+
+def route_topk(logits, u):
+    logits = _c(logits, np.float32)
+    t, e = logits.shape
+    idx = np.empty((t, u), dtype=np.int32)
+    w = np.empty((t, u), dtype=np.float32)
+    _check(lib().ftor_route_topk(_ptr(logits), None, t, e, u, _ptr(idx), _ptr(w)),
+           "ftor_route_topk")
+    return idx, w
+
+
+def moe_ffn(x, logits, gate_exps, up_exps, down_exps, dtype, k, n_ff, u, threads=1):
+    """Routed-expert MoE FFN; returns ``out[t][k]`` (starting from zero)."""
+    x = _c(x, np.float32)
+    logits = _c(logits, np.float32)
+    gate_exps, up_exps, down_exps = (_c(a, np.uint8) for a in (gate_exps, up_exps, down_exps))
+    t, e = logits.shape
+    out = np.zeros((t, k), dtype=np.float32)
+    _check(lib().ftor_moe_ffn(_ptr(x), _ptr(logits), t, k, n_ff, e, u, _ptr(gate_exps),
+                              _ptr(up_exps), _ptr(down_exps), dtype, _ptr(out), threads),
+           "ftor_moe_ffn")
+    return out
+
+
+# -------------------------------------------------------------- reference
+
+def ref_dequant_rows(w, dtype, k):
+    w = _c(w, np.uint8)
+    out = np.empty((w.shape[0], k), dtype=np.float32)
+    for r in range(w.shape[0]):
+        _check(ref().ftref_dequant_row(_ptr(out[r]), _ptr(w[r]), dtype, k), "ftref_dequant_row")
+    return out
+
+
+def ref_dot_row(x, wrow, dtype, k):
+    x = _c(x, np.float32)
+    wrow = _c(wrow, np.uint8)
+    out = np.zeros(1, dtype=np.float32)
+    _check(ref().ftref_dot_row_f32(_ptr(x), _ptr(wrow), dtype, k, _ptr(out)), "ftref_dot_row_f32")
+    return float(out[0])
+
+
+def ref_matmul(x, w, dtype, k, threads=1):
+    """The reference's CpuBackend::matmul, unmodified (sums rows for M>1)."""
+    x = _c(x, np.float32).reshape(-1, k)
+    w = _c(w, np.uint8)
+    y = np.zeros(w.shape[0] * x.shape[0], dtype=np.float32)
+    _check(ref().ftref_matmul(_ptr(x), x.shape[0], k, _ptr(w), dtype, w.shape[0], _ptr(y),
+                              threads), "ftref_matmul")
+    return y
+
+
+def ref_expert_chunk(x, out, gate, up, down, dtype, k, ic, threads=1):
+    x = _c(x, np.float32)
+    gate, up, down = (_c(a, np.uint8) for a in (gate, up, down))
+    _check(ref().ftref_run_expert_chunk(_ptr(x), _ptr(out), _ptr(gate), _ptr(up), _ptr(down),
+                                        dtype, x.shape[0], k, ic, gate.shape[1], down.shape[1],
+                                        threads), "ftref_run_expert_chunk")
+    return out
