@@ -1,0 +1,498 @@
+"""Benchmark of the B200 GGUF dequant-matmul path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the seven linear weights of a Llama-3-8B layer
+in Q4_K -- q (4096x4096), k, v (1024x4096), o (4096x4096), gate, up
+(14336x4096), down (4096x14336) -- as batch-1 decode GEMVs with fp32
+activations.  One step = one pass over 8 distinct layer copies (56 GEMVs,
+982 MB of blocks, about 7.8x the 126 MB L2, so every step streams from HBM).
+Inputs are seeded synthetic tensors with the config's distributions.
+
+* value     -- GB/s of weight blocks (algorithmic bytes: blocks + x + y)
+               with everything resident in HBM; CUDA graph of the step,
+               CUDA events on the launching stream.
+* e2e       -- the same pass through the reference-facing C ABI
+               (ftc_backend_matmul, the ft::IBackend::matmul equivalent):
+               host x in, host y out, per call; weights resident (uploaded
+               once, as at Engine::load).
+* roofline  -- the dominant kernel (gate/up shape 14336x4096) timed alone.
+* cpu_baseline -- the CPU port of the reference's CpuBackend::matmul on a
+               bounded sample (N=1, rank 0).
+For N>1 every rank runs the same workload on its own GPU (replicas; the
+decode GEMV does not shard): value = sum over ranks, time = max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from xwfes_b200 import formats as F, synth as S  # noqa: E402
+
+METRIC = "Q4_K dequant-GEMV HBM GB/s (% of peak) & prefill dequant-GEMM TFLOPS"
+LAYER = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+         ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
+N_LAYERS = 8
+# activation vector each GEMV reads (q/k/v share one, gate/up share one)
+X_OF = {"q": "attn_in", "k": "attn_in", "v": "attn_in", "o": "attn_out", "gate": "ffn_in",
+        "up": "ffn_in", "down": "ffn_mid"}
+X_LEN = {"attn_in": 4096, "attn_out": 4096, "ffn_in": 4096, "ffn_mid": 14336}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def layer_bytes():
+    w = sum(F.row_bytes(F.Q4_K, k) * n for _, n, k in LAYER)
+    xy = sum(4 * (n + k) for _, n, k in LAYER)
+    return w, xy
+
+
+def make_weights(seed=0):
+    return [{name: S.weight(F.Q4_K, n, k, seed=seed, name=f"L{li}.{name}")
+             for name, n, k in LAYER} for li in range(N_LAYERS)]
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples (every 100 ms) of one GPU's clocks and throttle
+    reasons while the timed region runs; the GPU is picked by PCI bus id."""
+    Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus = (bus_id or "").lower()
+        self.lines = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=5)
+
+    def summary(self):
+        sm, mx, pw, reasons = [], None, [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = [[v.strip() for v in ln.split(",")] for ln in self.lines]
+        rows = [f for f in rows if len(f) >= 9]
+        mine = [f for f in rows if self.bus and f[0].lower().endswith(self.bus)]
+        if not mine and rows:  # bus id unknown: the first GPU listed
+            first = rows[0][0]
+            mine = [f for f in rows if f[0] == first]
+        for f in mine:
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+                pw.append(float(f[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "power_w_median": statistics.median(pw) if pw else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- our path
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from xwfes_b200 import ftc
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    be = ftc.CudaBackend(local_rank)
+
+    t0 = time.time()
+    layers = make_weights(seed=0)
+    hosts = {}
+    for li, L in enumerate(layers):
+        for name, n, k in LAYER:
+            T = ftc.HostTensor(L[name], F.Q4_K, (k, n), name=f"L{li}.{name}")
+            be.upload(T)
+            hosts[(li, name)] = T
+    xs_host = {nm: S.activations_f32(1, ln, seed=0, name=nm) for nm, ln in X_LEN.items()}
+    xs = {nm: torch.from_numpy(a).to(dev) for nm, a in xs_host.items()}
+    ys = {name: torch.empty((1, n), dtype=torch.float32, device=dev) for name, n, _ in LAYER}
+    setup_s = time.time() - t0
+
+    # device views of the cached blocks (the same HBM copies the C ABI uses)
+    dptr = {key: be.device_ptr(T) for key, T in hosts.items()}
+
+    stream = torch.cuda.Stream(device=dev)
+    L = ftc.lib()
+
+    def launch(li, name, n, k, s):
+        rc = L.ftc_mul_mat_vec(F.Q4_K, dptr[(li, name)], n, k, F.row_bytes(F.Q4_K, k),
+                               xs[X_OF[name]].data_ptr(), 1, ys[name].data_ptr(), s)
+        if rc:
+            raise ftc.FtcError("ftc_mul_mat_vec", rc, ftc.last_error())
+
+    def step(s):
+        for li in range(N_LAYERS):
+            for name, n, k in LAYER:
+                launch(li, name, n, k, s)
+
+    sp = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        step(sp)  # eager warm-up outside capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(sp)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+
+    wbytes, xybytes = layer_bytes()
+    step_bytes = N_LAYERS * (wbytes + xybytes)
+    launches_per_step = N_LAYERS * len(LAYER)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    props = torch.cuda.get_device_properties(dev)
+    bus = getattr(props, "pci_bus_id", None)
+    smi_id = f"{bus:02x}:{getattr(props, 'pci_device_id', 0):02x}.0" if bus is not None else ""
+    with ClockSampler(smi_id) as clk, torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()  # replays on the current stream == `stream`
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+
+    # dominant kernel alone: gate shape over the 8 layer copies, graph-replayed
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=stream):
+        for li in range(N_LAYERS):
+            launch(li, "gate", 14336, 4096, sp)
+    reps = 200
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g2.replay()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(reps):
+            g2.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    k_ms = ev0.elapsed_time(ev1) / (reps * N_LAYERS)
+    k_bytes = F.row_bytes(F.Q4_K, 4096) * 14336 + 4 * (4096 + 14336)
+
+    # e2e through the C ABI: host x in, host y out, per ftc_backend_matmul call
+    ext = torch.cuda.ExternalStream(be.stream(), device=dev)
+    yh = {name: np.empty((1, n), dtype=np.float32) for name, n, _ in LAYER}
+
+    def e2e_step():
+        for li in range(N_LAYERS):
+            for name, n, k in LAYER:
+                be.matmul(xs_host[X_OF[name]], 1, k, hosts[(li, name)], yh[name])
+
+    for _ in range(3):
+        e2e_step()
+    e2e_steps = max(3, args.steps // 50)
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record(ext)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(ext)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+    h2d = N_LAYERS * sum(4 * k for _, _, k in LAYER)
+    d2h = N_LAYERS * sum(4 * n for _, n, _ in LAYER)
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms, k_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, k_ms = t.tolist()
+
+    del graph, g2
+    be.close()
+    if rank != 0:
+        return None
+    hbm, _, peak_kind = peaks()
+    gbs = step_bytes * world / (ms * 1e-3) / 1e9
+    k_gbs = k_bytes / (k_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(gbs, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded Q4_K blocks and N(0,1) fp32 activations, config 2 distributions)",
+        "config": {
+            "workload": "config 2: Q4_K decode GEMV, Llama-3-8B layer shapes "
+                        "(q,k,v,o 4096/1024x4096; gate,up 14336x4096; down 4096x14336), batch 1",
+            "layers_per_step": N_LAYERS,
+            "bytes_per_step": step_bytes,
+            "l2": "inputs larger than L2: 8 distinct layer copies (982 MB) per step",
+            "parallelism": f"replicas x{world}",
+            "graph": "CUDA graph of the 56-GEMV step",
+        },
+        "pct_of_peak": round(100 * gbs / world / hbm, 1),
+        "tokens_per_s": round(world * 1e3 / (ms / N_LAYERS * 32), 1),
+        "tokens_per_s_note": "per-GPU decode rate of a 32-layer Llama-3-8B linear stack "
+                             "at this layer time x world (attention and head excluded)",
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "gemv_q4k (14336x4096, batch 1)",
+            "achieved": round(k_gbs, 1),
+            "peak": hbm,
+            "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs burst)",
+            "unit": "GB/s",
+            "frac": round(k_gbs / hbm, 3),
+            "traffic": traffic_from_profiles(),
+            "bytes_per_launch": k_bytes,
+            "us_per_launch": round(k_ms * 1e3, 3),
+        },
+        "e2e": {
+            "value": round(step_bytes / (e2e_ms * 1e-3) / 1e9 * world, 2),
+            "unit": "GB/s",
+            "ms_per_step": round(e2e_ms, 4),
+            "steps": e2e_steps,
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "api": "ftc_backend_matmul (ft::IBackend::matmul), pinned staging, sync per call",
+        },
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+        "setup_s": round(setup_s, 1),
+    }
+    return line
+
+
+def traffic_from_profiles():
+    """dram bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/gemv_q4k_decode.md, line 'traffic_bytes_per_launch: N')."""
+    p = os.path.join(ROOT, "profiles", "gemv_q4k_decode.md")
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(ln.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def run_ncu_probe():
+    """Five launches of the gate-shaped GEMV (14336x4096 Q4_K, 33 MB, larger
+    than nothing else on the device): the small case for ncu captures."""
+    import torch
+    from xwfes_b200 import ftc
+    dev = torch.device("cuda", 0)
+    w = torch.from_numpy(S.weight(F.Q4_K, 14336, 4096, seed=0, name="L0.gate")).to(dev)
+    x = torch.from_numpy(S.activations_f32(1, 4096, seed=0, name="ffn_in")).to(dev)
+    for _ in range(5):
+        y = ftc.mul_mat_vec(w, F.Q4_K, 14336, 4096, x)
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": "gemv_q4k 14336x4096 x5", "y0": float(y[0, 0])}))
+    return 0
+
+
+# ----------------------------------------------------------- CPU baselines
+
+def cpu_sample(threads, budget_s=10.0):
+    """The CPU port of CpuBackend::matmul (oracle) over one config-2 layer,
+    repeated within about budget_s seconds."""
+    from oracle import oracle as O
+    L = make_weights(seed=0)[0]
+    xs = {nm: S.activations_f32(1, ln, seed=0, name=nm) for nm, ln in X_LEN.items()}
+    wbytes, xybytes = layer_bytes()
+
+    def one():
+        for name, n, k in LAYER:
+            O.matmul(xs[X_OF[name]], L[name], F.Q4_K, k, threads=threads)
+
+    t = time.perf_counter()
+    one()
+    t1 = time.perf_counter() - t
+    reps = max(1, min(50, int(budget_s / max(t1, 1e-3))))
+    t = time.perf_counter()
+    for _ in range(reps):
+        one()
+    dt = (time.perf_counter() - t) / reps
+    return (wbytes + xybytes) / dt / 1e9, reps, dt
+
+
+def reference_q8_0_config1(threads):
+    """The reference's own CpuBackend::matmul (oracle/_ref) on config 1."""
+    from oracle import oracle as O
+    if not O.have_ref():
+        return None
+    w = S.weight(F.Q8_0, 4096, 4096, seed=0, name="c1")
+    x = S.activations_f32(1, 4096, seed=0, name="c1")
+    O.ref_matmul(x, w, F.Q8_0, 4096, threads=threads)
+    reps = 20
+    t = time.perf_counter()
+    for _ in range(reps):
+        O.ref_matmul(x, w, F.Q8_0, 4096, threads=threads)
+    dt = (time.perf_counter() - t) / reps
+    return {"value": round(w.nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "reference", "sample": "config 1: Q8_0 4096x4096 GEMV, 20 calls"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path on this host's cores.  The
+    reference cannot run Q4_K (no decoder), so the timed arm is the port of
+    its CpuBackend::matmul (same row split, dot_row_f32 arithmetic) over the
+    same Q4_K layer; its own Q8_0 number is reported beside it."""
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    L = make_weights(seed=0)[0]
+    xs = {nm: S.activations_f32(1, ln, seed=0, name=nm) for nm, ln in X_LEN.items()}
+    wbytes, xybytes = layer_bytes()
+
+    def one():
+        for name, n, k in LAYER:
+            O.matmul(xs[X_OF[name]], L[name], F.Q4_K, k, threads=threads)
+
+    for _ in range(min(args.warmup, 2)):
+        one()
+    t = time.perf_counter()
+    one()
+    t1 = time.perf_counter() - t
+    steps = max(3, min(args.steps, int(90.0 / max(t1, 1e-3))))
+    t = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = (time.perf_counter() - t) / steps
+    gbs = (wbytes + xybytes) / dt / 1e9
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": steps,
+        "warmup": min(args.warmup, 2),
+        "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded Q4_K blocks and N(0,1) fp32 activations, config 2 distributions)",
+        "config": {"workload": "config 2: Q4_K decode GEMV, Llama-3-8B layer shapes, batch 1",
+                   "layers_per_step": 1, "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"one Llama-3-8B Q4_K layer (7 GEMVs, {wbytes} B) per step; "
+                                   "the reference has no Q4_K decoder, so this is the oracle "
+                                   "port of its CpuBackend::matmul"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "reference_q8_0_config1": reference_q8_0_config1(threads),
+    }
+
+
+# ------------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling mode: a few launches of the dominant kernel "
+                         "(gate-shaped Q4_K GEMV) on one layer copy, no timing")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.ncu:
+        return run_ncu_probe()
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args)), flush=True)
+        return 0
+
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    line = run_ours(args, rank, world, local_rank)
+    if rank == 0 and line is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            gbs, reps, dt = cpu_sample(threads)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"one Q4_K layer (7 GEMVs) x {reps} reps, {dt * 1e3:.1f} ms each; the "
+                          "reference has no Q4_K decoder, so this is the oracle port of its "
+                          "CpuBackend::matmul"}
+            ref = reference_q8_0_config1(threads)
+            if ref:
+                line["reference_q8_0_config1"] = ref
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

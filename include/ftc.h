@@ -1,0 +1,158 @@
+/*
+ * ftc.h -- C ABI of libftcuda.so, the B200 (sm_100a) GGUF dequant-matmul
+ * backend.  Plain pointers and sizes only; every function returns an int
+ * status (FTC_OK = 0) and ftc_last_error() describes the last failure on the
+ * calling thread.
+ *
+ * Two layers:
+ *   1. ftc_backend_*  -- one backend instance = one device + one stream +
+ *      a weight cache.  These take HOST buffers, copy inputs in and results
+ *      out, and return with the results complete on the host: the contract
+ *      of the reference's operator interface ft::IBackend
+ *      (ft/include/ft/backend.h:21-40).  A C++ ft::IBackend adapter over
+ *      these lives in xwfes_b200/host/cuda_backend.{h,cpp}.
+ *   2. ftc_* kernel entry points -- DEVICE pointers, launched on the given
+ *      cudaStream_t (passed as void*), asynchronous, no allocation.
+ *
+ * Weight layout everywhere: GGUF blocks exactly as the loader produces them
+ * (ft::HostTensor, ft/include/ft/types.h:119-140): W[n][k] is n rows of
+ * row_stride bytes, each row ceil(k / block) whole blocks along k.
+ */
+#ifndef FTC_H
+#define FTC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status */
+#define FTC_OK 0
+#define FTC_E_INVALID (-1)     /* bad argument: null pointer, shape, stride, alignment */
+#define FTC_E_UNSUPPORTED (-2) /* dtype / shape combination not implemented */
+#define FTC_E_CUDA (-3)        /* CUDA runtime error (message has the CUDA text) */
+#define FTC_E_NOMEM (-4)       /* device or pinned host allocation failed */
+#define FTC_E_INJECTED (-5)    /* host-side fault injection (FTC_INJECT_FAIL) fired */
+#define FTC_E_DEVICE (-6)      /* a kernel reported a bounded wait that ran out */
+
+/* ------------------------------------------------------------ dtypes */
+/* The reference's ft::DType values (ft/include/ft/types.h:20-27) plus the
+ * GGUF type ids of Q4_K and Q6_K, which its loader rejects
+ * (ft/src/gguf.cpp:129-137). */
+enum ftc_dtype {
+    FTC_F32 = 0,
+    FTC_F16 = 1,
+    FTC_Q4_0 = 2,
+    FTC_Q4_1 = 3,
+    FTC_Q8_0 = 8,
+    FTC_Q4_K = 12,
+    FTC_Q6_K = 14,
+    FTC_BF16 = 30
+};
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* ftc_last_error(void);
+/* ABI version, bumped on incompatible changes. */
+int ftc_abi_version(void);
+/* Bytes of one row of k weights of `dtype` (whole blocks), or -1. */
+int64_t ftc_row_bytes(int dtype, int64_t k);
+
+/* ============================================================ backend */
+
+typedef struct ftc_backend ftc_backend;
+
+/* Replaces constructing a backend (ft::CpuBackend / ft::VulkanBackend,
+ * ft/src/cpu_backend.cpp:77-86, ft/src/vulkan_backend.cpp:128-277): binds
+ * `device`, creates its stream and pinned staging.  On failure *out is NULL
+ * and the engine keeps its CPU backend (ft/src/engine.cpp:291-300). */
+int ftc_backend_create(int device, ftc_backend** out);
+void ftc_backend_destroy(ftc_backend* be);
+
+/* ft::IBackend::name() / info() (ft/include/ft/types.h:142-147 DeviceInfo):
+ * device name into `name` (NUL-terminated, truncated to cap) and its total
+ * memory.  integrated/uma are always false for a B200. */
+int ftc_backend_info(ftc_backend* be, char* name, size_t cap, uint64_t* mem_bytes);
+
+/* Upload a GGUF tensor's raw blocks to HBM once (Engine::load time,
+ * ft/src/engine.cpp:318-382).  The cache is keyed by the host address range
+ * [host, host + nbytes); later calls whose weight pointer falls inside that
+ * range use the device copy.  Re-uploading the same range is a no-op. */
+int ftc_backend_upload(ftc_backend* be, const void* host, size_t nbytes);
+/* Drop the cached copy of the range that starts at `host`. */
+int ftc_backend_evict(ftc_backend* be, const void* host);
+/* Bytes currently cached on the device. */
+int ftc_backend_cached_bytes(ftc_backend* be, uint64_t* bytes);
+
+/* ft::IBackend::matmul (ft/include/ft/backend.h:28-29):
+ *   y[m][n] = sum_k x[m][k] * W[n][k]   for m < M, n < N
+ * x: host fp32 [M][K]; w_host: the tensor's host data pointer (HostTensor::
+ * data), dtype and N rows of ceil(K/block) blocks; y: host fp32 [M][N].
+ * Uploads W on first use if no cached range covers it.  Returns with y
+ * written.  Unlike the reference's CpuBackend::matmul
+ * (ft/src/cpu_backend.cpp:90-104), which folds all M rows into y[n], every
+ * row m gets its own output row. */
+int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K,
+                       const void* w_host, int dtype, int64_t N, float* y);
+
+/* ft::ExpertChunkJob (ft/include/ft/backend.h:7-19), same fields. */
+typedef struct ftc_expert_chunk_job {
+    const float* x;      /* host fp32 [M][K] */
+    float* out;          /* host fp32 [M][K], accumulated into (+=) */
+    const void* gate;    /* host block pointers (inside a cached range or not) */
+    const void* up;
+    const void* down;
+    int dtype;
+    int64_t M;
+    int64_t K;
+    int64_t IC;          /* neurons in this window */
+    size_t gate_up_row_stride;
+    size_t down_row_stride;
+} ftc_expert_chunk_job;
+
+/* ft::IBackend::run_expert_chunk (ft/include/ft/backend.h:31), the maths of
+ * ft/src/cpu_backend.cpp:106-149:
+ *   h[m][i]   = silu(x_m . gate_i) * (x_m . up_i)          i < IC
+ *   out[m][k] += sum_i h[m][i] * down_i[k]                  (down_i = row i)
+ * Windows not inside a cached range are copied to the device per call. */
+int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* job);
+
+/* ft::IBackend::sync (ft/include/ft/backend.h:39). */
+int ftc_backend_sync(ftc_backend* be);
+
+/* The backend's cudaStream_t (as void*), for callers mixing in kernel calls. */
+void* ftc_backend_stream(ftc_backend* be);
+/* Device pointer of the cached copy of `host` (NULL if not cached). */
+const void* ftc_backend_device_ptr(ftc_backend* be, const void* host);
+
+/* Kernels never trap or spin forever: a pipeline wait that exceeds its
+ * bound (far above any legitimate wait) makes the kernel record a status and
+ * return.  This synchronizes `stream`, returns the OR of the recorded
+ * statuses in *status (0 = none; 1 = a bounded wait ran out) and clears
+ * them. */
+int ftc_device_status(void* stream, int* status);
+
+/* ====================================================== kernel entry points
+ * Device pointers; asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ * default stream).  They allocate nothing. */
+
+/* Dequantize n_rows rows of k weights to fp32: out[r][j] (row pitch k).
+ * Bit-exact with the reference's ft::dequant_row (ft/include/ft/quant.h:10-84)
+ * for F32/F16/BF16/Q8_0/Q4_0/Q4_1, and with the GGUF K-quant formulas for
+ * Q4_K/Q6_K.  k must be a whole number of blocks. */
+int ftc_dequant(int dtype, const void* w, int64_t n_rows, int64_t k, int64_t row_stride,
+                float* out, void* stream);
+
+/* Decode GEMV/GEMM on CUDA cores, fp32 activations and accumulation:
+ *   y[m][n] = sum_k x[m][k] * W[n][k]     m < M (1..8), n < N
+ * x fp32 with row pitch k, y fp32 with row pitch N.  The per-row arithmetic
+ * of ft::dot_row_f32 (ft/include/ft/quant.h:86-103) in a different
+ * summation order. */
+int ftc_mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
+                    const float* x, int64_t M, float* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FTC_H */

@@ -1,0 +1,92 @@
+"""The C ABI library without a GPU: it loads, exports every entry point
+include/ftc.h declares, and rejects bad arguments before touching CUDA."""
+import ctypes as C
+import os
+import re
+import subprocess
+import sys
+
+import pytest
+
+from xwfes_b200 import formats as F, ftc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    txt = open(os.path.join(ROOT, "include", "ftc.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(ftc_[a-z0-9_]+)\s*\(", txt)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(ftc.LIB_PATH):
+        from xwfes_b200 import build
+        build.build()
+    return ftc.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    syms = declared_symbols()
+    assert len(syms) >= 10
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in include/ftc.h but not exported"
+    assert set(syms) == set(ftc.SIGNATURES), "ctypes signatures out of sync with include/ftc.h"
+
+
+def test_row_bytes_matches_formats(lib):
+    for t in (F.F32, F.F16, F.BF16, F.Q4_0, F.Q4_1, F.Q8_0, F.Q4_K, F.Q6_K):
+        for k in (256, 4096, 14336):
+            assert lib.ftc_row_bytes(t, k) == F.row_bytes(t, k)
+    assert lib.ftc_row_bytes(99, 256) == -1
+    assert lib.ftc_abi_version() == 1
+
+
+def test_kernel_entry_points_validate_before_launch(lib):
+    # null pointers / bad shapes are refused before any CUDA call
+    rc = lib.ftc_mul_mat_vec(F.Q4_K, None, 16, 256, 144, None, 1, None, None)
+    assert rc == -1 and "null" in ftc.last_error()
+    rc = lib.ftc_mul_mat_vec(F.Q4_K, 16, 16, 255, 144, 16, 1, 16, None)
+    assert rc == -1 and "whole number of blocks" in ftc.last_error()
+    rc = lib.ftc_mul_mat_vec(F.Q4_K, 16, 16, 256, 144, 16, 9, 16, None)
+    assert rc == -1 and "M must be" in ftc.last_error()
+    rc = lib.ftc_mul_mat_vec(F.Q4_K, 16, 16, 256, 100, 16, 1, 16, None)
+    assert rc == -1 and "row_stride" in ftc.last_error()
+    rc = lib.ftc_mul_mat_vec(7, 16, 16, 256, 144, 16, 1, 16, None)
+    assert rc == -2
+    rc = lib.ftc_dequant(F.Q6_K, 16, 4, 100, 210, 16, None)
+    assert rc == -1
+
+
+def _run_child(code, env_extra):
+    env = dict(os.environ, **env_extra)
+    return subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env,
+                          capture_output=True, text=True, timeout=120)
+
+
+def test_fault_injection_fires_before_cuda():
+    code = ("import ctypes as C; from xwfes_b200 import ftc; L = ftc.lib(); h = C.c_void_p();"
+            "rc = L.ftc_backend_create(0, C.byref(h)); print(rc, h.value, ftc.last_error())")
+    r = _run_child(code, {"FTC_INJECT_FAIL": "ftc_backend_create"})
+    assert r.returncode == 0, r.stderr
+    rc, hv, *msg = r.stdout.split()
+    assert int(rc) == -5 and hv == "None" and "injected" in " ".join(msg)
+
+
+def test_backend_create_without_device_fails_cleanly():
+    """No GPU here: creating a backend returns an error status, never a
+    half-built handle (the engine then keeps its CPU backend)."""
+    code = ("import ctypes as C; from xwfes_b200 import ftc; L = ftc.lib(); h = C.c_void_p();"
+            "rc = L.ftc_backend_create(0, C.byref(h)); print(rc, h.value)")
+    r = _run_child(code, {"CUDA_VISIBLE_DEVICES": ""})
+    assert r.returncode == 0, r.stderr
+    rc, hv = r.stdout.split()
+    assert int(rc) in (-1, -3) and hv == "None"
+
+
+def test_library_refuses_to_fall_back(monkeypatch, tmp_path):
+    monkeypatch.setattr(ftc, "LIB_PATH", str(tmp_path / "missing.so"))
+    monkeypatch.setattr(ftc, "_lib", None)
+    with pytest.raises(FileNotFoundError):
+        ftc.lib()

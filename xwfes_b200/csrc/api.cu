@@ -1,0 +1,397 @@
+// api.cu -- the C ABI of libftcuda.so (include/ftc.h): status plumbing, the
+// backend instance (device, stream, HBM weight cache, pinned staging) and
+// the extern "C" entry points.
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace ftc {
+
+// ------------------------------------------------------------ status
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int set_error(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+    return set_error(FTC_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int ok() {
+    g_last_error.clear();
+    return FTC_OK;
+}
+
+bool inject_fail(const char* entry) {
+    const char* v = std::getenv("FTC_INJECT_FAIL");
+    if (!v || !*v) return false;
+    if (std::strcmp(v, "all") == 0) return true;
+    // comma-separated list of entry-point names
+    const size_t n = std::strlen(entry);
+    for (const char* p = v; *p;) {
+        const char* e = std::strchr(p, ',');
+        const size_t len = e ? (size_t)(e - p) : std::strlen(p);
+        if (len == n && std::strncmp(p, entry, n) == 0) return true;
+        if (!e) break;
+        p = e + 1;
+    }
+    return false;
+}
+
+// kernels (gemv.cu, dequant.cu, expert.cu)
+int mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
+                const float* x, int64_t M, float* y, cudaStream_t st);
+int dequant(int dtype, const void* w, int64_t n_rows, int64_t k, int64_t row_stride, float* out,
+            cudaStream_t st);
+int expert_chunk_dev(int dtype, const float* x, float* out, const void* gate, const void* up,
+                     const void* down, int64_t M, int64_t K, int64_t IC, int64_t gu_stride,
+                     int64_t dn_stride, float* gbuf, float* ubuf, float* hbuf, cudaStream_t st);
+
+// status readers of the translation units whose kernels use bounded waits
+int devstat_gemv_q4k(int clear);
+
+}  // namespace ftc
+
+using namespace ftc;
+
+// ------------------------------------------------------------ backend
+
+namespace {
+
+// Growable device / pinned-host buffer owned by a backend.
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    bool pinned = false;
+    int ensure(size_t bytes) {
+        if (bytes <= cap) return FTC_OK;
+        release();
+        size_t want = bytes < 4096 ? 4096 : bytes;
+        cudaError_t e = pinned ? cudaMallocHost(&p, want) : cudaMalloc(&p, want);
+        if (e != cudaSuccess) {
+            p = nullptr;
+            cap = 0;
+            return set_error(FTC_E_NOMEM, std::string("staging allocation: ") + cudaGetErrorString(e));
+        }
+        cap = want;
+        return FTC_OK;
+    }
+    void release() {
+        if (p) pinned ? cudaFreeHost(p) : cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+};
+
+struct CacheEntry {
+    const uint8_t* host;
+    size_t nbytes;
+    void* dev;
+};
+
+}  // namespace
+
+struct ftc_backend {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string name;
+    uint64_t mem = 0;
+    std::map<uintptr_t, CacheEntry> cache;  // keyed by host start address
+    uint64_t cached = 0;
+    DevBuf pin_in{nullptr, 0, true}, pin_out{nullptr, 0, true};
+    DevBuf dx, dy, dwin, dtmp;
+    std::mutex mu;
+
+    // Cached entry that fully covers [p, p + n), or nullptr.
+    const CacheEntry* find(const void* p, size_t n) const {
+        const uintptr_t a = (uintptr_t)p;
+        auto it = cache.upper_bound(a);
+        if (it == cache.begin()) return nullptr;
+        --it;
+        const CacheEntry& e = it->second;
+        if (a >= (uintptr_t)e.host && a + n <= (uintptr_t)e.host + e.nbytes) return &e;
+        return nullptr;
+    }
+
+    int upload(const void* host, size_t nbytes) {
+        if (find(host, nbytes)) return FTC_OK;
+        void* d = nullptr;
+        cudaError_t e = cudaMalloc(&d, nbytes);
+        if (e != cudaSuccess)
+            return set_error(FTC_E_NOMEM, std::string("weight upload: ") + cudaGetErrorString(e));
+        e = cudaMemcpyAsync(d, host, nbytes, cudaMemcpyHostToDevice, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) {
+            cudaFree(d);
+            return cuda_error(e, "weight upload copy");
+        }
+        cache[(uintptr_t)host] = CacheEntry{static_cast<const uint8_t*>(host), nbytes, d};
+        cached += nbytes;
+        return FTC_OK;
+    }
+
+    // Device address of host range [p, p + n): cached copy, else uploaded.
+    int resolve(const void* p, size_t n, const void** dev) {
+        const CacheEntry* e = find(p, n);
+        if (!e) {
+            int rc = upload(p, n);
+            if (rc) return rc;
+            e = find(p, n);
+        }
+        *dev = static_cast<const uint8_t*>(e->dev) + ((const uint8_t*)p - e->host);
+        return FTC_OK;
+    }
+};
+
+namespace {
+
+int bind(ftc_backend* be) {
+    FTC_REQUIRE(be, FTC_E_INVALID, "null backend");
+    FTC_CUDA(cudaSetDevice(be->device));
+    return FTC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ftc_last_error(void) { return g_last_error.c_str(); }
+
+int ftc_abi_version(void) { return 1; }
+
+int64_t ftc_row_bytes(int dtype, int64_t k) { return row_bytes(dtype, k); }
+
+int ftc_backend_create(int device, ftc_backend** out) {
+    FTC_REQUIRE(out, FTC_E_INVALID, "ftc_backend_create: null out");
+    *out = nullptr;
+    if (inject_fail("ftc_backend_create"))
+        return set_error(FTC_E_INJECTED, "ftc_backend_create: injected failure");
+    int n = 0;
+    FTC_CUDA(cudaGetDeviceCount(&n));
+    FTC_REQUIRE(device >= 0 && device < n, FTC_E_INVALID, "ftc_backend_create: no such device");
+    FTC_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    FTC_CUDA(cudaGetDeviceProperties(&prop, device));
+    FTC_REQUIRE(prop.major == 10, FTC_E_UNSUPPORTED,
+                "ftc_backend_create: libftcuda is built for sm_100a (B200) only");
+    ftc_backend* be = new ftc_backend();
+    be->device = device;
+    be->name = std::string("CUDA:") + prop.name;
+    be->mem = prop.totalGlobalMem;
+    cudaError_t e = cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete be;
+        return cuda_error(e, "cudaStreamCreate");
+    }
+    *out = be;
+    return ok();
+}
+
+void ftc_backend_destroy(ftc_backend* be) {
+    if (!be) return;
+    cudaSetDevice(be->device);
+    if (be->stream) cudaStreamSynchronize(be->stream);
+    for (auto& kv : be->cache) cudaFree(kv.second.dev);
+    be->pin_in.release();
+    be->pin_out.release();
+    be->dx.release();
+    be->dy.release();
+    be->dwin.release();
+    be->dtmp.release();
+    if (be->stream) cudaStreamDestroy(be->stream);
+    delete be;
+}
+
+int ftc_backend_info(ftc_backend* be, char* name, size_t cap, uint64_t* mem_bytes) {
+    FTC_REQUIRE(be, FTC_E_INVALID, "ftc_backend_info: null backend");
+    if (name && cap) {
+        std::strncpy(name, be->name.c_str(), cap - 1);
+        name[cap - 1] = 0;
+    }
+    if (mem_bytes) *mem_bytes = be->mem;
+    return ok();
+}
+
+int ftc_backend_upload(ftc_backend* be, const void* host, size_t nbytes) {
+    int rc = bind(be);
+    if (rc) return rc;
+    FTC_REQUIRE(host && nbytes, FTC_E_INVALID, "ftc_backend_upload: empty range");
+    if (inject_fail("ftc_backend_upload"))
+        return set_error(FTC_E_INJECTED, "ftc_backend_upload: injected failure");
+    std::lock_guard<std::mutex> lk(be->mu);
+    rc = be->upload(host, nbytes);
+    return rc ? rc : ok();
+}
+
+int ftc_backend_evict(ftc_backend* be, const void* host) {
+    int rc = bind(be);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(be->mu);
+    auto it = be->cache.find((uintptr_t)host);
+    FTC_REQUIRE(it != be->cache.end(), FTC_E_INVALID, "ftc_backend_evict: range not cached");
+    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    cudaFree(it->second.dev);
+    be->cached -= it->second.nbytes;
+    be->cache.erase(it);
+    return ok();
+}
+
+int ftc_backend_cached_bytes(ftc_backend* be, uint64_t* bytes) {
+    FTC_REQUIRE(be && bytes, FTC_E_INVALID, "ftc_backend_cached_bytes: null argument");
+    *bytes = be->cached;
+    return ok();
+}
+
+void* ftc_backend_stream(ftc_backend* be) { return be ? (void*)be->stream : nullptr; }
+
+const void* ftc_backend_device_ptr(ftc_backend* be, const void* host) {
+    if (!be) return nullptr;
+    std::lock_guard<std::mutex> lk(be->mu);
+    const CacheEntry* e = be->find(host, 1);
+    return e ? static_cast<const uint8_t*>(e->dev) + ((const uint8_t*)host - e->host) : nullptr;
+}
+
+int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K, const void* w_host,
+                       int dtype, int64_t N, float* y) {
+    int rc = bind(be);
+    if (rc) return rc;
+    const Fmt f = fmt_of(dtype);
+    FTC_REQUIRE(f.block_elems > 0, FTC_E_UNSUPPORTED, "ftc_backend_matmul: unknown dtype");
+    FTC_REQUIRE(x && w_host && y, FTC_E_INVALID, "ftc_backend_matmul: null pointer");
+    FTC_REQUIRE(M > 0 && K > 0 && N > 0, FTC_E_INVALID, "ftc_backend_matmul: empty shape");
+    FTC_REQUIRE(K % f.block_elems == 0, FTC_E_INVALID,
+                "ftc_backend_matmul: K must be a whole number of blocks");
+    if (inject_fail("ftc_backend_matmul"))
+        return set_error(FTC_E_INJECTED, "ftc_backend_matmul: injected failure");
+    std::lock_guard<std::mutex> lk(be->mu);
+    const int64_t stride = row_bytes(dtype, K);
+    const void* dW = nullptr;
+    if ((rc = be->resolve(w_host, (size_t)(stride * N), &dW))) return rc;
+    const size_t xb = (size_t)(M * K) * 4, yb = (size_t)(M * N) * 4;
+    if ((rc = be->pin_in.ensure(xb)) || (rc = be->pin_out.ensure(yb)) || (rc = be->dx.ensure(xb)) ||
+        (rc = be->dy.ensure(yb)))
+        return rc;
+    std::memcpy(be->pin_in.p, x, xb);
+    FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, xb, cudaMemcpyHostToDevice, be->stream));
+    const float* dx = static_cast<const float*>(be->dx.p);
+    float* dy = static_cast<float*>(be->dy.p);
+    for (int64_t m0 = 0; m0 < M; m0 += 8) {
+        const int64_t mc = M - m0 < 8 ? M - m0 : 8;
+        if ((rc = mul_mat_vec(dtype, dW, N, K, stride, dx + m0 * K, mc, dy + m0 * N, be->stream)))
+            return rc;
+    }
+    FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, be->stream));
+    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    std::memcpy(y, be->pin_out.p, yb);
+    return ok();
+}
+
+int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* job) {
+    int rc = bind(be);
+    if (rc) return rc;
+    FTC_REQUIRE(job, FTC_E_INVALID, "ftc_backend_run_expert_chunk: null job");
+    const int64_t M = job->M, K = job->K, IC = job->IC;
+    if (IC <= 0 || M <= 0 || K <= 0) return ok();  // as ft/src/cpu_backend.cpp:110
+    const Fmt f = fmt_of(job->dtype);
+    FTC_REQUIRE(f.block_elems > 0, FTC_E_UNSUPPORTED, "ftc_backend_run_expert_chunk: unknown dtype");
+    FTC_REQUIRE(job->x && job->out && job->gate && job->up && job->down, FTC_E_INVALID,
+                "ftc_backend_run_expert_chunk: null pointer");
+    FTC_REQUIRE(K % f.block_elems == 0, FTC_E_INVALID,
+                "ftc_backend_run_expert_chunk: K must be a whole number of blocks");
+    const int64_t rb = row_bytes(job->dtype, K);
+    FTC_REQUIRE((int64_t)job->gate_up_row_stride >= rb && (int64_t)job->down_row_stride >= rb,
+                FTC_E_INVALID, "ftc_backend_run_expert_chunk: stride smaller than a row");
+    if (inject_fail("ftc_backend_run_expert_chunk"))
+        return set_error(FTC_E_INJECTED, "ftc_backend_run_expert_chunk: injected failure");
+    std::lock_guard<std::mutex> lk(be->mu);
+    // Windows: cached ranges are used in place; anything else is streamed in
+    // (the reference's staging upload, ft/include/ft/chunker.h:126-147).
+    const size_t gu_bytes = (size_t)((IC - 1) * (int64_t)job->gate_up_row_stride + rb);
+    const size_t dn_bytes = (size_t)((IC - 1) * (int64_t)job->down_row_stride + rb);
+    const void* win[3] = {job->gate, job->up, job->down};
+    const size_t wbytes[3] = {gu_bytes, gu_bytes, dn_bytes};
+    const void* dev[3] = {nullptr, nullptr, nullptr};
+    size_t stream_off[3], stream_total = 0;
+    for (int i = 0; i < 3; ++i) {
+        const CacheEntry* e = be->find(win[i], wbytes[i]);
+        if (e) {
+            dev[i] = static_cast<const uint8_t*>(e->dev) + ((const uint8_t*)win[i] - e->host);
+        } else {
+            stream_off[i] = stream_total;
+            stream_total += (wbytes[i] + 255) & ~(size_t)255;
+        }
+    }
+    if (stream_total) {
+        if ((rc = be->dwin.ensure(stream_total))) return rc;
+        for (int i = 0; i < 3; ++i)
+            if (!dev[i]) {
+                void* d = static_cast<uint8_t*>(be->dwin.p) + stream_off[i];
+                FTC_CUDA(cudaMemcpyAsync(d, win[i], wbytes[i], cudaMemcpyHostToDevice, be->stream));
+                dev[i] = d;
+            }
+    }
+    const size_t xb = (size_t)(M * K) * 4, hb = (size_t)(M * IC) * 4;
+    if ((rc = be->pin_in.ensure(2 * xb)) || (rc = be->pin_out.ensure(xb)) ||
+        (rc = be->dx.ensure(2 * xb)) || (rc = be->dtmp.ensure(3 * hb + 768)))
+        return rc;
+    std::memcpy(be->pin_in.p, job->x, xb);
+    std::memcpy(static_cast<uint8_t*>(be->pin_in.p) + xb, job->out, xb);
+    FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, 2 * xb, cudaMemcpyHostToDevice, be->stream));
+    float* dxp = static_cast<float*>(be->dx.p);
+    float* dout = reinterpret_cast<float*>(static_cast<uint8_t*>(be->dx.p) + xb);
+    uint8_t* t = static_cast<uint8_t*>(be->dtmp.p);
+    float* g = reinterpret_cast<float*>(t);
+    float* u = reinterpret_cast<float*>(t + ((hb + 255) & ~(size_t)255));
+    float* h = reinterpret_cast<float*>(t + 2 * ((hb + 255) & ~(size_t)255));
+    if ((rc = expert_chunk_dev(job->dtype, dxp, dout, dev[0], dev[1], dev[2], M, K, IC,
+                               (int64_t)job->gate_up_row_stride, (int64_t)job->down_row_stride, g,
+                               u, h, be->stream)))
+        return rc;
+    FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dout, xb, cudaMemcpyDeviceToHost, be->stream));
+    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    std::memcpy(job->out, be->pin_out.p, xb);
+    return ok();
+}
+
+int ftc_backend_sync(ftc_backend* be) {
+    int rc = bind(be);
+    if (rc) return rc;
+    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    return ok();
+}
+
+int ftc_device_status(void* stream, int* status) {
+    FTC_REQUIRE(status, FTC_E_INVALID, "ftc_device_status: null status");
+    FTC_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    int v = 0;
+    for (int (*rd)(int) : {devstat_gemv_q4k}) {
+        const int s = rd(1);
+        FTC_REQUIRE(s >= 0, FTC_E_CUDA, "ftc_device_status: cannot read the status word");
+        v |= s;
+    }
+    *status = v;
+    return ok();
+}
+
+int ftc_dequant(int dtype, const void* w, int64_t n_rows, int64_t k, int64_t row_stride,
+                float* out, void* stream) {
+    int rc = dequant(dtype, w, n_rows, k, row_stride, out, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
+                    const float* x, int64_t M, float* y, void* stream) {
+    int rc = mul_mat_vec(dtype, w, N, K, row_stride, x, M, y, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+}  // extern "C"

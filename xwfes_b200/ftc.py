@@ -1,0 +1,249 @@
+"""ctypes binding of libftcuda.so (include/ftc.h).
+
+Device-pointer entry points take torch CUDA tensors (their ``data_ptr()``)
+and launch on torch's current stream unless a stream is given.  The library
+must exist: there is no CPU fallback, a missing or unbuildable library raises.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import formats as F
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libftcuda.so")
+
+_p = C.c_void_p
+_i64 = C.c_int64
+
+# name -> (restype, argtypes); one line per declaration in include/ftc.h
+SIGNATURES = {
+    "ftc_last_error": (C.c_char_p, []),
+    "ftc_abi_version": (C.c_int, []),
+    "ftc_row_bytes": (_i64, [C.c_int, _i64]),
+    "ftc_backend_create": (C.c_int, [C.c_int, C.POINTER(_p)]),
+    "ftc_backend_destroy": (None, [_p]),
+    "ftc_backend_info": (C.c_int, [_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_uint64)]),
+    "ftc_backend_upload": (C.c_int, [_p, _p, C.c_size_t]),
+    "ftc_backend_evict": (C.c_int, [_p, _p]),
+    "ftc_backend_cached_bytes": (C.c_int, [_p, C.POINTER(C.c_uint64)]),
+    "ftc_backend_matmul": (C.c_int, [_p, _p, _i64, _i64, _p, C.c_int, _i64, _p]),
+    "ftc_backend_run_expert_chunk": (C.c_int, [_p, _p]),
+    "ftc_backend_sync": (C.c_int, [_p]),
+    "ftc_backend_stream": (_p, [_p]),
+    "ftc_backend_device_ptr": (_p, [_p, _p]),
+    "ftc_device_status": (C.c_int, [_p, C.POINTER(C.c_int)]),
+    "ftc_dequant": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _p]),
+    "ftc_mul_mat_vec": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
+}
+
+
+class FtcError(RuntimeError):
+    def __init__(self, fn, rc, msg):
+        super().__init__(f"{fn} failed (status {rc}): {msg}")
+        self.rc = rc
+
+
+class ExpertChunkJob(C.Structure):
+    """``ftc_expert_chunk_job`` == ft::ExpertChunkJob (ft/include/ft/backend.h:7-19)."""
+    _fields_ = [("x", _p), ("out", _p), ("gate", _p), ("up", _p), ("down", _p),
+                ("dtype", C.c_int), ("M", _i64), ("K", _i64), ("IC", _i64),
+                ("gate_up_row_stride", C.c_size_t), ("down_row_stride", C.c_size_t)]
+
+
+_lib = None
+
+
+def lib():
+    """Load libftcuda.so (raises if it was never built: no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python -m xwfes_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error():
+    return lib().ftc_last_error().decode(errors="replace")
+
+
+def check(rc, fn):
+    if rc != 0:
+        raise FtcError(fn, rc, last_error())
+
+
+def _stream(stream):
+    if stream is not None:
+        return C.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+    import torch
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def device_status(stream=None):
+    """Synchronize the stream and return (and clear) the kernels' status word
+    (0: every bounded wait completed)."""
+    v = C.c_int()
+    check(lib().ftc_device_status(_stream(stream), C.byref(v)), "ftc_device_status")
+    return v.value
+
+
+def row_bytes(dtype, k):
+    return int(lib().ftc_row_bytes(F.dtype_id(dtype), k))
+
+
+# ------------------------------------------------------------ kernels
+
+def mul_mat_vec(w, dtype, n, k, x, y=None, row_stride=None, stream=None):
+    """y[m][n] = sum_k x[m][k] W[n][k] on the GPU (fp32, M = x.shape[0] <= 8).
+
+    ``w``: uint8 CUDA tensor of GGUF blocks; ``x``: fp32 CUDA tensor [M, k].
+    """
+    import torch
+    t = F.dtype_id(dtype)
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if y is None:
+        y = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    rs = row_stride if row_stride is not None else row_bytes(t, k)
+    check(lib().ftc_mul_mat_vec(t, w.data_ptr(), n, k, rs, x2.data_ptr(), m, y.data_ptr(),
+                                _stream(stream)), "ftc_mul_mat_vec")
+    return y
+
+
+def dequant(w, dtype, n_rows, k, out=None, row_stride=None, stream=None):
+    import torch
+    t = F.dtype_id(dtype)
+    if out is None:
+        out = torch.empty((n_rows, k), dtype=torch.float32, device=w.device)
+    rs = row_stride if row_stride is not None else row_bytes(t, k)
+    check(lib().ftc_dequant(t, w.data_ptr(), n_rows, k, rs, out.data_ptr(), _stream(stream)),
+          "ftc_dequant")
+    return out
+
+
+# ------------------------------------------------------------ host tensor
+
+class HostTensor:
+    """ft::HostTensor (ft/include/ft/types.h:119-140): a view of GGUF blocks in
+    host memory.  ne[0] = cols (K, the block axis), ne[1] = rows (N),
+    ne[2] = expert planes."""
+
+    def __init__(self, data, dtype, ne, name="t"):
+        self.data = np.ascontiguousarray(data, dtype=np.uint8)
+        self.dtype = F.dtype_id(dtype)
+        self.ne = tuple(int(v) for v in ne) + (1,) * (4 - len(ne))
+        self.name = name
+        if self.data.nbytes < self.row_stride_bytes() * self.ne[1] * self.ne[2] * self.ne[3]:
+            raise ValueError("HostTensor: data smaller than its shape")
+
+    def cols(self):
+        return self.ne[0]
+
+    def rows(self):
+        return self.ne[1]
+
+    def row_stride_bytes(self):
+        return F.row_bytes(self.dtype, self.ne[0])
+
+    def slice_bytes(self):
+        return self.row_stride_bytes() * self.ne[1]
+
+    def ptr(self, offset=0):
+        return self.data.ctypes.data + offset
+
+    def slice(self, e):
+        """Host address of expert plane e (HostTensor::slice)."""
+        return self.ptr(self.slice_bytes() * e)
+
+    @property
+    def nbytes(self):
+        return self.data.nbytes
+
+
+# ------------------------------------------------------------ backend
+
+class CudaBackend:
+    """Python mirror of the ft::IBackend a CUDA build plugs in
+    (ft/include/ft/backend.h:21-40), over the ftc_backend_* C ABI.  Host
+    buffers in, host buffers out; weights cached in HBM by host address."""
+
+    def __init__(self, device=0):
+        h = C.c_void_p()
+        check(lib().ftc_backend_create(device, C.byref(h)), "ftc_backend_create")
+        self._h = h
+        self._keep = {}  # host tensors whose addresses key the cache, by address
+
+    def close(self):
+        if self._h:
+            lib().ftc_backend_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def name(self):
+        buf = C.create_string_buffer(256)
+        mem = C.c_uint64()
+        check(lib().ftc_backend_info(self._h, buf, 256, C.byref(mem)), "ftc_backend_info")
+        return buf.value.decode()
+
+    def info(self):
+        buf = C.create_string_buffer(256)
+        mem = C.c_uint64()
+        check(lib().ftc_backend_info(self._h, buf, 256, C.byref(mem)), "ftc_backend_info")
+        return {"name": buf.value.decode(), "integrated": False, "uma": False,
+                "mem_bytes": mem.value}
+
+    def ready(self):
+        return bool(self._h)
+
+    def stream(self):
+        return lib().ftc_backend_stream(self._h)
+
+    def upload(self, t):
+        """Pre-load a HostTensor's blocks into HBM (Engine::load time)."""
+        self._keep[t.ptr()] = t
+        check(lib().ftc_backend_upload(self._h, t.ptr(), t.nbytes), "ftc_backend_upload")
+
+    def evict(self, t):
+        check(lib().ftc_backend_evict(self._h, t.ptr()), "ftc_backend_evict")
+        self._keep.pop(t.ptr(), None)
+
+    def cached_bytes(self):
+        v = C.c_uint64()
+        check(lib().ftc_backend_cached_bytes(self._h, C.byref(v)), "ftc_backend_cached_bytes")
+        return v.value
+
+    def device_ptr(self, t, offset=0):
+        return lib().ftc_backend_device_ptr(self._h, t.ptr(offset))
+
+    def matmul(self, x, M, K, W, y):
+        """IBackend::matmul: x fp32 [M][K] host, y fp32 [M][N] host (written)."""
+        assert x.dtype == np.float32 and x.flags.c_contiguous and x.size >= M * K
+        assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * W.rows()
+        self._keep[W.ptr()] = W
+        check(lib().ftc_backend_matmul(self._h, x.ctypes.data, M, K, W.ptr(), W.dtype,
+                                       W.rows(), y.ctypes.data), "ftc_backend_matmul")
+
+    def run_expert_chunk(self, x, out, gate, up, down, dtype, M, K, IC, gu_stride, dn_stride):
+        """IBackend::run_expert_chunk with host addresses (ints) for the
+        gate/up/down windows; ``out`` is accumulated into."""
+        assert out.dtype == np.float32 and out.flags.c_contiguous
+        job = ExpertChunkJob(x.ctypes.data, out.ctypes.data, gate, up, down, F.dtype_id(dtype),
+                             M, K, IC, gu_stride, dn_stride)
+        check(lib().ftc_backend_run_expert_chunk(self._h, C.byref(job)),
+              "ftc_backend_run_expert_chunk")
+
+    def sync(self):
+        check(lib().ftc_backend_sync(self._h), "ftc_backend_sync")
