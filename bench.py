@@ -247,6 +247,9 @@ def run_ours(args, rank, world, local_rank):
     h2d = N_LAYERS * sum(4 * k for _, _, k in LAYER)
     d2h = N_LAYERS * sum(4 * n for _, n, _ in LAYER)
 
+    prefill = time_prefill(dev)
+    gemm_status = ftc.device_status()
+
     # max over ranks
     t = torch.tensor([ms, e2e_ms, k_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -307,11 +310,61 @@ def run_ours(args, rank, world, local_rank):
             "d2h_bytes_per_step": d2h,
             "api": "ftc_backend_matmul (ft::IBackend::matmul), pinned staging, sync per call",
         },
+        "prefill_dequant_gemm": prefill_summary(prefill, gemm_status),
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
         "setup_s": round(setup_s, 1),
     }
     return line
+
+
+PREFILL_SHAPES = [(14336, 4096), (4096, 14336)]
+PREFILL_M = [128, 512, 2048, 8192]
+
+
+def time_prefill(dev, reps=20, copies=4):
+    """Config 3: Q4_K dequant-GEMM (tcgen05) at every (N, K) x M, bf16
+    activations, bf16 output.  Each timed launch uses the next of `copies`
+    weight copies and a distinct activation tensor per M, so consecutive
+    launches do not find their tiles in L2 (4 x 33 MB + activations)."""
+    import torch
+    from xwfes_b200 import ftc
+    out = {}
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream()
+    for n, k in PREFILL_SHAPES:
+        ws = [torch.from_numpy(S.weight(F.Q4_K, n, k, seed=c, name=f"p.{n}x{k}")).to(dev)
+              for c in range(copies)]
+        for m in PREFILL_M:
+            x = torch.from_numpy(S.activations_bf16(m, k, seed=0, name=f"p.{m}")).to(dev).view(
+                torch.bfloat16)
+            y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            for i in range(3):
+                ftc.gemm(ws[i % copies], F.Q4_K, n, k, x, y=y, y_dtype=F.BF16)
+            torch.cuda.synchronize()
+            ev0.record(st)
+            for i in range(reps):
+                ftc.gemm(ws[i % copies], F.Q4_K, n, k, x, y=y, y_dtype=F.BF16)
+            ev1.record(st)
+            torch.cuda.synchronize()
+            us = ev0.elapsed_time(ev1) * 1e3 / reps
+            out[f"{n}x{k}_m{m}"] = {"us": round(us, 2),
+                                    "tflops": round(2.0 * m * n * k / (us * 1e-6) / 1e12, 1)}
+        del ws
+    return out
+
+
+def prefill_summary(prefill, status):
+    _, bf16_peak, kind = peaks()
+    big = [v["tflops"] for kk, v in prefill.items() if kk.endswith("_m8192")]
+    best = max(v["tflops"] for v in prefill.values())
+    head = sum(big) / len(big)
+    return {"metric": "Q4_K prefill dequant-GEMM TFLOPS (config 3, M=8192, mean of both shapes)",
+            "value": round(head, 1), "unit": "TFLOP/s",
+            "frac_of_peak": round(head / bf16_peak, 3),
+            "peak": bf16_peak, "peak_kind": f"{kind} bf16 dense (MEASURED_PEAKS.json bf16_tflops)",
+            "best": best, "per_shape": prefill, "device_status": status,
+            "dtype": "bf16 x bf16(dequantized Q4_K) -> fp32 accumulate -> bf16"}
 
 
 def traffic_from_profiles():

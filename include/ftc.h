@@ -152,6 +152,17 @@ int ftc_dequant(int dtype, const void* w, int64_t n_rows, int64_t k, int64_t row
 int ftc_mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
                     const float* x, int64_t M, float* y, void* stream);
 
+/* Prefill dequant-GEMM on the tcgen05 tensor cores:
+ *   y[m][n] = sum_k x[m][k] * W[n][k]      m < M, n < N
+ * W: Q4_K rows (16-byte aligned, row_stride % 16 == 0, K % 256 == 0).
+ * x: [M][K] bf16 or fp16 (x_dtype), 16-byte aligned.  Each weight tile is
+ * dequantized on chip to x's 16-bit type (fp32 arithmetic, one rounding to
+ * 16 bits) and multiplied with fp32 accumulation.  y: [M][N] in y_dtype
+ * (FTC_F32, FTC_BF16 or FTC_F16).  The per-row semantics of
+ * ft::CpuBackend::matmul (ft/src/cpu_backend.cpp:90-104) for M > 1. */
+int ftc_gemm(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x,
+             int x_dtype, int64_t M, void* y, int y_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,125 @@
+"""GPU parity of the tcgen05 prefill dequant-GEMM (ftc_gemm).
+
+Exactness first: with one-hot activation rows, y[m][n] is a single product
+1.0 * w16[n][k_m] accumulated in fp32, so it must equal the dequantized weight
+rounded once to the operand type -- this pins the on-chip dequant, the
+128-byte swizzled operand layout and the token/row mapping bit for bit.
+
+Float tolerance: the GEMM multiplies 16-bit operands (activations as given,
+weights rounded to the same 16-bit type) with fp32 accumulation.
+  * Against an fp32 reference on the SAME 16-bit operands (isolates the
+    kernel's own arithmetic): relative error <= 2e-3 with a floor of
+    0.1 * rms(y).  The tensor cores sum each 16-product MMA step internally
+    before the fp32 accumulate, which over K = 14336 differs from sequential
+    fp32 FMAs by ~2e-5 * rms(y), hence the larger floor than the GEMV's.
+  * Against the exact-weight oracle (the reference's arithmetic on fp32
+    dequantized weights): max|y - ref| / max|ref| <= 2e-3; the rounding of
+    the weights to 16 bits is the extra error the tensor-core path adds."""
+import os
+
+import numpy as np
+import pytest
+
+from xwfes_b200 import formats as F, synth as S
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+THREADS = os.cpu_count() or 8
+
+
+@pytest.fixture(scope="module")
+def ftc():
+    assert torch.cuda.is_available()
+    from xwfes_b200 import ftc as mod
+    mod.lib()
+    return mod
+
+
+def rel_err(y, ref, floor=1e-2):
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    rms = np.sqrt(np.mean(ref * ref))
+    return float(np.max(np.abs(y - ref) / (np.abs(ref) + floor * rms)))
+
+
+def norm_err(y, ref):
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.max(np.abs(y - ref)) / np.max(np.abs(ref)))
+
+
+TDT = {F.BF16: torch.bfloat16, F.F16: torch.float16}
+
+
+def to16(a32, t):
+    return torch.from_numpy(np.ascontiguousarray(a32, dtype=np.float32)).to(TDT[t])
+
+
+@pytest.mark.parametrize("xt", [F.F16, F.BF16])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 1024), (256, 384, 512), (200, 130, 256)])
+def test_gemm_one_hot_exact(ftc, oracle, xt, m, n, k):
+    w = S.weight(F.Q4_K, n, k, seed=2, name="gemm.onehot")
+    deq = oracle.dequant_rows(w, F.Q4_K, k)
+    w16 = to16(deq, xt).float().numpy()            # one rounding to the operand type
+    ks = (np.arange(m) * 37 + 11) % k
+    x = np.zeros((m, k), dtype=np.float32)
+    x[np.arange(m), ks] = 1.0
+    y = ftc.gemm(torch.from_numpy(w).cuda(), F.Q4_K, n, k, to16(x, xt).cuda(), y_dtype=F.F32)
+    torch.cuda.synchronize()
+    assert ftc.device_status() == 0
+    got = y.cpu().numpy()
+    assert np.array_equal(got, w16[:, ks].T)
+
+
+def _torch_ref(ftc, wd, n, k, x16):
+    """fp32 reference on the same 16-bit operands: dequantized weights
+    (bit-exact kernel, verified against the oracle) rounded to x's type."""
+    deq = ftc.dequant(wd, F.Q4_K, n, k)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = x16.float() @ deq.to(x16.dtype).float().T
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    return ref
+
+
+@pytest.mark.parametrize("xt", [F.F16, F.BF16])
+@pytest.mark.parametrize("m,n,k", [(256, 512, 2048), (130, 1000, 4096), (512, 256, 14336)])
+def test_gemm_random_vs_oracle(ftc, oracle, xt, m, n, k):
+    w = S.weight(F.Q4_K, n, k, seed=3, name="gemm.rand")
+    xb = S.activations_f32(m, k, seed=3)
+    x16 = to16(xb, xt)
+    wd = torch.from_numpy(w).cuda()
+    y = ftc.gemm(wd, F.Q4_K, n, k, x16.cuda(), y_dtype=F.F32)
+    ref16 = _torch_ref(ftc, wd, n, k, x16.cuda())
+    torch.cuda.synchronize()
+    assert ftc.device_status() == 0
+    got = y.cpu().numpy()
+    assert rel_err(got, ref16.cpu().numpy(), floor=0.1) <= 2e-3
+    # the reference's own arithmetic (fp32 weights, fp32 accumulate) on the
+    # same activations, for a row subset
+    rows = slice(0, min(m, 64))
+    ora = oracle.matmul(x16.float().numpy()[rows], w, F.Q4_K, k, threads=THREADS)
+    assert norm_err(got[rows], ora) <= 2e-3
+
+
+@pytest.mark.parametrize("n,k", [(14336, 4096), (4096, 14336)])
+@pytest.mark.parametrize("m", [128, 512, 2048, 8192])
+def test_gemm_config3(ftc, oracle, n, k, m):
+    """Config 3 at full size, bf16 activations and bf16 output."""
+    w = S.weight(F.Q4_K, n, k, seed=0, name=f"c3.{n}x{k}")
+    wd = torch.from_numpy(w).cuda()
+    x16 = torch.from_numpy(S.activations_bf16(m, k, seed=0, name=f"c3.{m}")).cuda().view(
+        torch.bfloat16)
+    y = ftc.gemm(wd, F.Q4_K, n, k, x16, y_dtype=F.BF16)
+    y32 = ftc.gemm(wd, F.Q4_K, n, k, x16, y_dtype=F.F32)
+    ref = _torch_ref(ftc, wd, n, k, x16)
+    torch.cuda.synchronize()
+    assert ftc.device_status() == 0
+    # fp32 output against the same-operand fp32 reference
+    assert rel_err(y32.cpu().numpy(), ref.cpu().numpy(), floor=0.1) <= 2e-3
+    # bf16 output is the fp32 result rounded once
+    assert torch.equal(y, y32.to(torch.bfloat16))
+    rows = slice(0, 16)
+    ora = oracle.matmul(x16[rows].float().cpu().numpy(), w, F.Q4_K, k, threads=THREADS)
+    assert norm_err(y32[rows].cpu().numpy(), ora) <= 2e-3

@@ -56,8 +56,12 @@ int expert_chunk_dev(int dtype, const float* x, float* out, const void* gate, co
                      const void* down, int64_t M, int64_t K, int64_t IC, int64_t gu_stride,
                      int64_t dn_stride, float* gbuf, float* ubuf, float* hbuf, cudaStream_t st);
 
+int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x, int x_dtype,
+             int64_t M, void* y, int y_dtype, cudaStream_t st);
+
 // status readers of the translation units whose kernels use bounded waits
 int devstat_gemv_q4k(int clear);
+int devstat_gemm_q4k(int clear);
 
 }  // namespace ftc
 
@@ -373,7 +377,7 @@ int ftc_device_status(void* stream, int* status) {
     FTC_REQUIRE(status, FTC_E_INVALID, "ftc_device_status: null status");
     FTC_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
     int v = 0;
-    for (int (*rd)(int) : {devstat_gemv_q4k}) {
+    for (int (*rd)(int) : {devstat_gemv_q4k, devstat_gemm_q4k}) {
         const int s = rd(1);
         FTC_REQUIRE(s >= 0, FTC_E_CUDA, "ftc_device_status: cannot read the status word");
         v |= s;
@@ -391,6 +395,13 @@ int ftc_dequant(int dtype, const void* w, int64_t n_rows, int64_t k, int64_t row
 int ftc_mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
                     const float* x, int64_t M, float* y, void* stream) {
     int rc = mul_mat_vec(dtype, w, N, K, row_stride, x, M, y, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_gemm(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x,
+             int x_dtype, int64_t M, void* y, int y_dtype, void* stream) {
+    FTC_REQUIRE(dtype == FTC_Q4_K, FTC_E_UNSUPPORTED, "ftc_gemm: only Q4_K weights");
+    int rc = gemm_q4k(w, N, K, row_stride, x, x_dtype, M, y, y_dtype, (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

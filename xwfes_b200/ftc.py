@@ -36,6 +36,7 @@ SIGNATURES = {
     "ftc_device_status": (C.c_int, [_p, C.POINTER(C.c_int)]),
     "ftc_dequant": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _p]),
     "ftc_mul_mat_vec": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
+    "ftc_gemm": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, C.c_int, _i64, _p, C.c_int, _p]),
 }
 
 
@@ -115,6 +116,27 @@ def mul_mat_vec(w, dtype, n, k, x, y=None, row_stride=None, stream=None):
     rs = row_stride if row_stride is not None else row_bytes(t, k)
     check(lib().ftc_mul_mat_vec(t, w.data_ptr(), n, k, rs, x2.data_ptr(), m, y.data_ptr(),
                                 _stream(stream)), "ftc_mul_mat_vec")
+    return y
+
+
+_TORCH_OUT = {F.F32: "float32", F.BF16: "bfloat16", F.F16: "float16"}
+
+
+def gemm(w, dtype, n, k, x, y=None, y_dtype=F.BF16, row_stride=None, stream=None):
+    """Tensor-core dequant-GEMM: y[m][n] = sum_k x[m][k] W[n][k].
+
+    ``x``: bf16 or fp16 CUDA tensor [M, k]; ``y`` in ``y_dtype``."""
+    import torch
+    t = F.dtype_id(dtype)
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    xt = {torch.bfloat16: F.BF16, torch.float16: F.F16}[x2.dtype]
+    yt = F.dtype_id(y_dtype)
+    if y is None:
+        y = torch.empty((m, n), dtype=getattr(torch, _TORCH_OUT[yt]), device=x.device)
+    rs = row_stride if row_stride is not None else row_bytes(t, k)
+    check(lib().ftc_gemm(t, w.data_ptr(), n, k, rs, x2.data_ptr(), xt, m, y.data_ptr(), yt,
+                         _stream(stream)), "ftc_gemm")
     return y
 
 
