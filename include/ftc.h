@@ -163,6 +163,24 @@ int ftc_mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_
 int ftc_gemm(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x,
              int x_dtype, int64_t M, void* y, int y_dtype, void* stream);
 
+/* The expert chunk of ftc_backend_run_expert_chunk on DEVICE buffers,
+ * without allocating anything: for callers that cannot call cudaMalloc (an
+ * engine whose HBM is owned by its own allocator, code inside someone
+ * else's stream capture, a serving thread where allocation is forbidden).
+ * No counterpart in the reference: its backends always own their buffers.
+ *   h[m][i]   = silu(x_m . gate_i) * (x_m . up_i)      i < IC
+ *   out[m][k] += sum_i h[m][i] * down_i[k]
+ * x, out: device fp32 [M][K]; gate/up/down: device block pointers.  The
+ * intermediate gate, up and h live in one library-owned __device__ array
+ * (768 KB on every GPU that loads the library): M * IC must be at most
+ * FTC_EXPERT_STATIC_MAX_HC, else FTC_E_INVALID.  All calls on a device share
+ * that array, so calls that overlap on the GPU race; the first call on a
+ * device looks up the array's address (make it before any stream capture). */
+#define FTC_EXPERT_STATIC_MAX_HC 65536
+int ftc_expert_chunk_static(int dtype, const float* x, float* out, const void* gate,
+                            const void* up, const void* down, int64_t M, int64_t K, int64_t IC,
+                            int64_t gate_up_row_stride, int64_t down_row_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

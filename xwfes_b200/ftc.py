@@ -37,6 +37,8 @@ SIGNATURES = {
     "ftc_dequant": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _p]),
     "ftc_mul_mat_vec": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "ftc_gemm": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, C.c_int, _i64, _p, C.c_int, _p]),
+    "ftc_expert_chunk_static": (C.c_int, [C.c_int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+                                          _i64, _p]),
 }
 
 
