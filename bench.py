@@ -45,6 +45,11 @@ N_LAYERS = 8
 # activation vector each GEMV reads (q/k/v share one, gate/up share one)
 X_OF = {"q": "attn_in", "k": "attn_in", "v": "attn_in", "o": "attn_out", "gate": "ffn_in",
         "up": "ffn_in", "down": "ffn_mid"}
+# launches of one decode layer: matrices that read the same activations go
+# in one grouped launch, as a decode step issues them (o and down each wait
+# for the attention / SiLU result in a real model)
+GROUPS = [("qkv", ("q", "k", "v")), ("o", ("o",)), ("gate_up", ("gate", "up")), ("down", ("down",))]
+SHAPE = {name: (n, k) for name, n, k in LAYER}
 X_LEN = {"attn_in": 4096, "attn_out": 4096, "ffn_in": 4096, "ffn_mid": 14336}
 
 
@@ -159,16 +164,28 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream(device=dev)
     L = ftc.lib()
 
-    def launch(li, name, n, k, s):
-        rc = L.ftc_mul_mat_vec(F.Q4_K, dptr[(li, name)], n, k, F.row_bytes(F.Q4_K, k),
-                               xs[X_OF[name]].data_ptr(), 1, ys[name].data_ptr(), s)
+    import ctypes as C
+    group_args = {}
+    for li in range(N_LAYERS):
+        for gname, members in GROUPS:
+            P = len(members)
+            k = SHAPE[members[0]][1]
+            group_args[(li, gname)] = (
+                P, (C.c_void_p * P)(*[dptr[(li, m)] for m in members]),
+                (C.c_int64 * P)(*[SHAPE[m][0] for m in members]), k,
+                xs[X_OF[members[0]]].data_ptr(),
+                (C.c_void_p * P)(*[ys[m].data_ptr() for m in members]))
+
+    def launch(li, gname, s):
+        P, wa, na, k, xp, ya = group_args[(li, gname)]
+        rc = L.ftc_mul_mat_vec_multi(F.Q4_K, P, wa, na, k, F.row_bytes(F.Q4_K, k), xp, 1, ya, s)
         if rc:
-            raise ftc.FtcError("ftc_mul_mat_vec", rc, ftc.last_error())
+            raise ftc.FtcError("ftc_mul_mat_vec_multi", rc, ftc.last_error())
 
     def step(s):
         for li in range(N_LAYERS):
-            for name, n, k in LAYER:
-                launch(li, name, n, k, s)
+            for gname, _ in GROUPS:
+                launch(li, gname, s)
 
     sp = stream.cuda_stream
     with torch.cuda.stream(stream):
@@ -184,7 +201,7 @@ def run_ours(args, rank, world, local_rank):
 
     wbytes, xybytes = layer_bytes()
     step_bytes = N_LAYERS * (wbytes + xybytes)
-    launches_per_step = N_LAYERS * len(LAYER)
+    launches_per_step = N_LAYERS * len(GROUPS)
 
     def barrier():
         if world > 1:
@@ -205,11 +222,11 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
 
-    # dominant kernel alone: gate shape over the 8 layer copies, graph-replayed
+    # dominant kernel alone: the gate/up launch over the 8 layer copies, graph-replayed
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2, stream=stream):
         for li in range(N_LAYERS):
-            launch(li, "gate", 14336, 4096, sp)
+            launch(li, "gate_up", sp)
     reps = 200
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -221,7 +238,29 @@ def run_ours(args, rank, world, local_rank):
         ev1.record(stream)
         torch.cuda.synchronize()
     k_ms = ev0.elapsed_time(ev1) / (reps * N_LAYERS)
-    k_bytes = F.row_bytes(F.Q4_K, 4096) * 14336 + 4 * (4096 + 14336)
+    k_bytes = 2 * F.row_bytes(F.Q4_K, 4096) * 14336 + 4 * (4096 + 2 * 14336)
+
+    # every launch group alone (8 launches per graph), for the per-group breakdown
+    per_group = {}
+    for gname, members in GROUPS:
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg, stream=stream):
+            for li in range(N_LAYERS):
+                launch(li, gname, sp)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                gg.replay()
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(50):
+                gg.replay()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+        us = ev0.elapsed_time(ev1) * 1e3 / (50 * N_LAYERS)
+        gbytes = sum(F.row_bytes(F.Q4_K, SHAPE[m][1]) * SHAPE[m][0] for m in members)
+        per_group[gname] = {"us": round(us, 2), "MB": round(gbytes / 1e6, 1),
+                            "GBps": round(gbytes / (us * 1e-6) / 1e9, 0)}
+        del gg
 
     # e2e through the C ABI: host x in, host y out, per ftc_backend_matmul call
     ext = torch.cuda.ExternalStream(be.stream(), device=dev)
@@ -283,7 +322,8 @@ def run_ours(args, rank, world, local_rank):
             "bytes_per_step": step_bytes,
             "l2": "inputs larger than L2: 8 distinct layer copies (982 MB) per step",
             "parallelism": f"replicas x{world}",
-            "graph": "CUDA graph of the 56-GEMV step",
+            "graph": "CUDA graph of the step: 8 layers x 4 launches (q/k/v grouped, o, "
+                     "gate/up grouped, down), programmatic dependent launch between them",
         },
         "pct_of_peak": round(100 * gbs / world / hbm, 1),
         "tokens_per_s": round(world * 1e3 / (ms / N_LAYERS * 32), 1),
@@ -291,7 +331,7 @@ def run_ours(args, rank, world, local_rank):
                              "at this layer time x world (attention and head excluded)",
         "roofline": {
             "bound": "hbm",
-            "kernel": "gemv_q4k (14336x4096, batch 1)",
+            "kernel": "gemv_q4k_dp4a, grouped gate+up (2 x 14336x4096), batch 1",
             "achieved": round(k_gbs, 1),
             "peak": hbm,
             "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs burst)",
@@ -299,6 +339,7 @@ def run_ours(args, rank, world, local_rank):
             "frac": round(k_gbs / hbm, 3),
             "traffic": traffic_from_profiles(),
             "bytes_per_launch": k_bytes,
+            "per_group": per_group,
             "us_per_launch": round(k_ms * 1e3, 3),
         },
         "e2e": {
@@ -383,17 +424,18 @@ def traffic_from_profiles():
 
 
 def run_ncu_probe():
-    """Five launches of the gate-shaped GEMV (14336x4096 Q4_K, 33 MB, larger
-    than nothing else on the device): the small case for ncu captures."""
+    """Five grouped gate+up launches (2 x 14336x4096 Q4_K, 66 MB), the bench's
+    dominant kernel, on one layer copy: the small case for ncu captures."""
     import torch
     from xwfes_b200 import ftc
     dev = torch.device("cuda", 0)
-    w = torch.from_numpy(S.weight(F.Q4_K, 14336, 4096, seed=0, name="L0.gate")).to(dev)
+    ws = [torch.from_numpy(S.weight(F.Q4_K, 14336, 4096, seed=0, name=f"L0.{m}")).to(dev)
+          for m in ("gate", "up")]
     x = torch.from_numpy(S.activations_f32(1, 4096, seed=0, name="ffn_in")).to(dev)
     for _ in range(5):
-        y = ftc.mul_mat_vec(w, F.Q4_K, 14336, 4096, x)
+        ys = ftc.mul_mat_vec_multi(ws, F.Q4_K, [14336, 14336], 4096, x)
     torch.cuda.synchronize()
-    print(json.dumps({"probe": "gemv_q4k 14336x4096 x5", "y0": float(y[0, 0])}))
+    print(json.dumps({"probe": "gemv_q4k_dp4a gate+up 2x14336x4096 x5", "y0": float(ys[0][0, 0])}))
     return 0
 
 

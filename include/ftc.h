@@ -152,6 +152,15 @@ int ftc_dequant(int dtype, const void* w, int64_t n_rows, int64_t k, int64_t row
 int ftc_mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
                     const float* x, int64_t M, float* y, void* stream);
 
+/* Several decode GEMVs that read the same activations (q/k/v, gate/up) in
+ * one launch: for i < n_mats, y_i[m][n] = sum_k x[m][k] * W_i[n][k], n < N[i].
+ * w, N, y: host arrays of n_mats (<= 8) device pointers / row counts; all
+ * matrices share dtype, K and row_stride.  Each y_i equals what
+ * ftc_mul_mat_vec gives for that matrix alone, bit for bit. */
+int ftc_mul_mat_vec_multi(int dtype, int n_mats, const void* const* w, const int64_t* N,
+                          int64_t K, int64_t row_stride, const float* x, int64_t M,
+                          float* const* y, void* stream);
+
 /* Prefill dequant-GEMM on the tcgen05 tensor cores:
  *   y[m][n] = sum_k x[m][k] * W[n][k]      m < M, n < N
  * W: Q4_K rows (16-byte aligned, row_stride % 16 == 0, K % 256 == 0).

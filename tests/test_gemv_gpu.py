@@ -130,6 +130,24 @@ def test_q4_k_batch1_row_counts(ftc, oracle, n):
     assert ftc.device_status() == 0
 
 
+@pytest.mark.parametrize("ns,k", [((4096, 1024, 1024), 4096), ((14336, 14336), 4096),
+                                  ((7, 300, 1), 2560), ((4096, 4096), 14336)])
+def test_grouped_gemv_equals_single(ftc, oracle, ns, k):
+    """q/k/v- and gate/up-style groups in one launch give each matrix exactly
+    its single-launch result."""
+    ws = [S.weight(F.Q4_K, n, k, seed=i, name=f"grp.{i}") for i, n in enumerate(ns)]
+    x = S.activations_f32(1, k, seed=5, name="grp")
+    xd = dev(x)
+    wd = [dev(w) for w in ws]
+    ys = ftc.mul_mat_vec_multi(wd, F.Q4_K, list(ns), k, xd)
+    singles = [ftc.mul_mat_vec(w, F.Q4_K, n, k, xd) for w, n in zip(wd, ns)]
+    torch.cuda.synchronize()
+    assert ftc.device_status() == 0
+    for w, y, y1 in zip(ws, ys, singles):
+        assert torch.equal(y, y1)
+        assert rel_err(y.cpu().numpy(), oracle.matmul(x, w, F.Q4_K, k, threads=THREADS)) <= TOL
+
+
 # ------------------------------------------------ config shapes, full size
 
 CONFIG2 = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)]

@@ -1,30 +1,35 @@
-// gemv_q4k.cu -- the decode GEMV for Q4_K weights, batch 1 and 2:
+// gemv_q4k.cu -- the decode GEMV for Q4_K weights, batch 1:
 //
-//   y[m][n] = sum_k x[m][k] * W[n][k]        W: Q4_K super-blocks of 256
+//   y[n] = sum_k x[k] * W[n][k]        W: Q4_K super-blocks of 256 weights
 //
 // HBM-bound by design: every weight byte crosses HBM once, through a ring of
-// bulk (TMA) copies into shared memory, and the SM spends about 1.8 issue
-// slots per weight so that decoding stays well under the copy rate.
+// bulk (TMA) copies into shared memory, and the SM spends ~1.7 issue slots
+// per weight, so decoding keeps up with the copy rate.
 //
-// Exact-integer activations.  At start-up each consumer lane turns its 64
-// activations into 24-bit integers with one power-of-two scale per 256-block:
-// x = s_b * x_int, |x_int| < 2^22, error <= s_b/2 <= 2^-22 * max|x_block|
-// (zero for activations whose significant bits fit, e.g. one-hot vectors).
-// x_int is held as three byte planes (hi signed, mid and lo unsigned), so
+// Exact-integer activations.  At start-up the CTA turns x into 24-bit
+// integers with one power-of-two scale per 256-block: x = s_b * x_int,
+// |x_int| < 2^22, error <= s_b/2 <= 2^-22 * max|x_block| (zero for
+// activations whose bits fit, e.g. one-hot vectors).  x_int is kept as three
+// byte planes (hi signed, mid and lo unsigned) in shared memory, so
 //   sum_l q_l * x_int_l = 65536*sum(q*hi) + 256*sum(q*mid) + sum(q*lo)
-// comes from six dp4a per eight 4-bit codes, all in exact integer
-// arithmetic; each sub-block's scale and min are applied once per row.
-// Summation order differs from ft::dot_row_f32 (ft/include/ft/quant.h:86-103);
-// the result agrees with the reference's fp32 sum to ~1e-6 relative.
+// comes from six dp4a per eight 4-bit codes in exact integer arithmetic; each
+// sub-block's scale and min are applied once per row.  The summation order
+// differs from ft::dot_row_f32 (ft/include/ft/quant.h:86-103); the result
+// agrees with the reference's fp32 sum to ~1e-6 relative.
 //
-// Work split.  A warp owns 8 super-blocks of K (4 lanes per super-block,
-// lane t of a quartet takes code bytes [32t, 32t+32): sub-blocks 2t and
-// 2t+1), keeps its 64 activations per m in registers for the whole kernel,
-// and every row of a chunk passes through it.  WK = ceil(K/2048) warps cover
-// a row; WR groups of WK warps share the rows of a chunk.  One more warp is
-// the producer: it keeps S chunks of RC rows (contiguous bytes) in flight
-// with cp.async.bulk, and after consumers release a stage it adds their
-// per-row partial sums (fixed order: deterministic) and writes y.
+// Work split.  A consumer warp owns 8 super-blocks of K (4 lanes per
+// super-block: lane t of a quartet takes code bytes [32t, 32t+32), i.e.
+// sub-blocks 2t (low nibbles) and 2t+1 (high nibbles)), keeps the matching
+// 64 activations as plane words in registers, and every row of a chunk
+// passes through it.  WK = ceil(K/2048) warps cover a row; WR groups of WK
+// warps share the rows of a chunk.  One more warp is the producer: it keeps
+// kStages chunks of RC rows (contiguous bytes) in flight with
+// cp.async.bulk and, once consumers release a stage, refills it first and
+// then adds their per-row partials in a fixed order (deterministic) into y.
+//
+// Launched with programmatic dependent launch: weight copies start before
+// griddepcontrol.wait, activations are read after it, so back-to-back GEMVs
+// overlap one kernel's tail with the next one's weight prefetch.
 #include <algorithm>
 
 #include "common.cuh"
@@ -34,66 +39,90 @@ namespace ftc {
 
 FTC_DEVSTAT_READER(devstat_gemv_q4k)
 
+constexpr int kGemvMaxMats = 8;
+
 namespace {
 
 constexpr int kStages = 4;
+constexpr int kPlaneWords = 48;  // per (super-block, quartet lane): 3 planes x 16 words
+constexpr int kMaxThreads = 608; // 18 consumer warps + 1 producer at <= 107 registers
 
-struct XParts {
-    uint32_t h[16], m[16], l[16];  // byte planes of 64 x_int (4 per word)
-    float sum_lo, sum_hi;          // sum of x_int over each 32-weight sub-block
-    float scale;                   // s_b
+}  // namespace
+
+// Up to kGemvMaxMats weight matrices with the same K that read the same
+// activation vector (q/k/v, gate/up): one launch walks all their row chunks.
+struct GemvBatch {
+    const uint8_t* W[kGemvMaxMats];
+    float* y[kGemvMaxMats];
+    int N[kGemvMaxMats];
+    int first_chunk[kGemvMaxMats + 1];  // prefix sums of ceil(N / RC)
+    int P;
 };
 
-// Load 64 activations (16 float4), derive the quartet's power-of-two scale
-// and split into byte planes.  Lanes with !valid contribute zeros.
-__device__ __forceinline__ void load_x_parts(const float* __restrict__ xp, bool valid,
-                                             XParts& P) {
-    float v[64];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        float4 f = valid ? __ldg(reinterpret_cast<const float4*>(xp) + i)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[4 * i] = f.x;
-        v[4 * i + 1] = f.y;
-        v[4 * i + 2] = f.z;
-        v[4 * i + 3] = f.w;
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    // amax in [2^p, 2^(p+1)): s_b = 2^(p-21) keeps |x / s_b| < 2^22.
-    int eb = (int)((__float_as_uint(amax) >> 23) & 0xFF);  // biased exponent
-    int se = max(eb - 21, 1);
-    const float s = __uint_as_float((uint32_t)se << 23);
-    const float inv = __uint_as_float((uint32_t)(254 - se) << 23);
-    int sl = 0, sh = 0;
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-        uint32_t h = 0, m = 0, l = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int q = __float2int_rn(v[4 * u + i] * inv);
-            q = min(max(q, -(1 << 22)), (1 << 22) - 1);
-            if (u < 8) sl += q; else sh += q;
-            h |= ((uint32_t)(q >> 16) & 0xFFu) << (8 * i);
-            m |= ((uint32_t)(q >> 8) & 0xFFu) << (8 * i);
-            l |= ((uint32_t)q & 0xFFu) << (8 * i);
-        }
-        P.h[u] = h;
-        P.m[u] = m;
-        P.l[u] = l;
-    }
-    P.sum_lo = (float)sl;
-    P.sum_hi = (float)sh;
-    P.scale = s;
+namespace {
+
+// d = a (unsigned bytes) . b (signed bytes) + c
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-// One row: this lane's 64 weights (code bytes [32t, 32t+32) of the block)
-// against its activations.  Returns s_b * (d * SQ - dmin * U).
-__device__ __forceinline__ float q4k_row_partial(const uint8_t* blk, int t, bool hi_half,
-                                                 int sh0, const XParts& P) {
+// Per-CTA activation prologue: consumer warp w converts super-blocks w,
+// w + NCW, ... (lane j: elements 8j..8j+7 of the block) into plane words,
+// sub-block sums and the block scale, laid out for the consumers:
+//   planes[(sb*4 + t)*48 + plane*16 + u]   u = word within the lane's 64
+//   sums[(sb*4 + t)*2 + {0: low sub-block, 1: high}],  scales[sb]
+__device__ __forceinline__ void build_planes(const float* __restrict__ x, int nsb, int cw, int ncw,
+                                             int lane, uint32_t* planes, float* sums,
+                                             float* scales) {
+    for (int sb = cw; sb < nsb; sb += ncw) {
+        const float4* xp = reinterpret_cast<const float4*>(x + (int64_t)sb * 256 + 8 * lane);
+        const float4 a = __ldg(xp), b = __ldg(xp + 1);
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        // amax in [2^p, 2^(p+1)): s_b = 2^(p-21) keeps |x / s_b| < 2^22
+        const int eb = (int)((__float_as_uint(amax) >> 23) & 0xFF);
+        const int se = max(eb - 21, 1);
+        const float inv = __uint_as_float((uint32_t)(254 - se) << 23);
+        uint32_t h[2] = {0, 0}, m[2] = {0, 0}, l[2] = {0, 0};
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            // round(x * inv) via the 1.5 * 2^23 magic constant (x * inv is exact)
+            const int q = __float_as_int(fmaf(v[i], inv, 12582912.0f)) - 0x4B400000;
+            sum += q;
+            h[i >> 2] |= ((uint32_t)(q >> 16) & 0xFFu) << (8 * (i & 3));
+            m[i >> 2] |= ((uint32_t)(q >> 8) & 0xFFu) << (8 * (i & 3));
+            l[i >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (i & 3));
+        }
+        const int t = lane >> 3, u = 2 * (lane & 7);
+        uint32_t* dst = planes + (sb * 4 + t) * kPlaneWords;
+        *reinterpret_cast<uint2*>(dst + u) = make_uint2(h[0], h[1]);
+        *reinterpret_cast<uint2*>(dst + 16 + u) = make_uint2(m[0], m[1]);
+        *reinterpret_cast<uint2*>(dst + 32 + u) = make_uint2(l[0], l[1]);
+        // sub-block sums: lanes 8t..8t+3 hold sub-block 2t, 8t+4..8t+7 sub-block 2t+1
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if ((lane & 3) == 0) sums[(sb * 4 + t) * 2 + ((lane >> 2) & 1)] = (float)sum;
+        if (lane == 0) scales[sb] = __uint_as_float((uint32_t)se << 23);
+    }
+}
+
+struct LaneX {
+    uint32_t h[16], m[16], l[16];
+    float sum_lo, sum_hi, scale;
+};
+
+// One row: this lane's 64 weights against its activations.
+// Returns s_b * (d * SQ - dmin * U), SQ = sum q*x_int, U = sum m*x_int.
+__device__ __forceinline__ float q4k_row_partial(const uint8_t* blk, int t, uint32_t use_s2,
+                                                 int sh0, uint32_t mask_a, uint32_t mask_b,
+                                                 const LaneX& X) {
     const uint4 hd = *reinterpret_cast<const uint4*>(blk);
     const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * t);
     const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * t);
@@ -102,50 +131,98 @@ __device__ __forceinline__ float q4k_row_partial(const uint8_t* blk, int t, bool
     uint32_t ml = 0, mh = 0, ll = 0, lh = 0;
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-        const uint32_t lo = w[u] & 0x0F0F0F0Fu;         // sub-block 2t, weights 4u..4u+3
-        const uint32_t hi = (w[u] >> 4) & 0x0F0F0F0Fu;  // sub-block 2t+1
-        hl = __dp4a((int)lo, (int)P.h[u], hl);
-        ml = __dp4a(lo, P.m[u], ml);
-        ll = __dp4a(lo, P.l[u], ll);
-        hh = __dp4a((int)hi, (int)P.h[8 + u], hh);
-        mh = __dp4a(hi, P.m[8 + u], mh);
-        lh = __dp4a(hi, P.l[8 + u], lh);
+        const uint32_t lo = w[u] & 0x0F0F0F0Fu;  // q of sub-block 2t, weights 4u..4u+3
+        const uint32_t hi = w[u] & 0xF0F0F0F0u;  // 16 * q of sub-block 2t+1
+        hl = __dp4a((int)lo, (int)X.h[u], hl);
+        ml = __dp4a(lo, X.m[u], ml);
+        ll = __dp4a(lo, X.l[u], ll);
+        hh = dp4a_us(hi, X.h[8 + u], hh);
+        mh = __dp4a(hi, X.m[8 + u], mh);
+        lh = __dp4a(hi, X.l[8 + u], lh);
     }
     // scales / mins of sub-blocks 2t (byte i) and 2t+1 (byte i+1), i = sh0/8:
     //   sub-blocks 0-3: scale = s0.byte & 63, min = s1.byte & 63
     //   sub-blocks 4-7: scale = (s2.byte & 15) | (s0.byte >> 6) << 4,
     //                   min   = (s2.byte >> 4) | (s1.byte >> 6) << 4
+    // branch-free: mask_a = 0x3F3F / 0x0F0F, mask_b = 0 / 0x3030 per lane
     const uint32_t s0 = hd.y, s1 = hd.z, s2 = hd.w;
-    uint32_t sc, mn;
-    if (hi_half) {
-        sc = ((s2 >> sh0) & 0x0F0Fu) | ((s0 >> (sh0 + 2)) & 0x3030u);
-        mn = ((s2 >> (sh0 + 4)) & 0x0F0Fu) | ((s1 >> (sh0 + 2)) & 0x3030u);
-    } else {
-        sc = (s0 >> sh0) & 0x3F3Fu;
-        mn = (s1 >> sh0) & 0x3F3Fu;
-    }
+    const uint32_t sa = use_s2 ? s2 : s0;
+    const uint32_t ma = use_s2 ? (s2 >> 4) : s1;
+    const uint32_t sc = ((sa >> sh0) & mask_a) | ((s0 >> (sh0 + 2)) & mask_b);
+    const uint32_t mn = ((ma >> sh0) & mask_a) | ((s1 >> (sh0 + 2)) & mask_b);
     const int sc0 = (int)(sc & 0xFF), sc1 = (int)(sc >> 8);
-    const int ph = sc0 * hl + sc1 * hh;                 // |.| < 2^23
-    const int pm = (int)(sc0 * ml + sc1 * mh);          // < 2^24
-    const int pl = (int)(sc0 * ll + sc1 * lh);
+    // high-nibble sums carry a factor 16 (exact: every term is a multiple of 16)
+    const int ph = sc0 * hl + sc1 * (hh >> 4);                            // |.| < 2^23
+    const int pm = (int)(sc0 * ml + sc1 * (mh >> 4));                     // < 2^24
+    const int pl = (int)(sc0 * ll + sc1 * (lh >> 4));
     const float sq = fmaf(65536.f, (float)ph, fmaf(256.f, (float)pm, (float)pl));
-    const float u = fmaf((float)(mn >> 8), P.sum_hi, (float)(mn & 0xFF) * P.sum_lo);
+    const float um = fmaf((float)(mn >> 8), X.sum_hi, (float)(mn & 0xFF) * X.sum_lo);
     const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
-    return P.scale * fmaf(-dmin, u, d * sq);
+    return X.scale * fmaf(-dmin, um, d * sq);
+}
+
+// Sum each of R per-lane values over the warp.  Halving steps exchange half
+// of the values with the partner lane (xor 1, 2, ...), so after log2(R)
+// steps each lane holds one row; the remaining steps are a plain butterfly.
+// Lane l ends with the total of row lane_row<R>(l) (every lane of a group of
+// R consecutive lanes holds a different row).
+template <int R>
+__device__ __forceinline__ float warp_rows_sum(float (&v)[R], int lane) {
+    if constexpr (R == 1) {
+        float a = v[0];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        return a;
+    } else if constexpr (R == 2) {
+        const bool b = lane & 1;
+        float a = (b ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, b ? v[0] : v[1], 1);
+#pragma unroll
+        for (int o = 2; o < 32; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        return a;
+    } else {  // R == 4
+        const bool b0 = lane & 1, b1 = lane & 2;
+        // step 1: keep rows {2*b0, 2*b0+1}
+        const float k0 = (b0 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, b0 ? v[0] : v[2], 1);
+        const float k1 = (b0 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, b0 ? v[1] : v[3], 1);
+        // step 2: keep row 2*b0 + b1
+        float a = (b1 ? k1 : k0) + __shfl_xor_sync(0xffffffffu, b1 ? k0 : k1, 2);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        return a;
+    }
+}
+
+template <int R>
+__device__ __forceinline__ int lane_row(int lane) {
+    if constexpr (R == 4) return 2 * (lane & 1) + ((lane >> 1) & 1);
+    else if constexpr (R == 2) return lane & 1;
+    else return 0;
+}
+
+// matrix holding chunk c, its first row and its row count in the chunk
+__device__ __forceinline__ int chunk_matrix(const GemvBatch& B, int c) {
+    int p = 0;
+    while (p + 1 < B.P && c >= B.first_chunk[p + 1]) ++p;
+    return p;
 }
 
 template <int RPW>
-__global__ void __launch_bounds__(512, 1)
-gemv_q4k_dp4a(const uint8_t* __restrict__ W, int64_t stride, int N, int nsb, int WK, int WR,
-              const float* __restrict__ x, float* __restrict__ y) {
+__global__ void __launch_bounds__(kMaxThreads, 1)
+gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int WK, int WR,
+              int RC, const float* __restrict__ x) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int RC = RPW * WR;                   // rows per chunk
+    // RC rows per chunk (<= RPW * WR, chosen by the host to balance CTAs);
+    // stages and partial slots are sized for RPW * WR rows
+    const int RM = RPW * WR;
     const int NCW = WK * WR;                   // consumer warps
-    const int stage_bytes = RC * (int)stride;  // multiple of 16
+    const int stage_bytes = RM * (int)stride;  // multiple of 16
     uint8_t* stg = smem;
-    float* red = reinterpret_cast<float*>(smem + kStages * stage_bytes);  // [S][WK][RC]
+    uint32_t* planes = reinterpret_cast<uint32_t*>(smem + kStages * stage_bytes);
+    float* sums = reinterpret_cast<float*>(planes + nsb * 4 * kPlaneWords);
+    float* scales = sums + nsb * 8;
+    float* red = scales + nsb;  // [2 rounds][kStages][WK][RM]
     uint64_t* full = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(red + kStages * WK * RC) + 15) & ~uintptr_t(15));
+        (reinterpret_cast<uintptr_t>(red + 2 * kStages * WK * RM) + 15) & ~uintptr_t(15));
     uint64_t* empty = full + kStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -157,36 +234,51 @@ gemv_q4k_dp4a(const uint8_t* __restrict__ W, int64_t stride, int N, int nsb, int
         mbar_fence_init();
     }
     __syncthreads();
-    const int nchunks = (N + RC - 1) / RC;
+    grid_launch_dependents();
+    const int nchunks = B.first_chunk[B.P];
 
     if (warp == NCW) {
         // ------------------------------------------------ producer warp
+        // (weights do not depend on the preceding kernel: no dependency wait)
         const uint64_t pol = policy_evict_first();
         bool ok = true;
         int it = 0;
         auto reduce = [&](int j) {  // partials of iteration j -> y
-            const int s = j % kStages;
+            const int s = j % kStages, rd = (j / kStages) & 1;
             const int c = blockIdx.x + j * gridDim.x;
-            const int rows = min(RC, N - c * RC);
-            if (lane < rows) {
+            const int p = chunk_matrix(B, c);
+            const int lc = c - B.first_chunk[p];
+            const int rows = min(RC, B.N[p] - lc * RC);
+            for (int row = lane; row < rows; row += 32) {
+                const float* r = red + ((rd * kStages + s) * WK) * RM + row;
                 float v = 0.f;
-                for (int wk = 0; wk < WK; ++wk) v += red[(s * WK + wk) * RC + lane];
-                y[(int64_t)c * RC + lane] = v;
+                for (int wk = 0; wk < WK; ++wk) v += r[wk * RM];
+                B.y[p][(int64_t)lc * RC + row] = v;
             }
+        };
+        auto issue = [&](int c, int s) {
+            if (lane == 0) {
+                const int p = chunk_matrix(B, c);
+                const int lc = c - B.first_chunk[p];
+                const int rows = min(RC, B.N[p] - lc * RC);
+                const uint32_t bytes = (uint32_t)(rows * stride);
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s(stg + s * stage_bytes, B.W[p] + (int64_t)lc * RC * stride, bytes, &full[s],
+                         pol);
+            }
+            __syncwarp();
         };
         for (int c = blockIdx.x; c < nchunks; c += gridDim.x, ++it) {
             const int s = it % kStages;
             if (it >= kStages) {
+                // consumers are done with iteration it - kStages: refill the
+                // stage first, then fold that iteration's partials into y
                 ok = mbar_wait_warp(&empty[s], ((it / kStages) - 1) & 1);
                 if (!ok) break;
+                issue(c, s);
                 reduce(it - kStages);
-            }
-            __syncwarp();
-            if (lane == 0) {
-                const int rows = min(RC, N - c * RC);
-                const uint32_t bytes = (uint32_t)(rows * stride);
-                mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_g2s(stg + s * stage_bytes, W + (int64_t)c * RC * stride, bytes, &full[s], pol);
+            } else {
+                issue(c, s);
             }
         }
         if (ok) {
@@ -203,80 +295,146 @@ gemv_q4k_dp4a(const uint8_t* __restrict__ W, int64_t stride, int N, int nsb, int
     }
 
     // ---------------------------------------------------- consumer warps
+    grid_dependency_wait();  // x may be the preceding kernel's output
+    build_planes(x, nsb, warp, NCW, lane, planes, sums, scales);
+    named_barrier(1, NCW * 32);
+
     const int wr = warp / WK, wk = warp % WK;
     const int qd = lane >> 2, t = lane & 3;
     const int sb = wk * 8 + qd;
     const bool valid = sb < nsb;
-    const bool hi_half = t >= 2;             // sub-blocks 4..7 use the split encoding
+    const uint32_t use_s2 = t >= 2;          // sub-blocks 4..7 use the split encoding
     const int sh0 = 8 * ((2 * t) & 3);       // byte of sub-block 2t within its word
-    XParts P;
-    load_x_parts(x + (int64_t)sb * 256 + 64 * t, valid, P);
+    const uint32_t mask_a = use_s2 ? 0x0F0Fu : 0x3F3Fu;
+    const uint32_t mask_b = use_s2 ? 0x3030u : 0u;
+    LaneX X;
+    if (valid) {
+        const uint4* src = reinterpret_cast<const uint4*>(planes + (sb * 4 + t) * kPlaneWords);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 a = src[i], b = src[4 + i], c = src[8 + i];
+            X.h[4 * i] = a.x; X.h[4 * i + 1] = a.y; X.h[4 * i + 2] = a.z; X.h[4 * i + 3] = a.w;
+            X.m[4 * i] = b.x; X.m[4 * i + 1] = b.y; X.m[4 * i + 2] = b.z; X.m[4 * i + 3] = b.w;
+            X.l[4 * i] = c.x; X.l[4 * i + 1] = c.y; X.l[4 * i + 2] = c.z; X.l[4 * i + 3] = c.w;
+        }
+        X.sum_lo = sums[(sb * 4 + t) * 2];
+        X.sum_hi = sums[(sb * 4 + t) * 2 + 1];
+        X.scale = scales[sb];
+    }
 
+    // Rows past the end of a partial chunk and super-blocks past K are
+    // computed on in-bounds bytes (clamped) and discarded by a select: no
+    // divergent branches in the row loop.
+    const int sb_ld = valid ? sb : nsb - 1;
     int it = 0;
     for (int c = blockIdx.x; c < nchunks; c += gridDim.x, ++it) {
-        const int s = it % kStages;
+        const int s = it % kStages, rd = (it / kStages) & 1;
         if (!mbar_wait_warp(&full[s], (it / kStages) & 1)) break;
-        const int rows = min(RC, N - c * RC);
-        const uint8_t* base = stg + s * stage_bytes + sb * 144;
+        const uint8_t* base = stg + s * stage_bytes + sb_ld * 144 + wr * stride;
         float acc[RPW];
 #pragma unroll
         for (int i = 0; i < RPW; ++i) {
-            const int r = wr + WR * i;
-            acc[i] = (valid && r < rows) ? q4k_row_partial(base + r * stride, t, hi_half, sh0, P)
-                                         : 0.f;
+            const float v = q4k_row_partial(base + (WR * i) * stride, t, use_s2, sh0, mask_a,
+                                            mask_b, X);
+            acc[i] = valid ? v : 0.f;
         }
-#pragma unroll
-        for (int i = 0; i < RPW; ++i)
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-        float mine = 0.f;
-#pragma unroll
-        for (int i = 0; i < RPW; ++i)
-            if (lane == i) mine = acc[i];
-        if (lane < RPW) red[(s * WK + wk) * RC + wr + WR * lane] = mine;
+        // transposed butterfly: after log2(RPW) halving steps lane l holds one
+        // row's partial (row index from its low bits), then a plain reduction
+        float v = warp_rows_sum<RPW>(acc, lane);
+        const int row = lane_row<RPW>(lane);
+        if (lane < RPW) red[((rd * kStages + s) * WK + wk) * RM + wr + WR * row] = v;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
 }
 
 struct Q4kPlan {
-    int WK, WR, RPW, grid, threads;
+    int WK, WR, RPW, RC, grid, threads;
     size_t smem;
 };
 
-bool plan_q4k(int64_t N, int64_t K, int64_t stride, Q4kPlan& p) {
+bool plan_q4k(int64_t Ntot, int64_t K, int64_t stride, Q4kPlan& p) {
     const int nsb = (int)(K / 256);
     p.WK = (nsb + 7) / 8;
     if (p.WK > 15) return false;
-    p.WR = std::max(1, 14 / p.WK);  // ~14 consumer warps + 1 producer <= 512 threads
+    p.WR = std::max(1, (kMaxThreads / 32 - 1) / p.WK);  // consumer warps + 1 producer
     static int sms = 0;
     if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    // rows per chunk: ~32 KB chunks, but small enough that every SM gets two
-    int64_t rc = std::max<int64_t>(1, 32768 / stride);
-    rc = std::min<int64_t>(rc, std::max<int64_t>(p.WR, N / (2 * (int64_t)sms)));
+    // rows per chunk: ~48 KB chunks, but small enough that every SM gets two
+    int64_t rc = std::max<int64_t>(1, 49152 / stride + p.WR / 2);
+    rc = std::min<int64_t>(rc, std::max<int64_t>(p.WR, Ntot / (2 * (int64_t)sms)));
     const int64_t rpw = std::max<int64_t>(1, rc / p.WR);
     p.RPW = rpw >= 4 ? 4 : (rpw >= 2 ? 2 : 1);
-    while (p.RPW > 1 && p.RPW * p.WR > 32) p.RPW /= 2;  // the producer reduces one row per lane
-    if (p.RPW * p.WR > 32) return false;
+    while (p.RPW > 1 && p.RPW * p.WR > 64) p.RPW /= 2;  // the producer reduces <= 2 rows per lane
+    if (p.RPW * p.WR > 64) return false;
     const int RC = p.RPW * p.WR;
     p.threads = (p.WK * p.WR + 1) * 32;
-    p.smem = (size_t)kStages * RC * stride + (size_t)kStages * p.WK * RC * 4 + 16 +
-             2 * kStages * 8;
-    if (p.smem > 220 * 1024 || p.threads > 512) return false;
-    const int64_t nchunks = (N + RC - 1) / RC;
-    p.grid = (int)std::min<int64_t>(nchunks, sms);
+    p.smem = (size_t)kStages * RC * stride                 // weight stages
+             + (size_t)nsb * 4 * kPlaneWords * 4          // activation planes
+             + (size_t)nsb * 9 * 4                         // sums + scales
+             + (size_t)2 * kStages * p.WK * RC * 4         // partials, two rounds
+             + 16 + 2 * kStages * 8;                        // barriers
+    while (p.smem > 220 * 1024 && p.RPW > 1) {             // shrink chunks to fit
+        p.smem -= (size_t)kStages * (p.RPW / 2) * p.WR * stride;
+        p.smem -= (size_t)2 * kStages * p.WK * (p.RPW / 2) * p.WR * 4;
+        p.RPW /= 2;
+    }
+    if (p.smem > 220 * 1024 || p.threads > kMaxThreads) return false;
+    p.RC = p.RPW * p.WR;
     return true;
+}
+
+// Rows per chunk for a batch: the largest RC <= rc_max whose chunk count
+// fills the last round of CTAs best (a small launch otherwise ends with one
+// mostly idle round).
+int balance_rc(int P, const int64_t* N, int rc_max, int sms) {
+    int best = rc_max;
+    double best_eff = 0.0;
+    for (int rc = rc_max; rc >= std::max(1, rc_max / 2); --rc) {
+        int64_t ch = 0;
+        for (int i = 0; i < P; ++i) ch += (N[i] + rc - 1) / rc;
+        const int64_t rounds = (ch + sms - 1) / sms;
+        // useful work / (rounds * rc): rewards full rounds and big chunks
+        int64_t rows = 0;
+        for (int i = 0; i < P; ++i) rows += N[i];
+        const double eff = (double)rows / ((double)rounds * sms * rc);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = rc;
+        }
+    }
+    return best;
 }
 
 }  // namespace
 
-// Fast path for Q4_K, M == 1.  Returns FTC_E_UNSUPPORTED when the shape or
-// alignment does not fit (the caller then uses the general kernels).
-int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
-                  float* y, cudaStream_t st) {
-    if ((uintptr_t)W % 16 || stride % 16 || (uintptr_t)x % 16 || K % 256) return FTC_E_UNSUPPORTED;
+// Fast path for Q4_K, M == 1, over one or more matrices sharing x.  Returns
+// FTC_E_UNSUPPORTED when the shape or alignment does not fit (the caller then
+// uses the general kernels).
+int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y,
+                        int64_t stride, int64_t K, const float* x, cudaStream_t st) {
+    if (P < 1 || P > kGemvMaxMats) return FTC_E_UNSUPPORTED;
+    if (stride % 16 || (uintptr_t)x % 16 || K % 256) return FTC_E_UNSUPPORTED;
+    int64_t ntot = 0;
+    for (int i = 0; i < P; ++i) {
+        if ((uintptr_t)W[i] % 16 || N[i] <= 0 || N[i] > (1 << 30)) return FTC_E_UNSUPPORTED;
+        ntot += N[i];
+    }
     Q4kPlan p;
-    if (!plan_q4k(N, K, stride, p)) return FTC_E_UNSUPPORTED;
+    if (!plan_q4k(ntot, K, stride, p)) return FTC_E_UNSUPPORTED;
+    static int sms = 0;
+    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int RC = balance_rc(P, N, p.RPW * p.WR, sms);
+    GemvBatch B = {};
+    B.P = P;
+    B.first_chunk[0] = 0;
+    for (int i = 0; i < P; ++i) {
+        B.W[i] = W[i];
+        B.y[i] = y[i];
+        B.N[i] = (int)N[i];
+        B.first_chunk[i + 1] = B.first_chunk[i] + (int)((N[i] + RC - 1) / RC);
+    }
+    p.grid = std::min(B.first_chunk[P], sms);
     const int nsb = (int)(K / 256);
     // opt in to large dynamic shared memory once per instantiation
     static bool configured[3] = {false, false, false};
@@ -287,7 +445,18 @@ int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const 
             if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemv_q4k_dp4a)");
             configured[idx] = true;
         }
-        kern<<<p.grid, p.threads, p.smem, st>>>(W, stride, (int)N, nsb, p.WK, p.WR, x, y);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(p.grid);
+        cfg.blockDim = dim3(p.threads);
+        cfg.dynamicSmemBytes = p.smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, B, stride, nsb, p.WK, p.WR, RC, x);
+        if (e != cudaSuccess) return cuda_error(e, "launch gemv_q4k_dp4a");
         return FTC_OK;
     };
     int rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4>, 2)
@@ -296,6 +465,11 @@ int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const 
     if (rc != FTC_OK) return rc;
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;
+}
+
+int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
+                  float* y, cudaStream_t st) {
+    return gemv_q4k_fast_multi(1, &W, &N, &y, stride, K, x, st);
 }
 
 }  // namespace ftc

@@ -36,6 +36,8 @@ SIGNATURES = {
     "ftc_device_status": (C.c_int, [_p, C.POINTER(C.c_int)]),
     "ftc_dequant": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _p]),
     "ftc_mul_mat_vec": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
+    "ftc_mul_mat_vec_multi": (C.c_int, [C.c_int, C.c_int, C.POINTER(_p), C.POINTER(_i64), _i64,
+                                        _i64, _p, _i64, C.POINTER(_p), _p]),
     "ftc_gemm": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, C.c_int, _i64, _p, C.c_int, _p]),
     "ftc_expert_chunk_static": (C.c_int, [C.c_int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                           _i64, _p]),
@@ -119,6 +121,24 @@ def mul_mat_vec(w, dtype, n, k, x, y=None, row_stride=None, stream=None):
     check(lib().ftc_mul_mat_vec(t, w.data_ptr(), n, k, rs, x2.data_ptr(), m, y.data_ptr(),
                                 _stream(stream)), "ftc_mul_mat_vec")
     return y
+
+
+def mul_mat_vec_multi(ws, dtype, ns, k, x, ys=None, row_stride=None, stream=None):
+    """Several GEMVs sharing x in one launch: ys[i] = x @ W_i^T."""
+    import torch
+    t = F.dtype_id(dtype)
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if ys is None:
+        ys = [torch.empty((m, n), dtype=torch.float32, device=x.device) for n in ns]
+    P = len(ws)
+    wa = (_p * P)(*[w.data_ptr() for w in ws])
+    na = (_i64 * P)(*ns)
+    ya = (_p * P)(*[y.data_ptr() for y in ys])
+    rs = row_stride if row_stride is not None else row_bytes(t, k)
+    check(lib().ftc_mul_mat_vec_multi(t, P, wa, na, k, rs, x2.data_ptr(), m, ya, _stream(stream)),
+          "ftc_mul_mat_vec_multi")
+    return ys
 
 
 _TORCH_OUT = {F.F32: "float32", F.BF16: "bfloat16", F.F16: "float16"}
