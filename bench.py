@@ -439,6 +439,24 @@ def run_ncu_probe():
     return 0
 
 
+def run_ncu_gemm_probe():
+    """Three config-3 dequant-GEMM launches (W 33 MB, X 16 MB, Y 58 MB on the
+    device): the small case for ncu captures of the tensor-core kernel."""
+    import torch
+    from xwfes_b200 import ftc
+    dev = torch.device("cuda", 0)
+    n, k, m = 14336, 4096, 2048
+    w = torch.from_numpy(S.weight(F.Q4_K, n, k, seed=0, name=f"p.{n}x{k}")).to(dev)
+    x = torch.from_numpy(S.activations_bf16(m, k, seed=0, name=f"p.{m}")).to(dev).view(
+        torch.bfloat16)
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        ftc.gemm(w, F.Q4_K, n, k, x, y=y, y_dtype=F.BF16)
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": "gemm_q4k_tc 14336x4096 M=2048 x3", "status": ftc.device_status()}))
+    return 0
+
+
 # ----------------------------------------------------------- CPU baselines
 
 def cpu_sample(threads, budget_s=10.0):
@@ -544,7 +562,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: a few launches of the dominant kernel "
-                         "(gate-shaped Q4_K GEMV) on one layer copy, no timing")
+                         "(grouped gate+up Q4_K GEMV) on one layer copy, no timing")
+    ap.add_argument("--ncu-gemm", action="store_true",
+                    help="profiling mode: three launches of the config-3 dequant-GEMM "
+                         "(14336x4096, M=2048, bf16), no timing")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -554,6 +575,8 @@ def main():
 
     if args.ncu:
         return run_ncu_probe()
+    if args.ncu_gemm:
+        return run_ncu_gemm_probe()
 
     if args.impl == "reference":
         if rank != 0:

@@ -1,0 +1,161 @@
+// test_cuda_backend.cpp -- ft::CudaBackend (the C++ IBackend drop-in) on a
+// B200, in the style of the reference's own test binary
+// (ft/src/tests/test_core.cpp: CHECK macro, failure count, exit status).
+// Checked against the CPU oracle (oracle/ftoracle.c, linked as a checker).
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+#include <vector>
+
+#include "cuda_backend.h"
+#include "ftoracle.h"
+
+using namespace ft;
+
+static int g_fails = 0;
+
+#define CHECK(cond, msg)                                     \
+    do {                                                     \
+        if (!(cond)) {                                       \
+            std::printf("FAIL %d: %s\n", __LINE__, msg);     \
+            ++g_fails;                                       \
+        }                                                    \
+    } while (0)
+
+static uint32_t g_lcg = 123456789u;
+static uint32_t next_u32() {
+    g_lcg = g_lcg * 1664525u + 1013904223u;
+    return g_lcg;
+}
+static float rnd() { return ((float)((next_u32() >> 9) & 0x7FFF) / 32768.f) * 2.f - 1.f; }
+
+// Random blocks with sane fp16 scales for the formats under test.
+static std::vector<uint8_t> random_blocks(DType t, int64_t rows, int64_t cols) {
+    const size_t rb = dtype_row_bytes(t, cols);
+    std::vector<uint8_t> b(rb * (size_t)rows);
+    for (auto& v : b) v = (uint8_t)(next_u32() >> 24);
+    const size_t bb = dtype_bytes_per_block(t);
+    const size_t nblk = b.size() / bb;
+    for (size_t i = 0; i < nblk; ++i) {
+        uint8_t* p = b.data() + i * bb;
+        const uint16_t d = ftor_float_to_half(0.01f + 0.01f * std::fabs(rnd()));
+        if (t == DType::Q8_0) std::memcpy(p, &d, 2);
+        if (t == DType::Q4_K) { std::memcpy(p, &d, 2); std::memcpy(p + 2, &d, 2); }
+        if (t == DType::Q6_K) std::memcpy(p + 208, &d, 2);
+    }
+    return b;
+}
+
+static HostTensor view(const std::vector<uint8_t>& b, DType t, int64_t cols, int64_t rows) {
+    HostTensor h;
+    h.name = "w";
+    h.ne[0] = cols;
+    h.ne[1] = rows;
+    h.n_dims = 2;
+    h.dtype = t;
+    h.data = b.data();
+    h.nbytes = b.size();
+    return h;
+}
+
+// max |a-b| / (|b| + 1e-2 * rms(b))
+static double rel_err(const std::vector<float>& a, const std::vector<float>& b) {
+    double ss = 0;
+    for (float v : b) ss += (double)v * v;
+    const double rms = std::sqrt(ss / (double)b.size());
+    double m = 0;
+    for (size_t i = 0; i < b.size(); ++i)
+        m = std::fmax(m, std::fabs((double)a[i] - b[i]) / (std::fabs((double)b[i]) + 1e-2 * rms));
+    return m;
+}
+
+static void test_matmul(CudaBackend& be, DType t, int64_t N, int64_t K, int64_t M) {
+    auto w = random_blocks(t, N, K);
+    HostTensor W = view(w, t, K, N);
+    std::vector<float> x((size_t)(M * K));
+    for (auto& v : x) v = rnd();
+    std::vector<float> y((size_t)(M * N), NAN), ref((size_t)(M * N));
+    be.matmul(x.data(), M, K, W, y.data());
+    ftor_matmul(x.data(), M, K, w.data(), (int)t, N, (int64_t)W.row_stride_bytes(), ref.data(), 8);
+    char msg[96];
+    std::snprintf(msg, sizeof msg, "matmul dtype %u N %lld K %lld M %lld", (unsigned)t,
+                  (long long)N, (long long)K, (long long)M);
+    CHECK(rel_err(y, ref) <= 2e-3, msg);
+}
+
+// The reference chunker test's shapes (ft/src/tests/test_core.cpp:307-346):
+// F32 K=16, FF=48, M=3 in windows of 8, accumulated window by window.
+static void test_expert_chunk_windows(CudaBackend& be) {
+    const int64_t K = 16, FF = 48, M = 3, C = 8;
+    std::vector<float> gate((size_t)(K * FF)), up((size_t)(K * FF)), down((size_t)(K * FF));
+    for (auto& v : gate) v = rnd() * 0.5f;
+    for (auto& v : up) v = rnd() * 0.5f;
+    for (auto& v : down) v = rnd() * 0.5f;
+    std::vector<float> x((size_t)(M * K));
+    for (auto& v : x) v = rnd();
+    std::vector<float> out((size_t)(M * K), 0.f), ref((size_t)(M * K), 0.f);
+    const size_t stride = (size_t)K * 4;
+    for (int64_t i0 = 0; i0 < FF; i0 += C) {
+        ExpertChunkJob job;
+        job.x = x.data();
+        job.out = out.data();
+        job.gate = gate.data() + i0 * K;
+        job.up = up.data() + i0 * K;
+        job.down = down.data() + i0 * K;
+        job.dt = DType::F32;
+        job.M = M;
+        job.K = K;
+        job.IC = C;
+        job.gate_up_row_stride = stride;
+        job.down_row_stride = stride;
+        be.run_expert_chunk(job);
+        ftor_expert_chunk(x.data(), ref.data(), (const uint8_t*)(gate.data() + i0 * K),
+                          (const uint8_t*)(up.data() + i0 * K), (const uint8_t*)(down.data() + i0 * K),
+                          FTOR_F32, M, K, C, (int64_t)stride, (int64_t)stride, 1);
+    }
+    double maxerr = 0;
+    for (size_t j = 0; j < ref.size(); ++j)
+        maxerr = std::fmax(maxerr, std::fabs(ref[j] - out[j]) / (std::fabs(ref[j]) + 1e-3));
+    CHECK(maxerr < 1e-4, "chunked expert equivalence (reference test bound)");
+}
+
+static void test_upload_and_errors(CudaBackend& be) {
+    auto w = random_blocks(DType::Q4_K, 256, 4096);
+    HostTensor W = view(w, DType::Q4_K, 4096, 256);
+    be.upload(W);
+    std::vector<float> x(4096, 0.25f), y(256);
+    be.matmul(x.data(), 1, 4096, W, y.data());
+    bool threw = false;
+    try {
+        be.matmul(x.data(), 1, 2048, W, y.data());  // K does not match W
+    } catch (const std::runtime_error&) {
+        threw = true;
+    }
+    CHECK(threw, "mismatched K throws std::runtime_error");
+    be.sync();
+}
+
+int main() {
+    try {
+        CudaBackend be(0);
+        CHECK(be.ready(), "backend ready");
+        CHECK(be.info().mem_bytes > (100ull << 30), "device memory reported");
+        CHECK(be.alloc_staging(1 << 20) == nullptr, "no staging buffers");
+        test_matmul(be, DType::Q4_K, 512, 4096, 1);
+        test_matmul(be, DType::Q4_K, 1024, 14336, 3);
+        test_matmul(be, DType::Q8_0, 256, 4096, 1);
+        test_matmul(be, DType::Q6_K, 300, 4096, 2);
+        test_expert_chunk_windows(be);
+        test_upload_and_errors(be);
+    } catch (const std::exception& e) {
+        std::printf("FAIL exception: %s\n", e.what());
+        ++g_fails;
+    }
+    if (g_fails) {
+        std::printf("%d checks FAILED\n", g_fails);
+        return 1;
+    }
+    std::printf("all tests passed\n");
+    return 0;
+}

@@ -1,0 +1,40 @@
+"""The C++ ft::IBackend adapter (xwfes_b200/host/cuda_backend.cpp): it must
+compile against the interface header (CPU, no GPU needed) and pass the C++
+test binary tests/cpp/test_cuda_backend.cpp on a B200."""
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HOST = os.path.join(ROOT, "xwfes_b200", "host")
+
+
+def compile_test(out):
+    from oracle import oracle as O
+    from xwfes_b200 import build, ftc
+    if not os.path.exists(ftc.LIB_PATH):
+        build.build()
+    O.lib()  # builds oracle/liboracle.so if needed
+    cmd = ["g++", "-std=c++17", "-O2", "-I", os.path.join(HOST, "compat"), "-I", HOST,
+           "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "oracle"),
+           os.path.join(ROOT, "tests", "cpp", "test_cuda_backend.cpp"),
+           os.path.join(HOST, "cuda_backend.cpp"),
+           "-L", os.path.dirname(ftc.LIB_PATH), "-lftcuda",
+           "-L", os.path.join(ROOT, "oracle"), "-loracle",
+           "-Wl,-rpath," + os.path.dirname(ftc.LIB_PATH) + ":" + os.path.join(ROOT, "oracle"),
+           "-o", out]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return out
+
+
+def test_adapter_compiles(tmp_path):
+    assert os.path.exists(compile_test(str(tmp_path / "test_cuda_backend")))
+
+
+@pytest.mark.gpu
+def test_adapter_passes_on_gpu(tmp_path):
+    exe = compile_test(str(tmp_path / "test_cuda_backend"))
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "all tests passed" in r.stdout, r.stdout + r.stderr

@@ -1,9 +1,10 @@
 """GPU parity of the tcgen05 prefill dequant-GEMM (ftc_gemm).
 
 Exactness first: with one-hot activation rows, y[m][n] is a single product
-1.0 * w16[n][k_m] accumulated in fp32, so it must equal the dequantized weight
-rounded once to the operand type -- this pins the on-chip dequant, the
-128-byte swizzled operand layout and the token/row mapping bit for bit.
+1.0 * w16[n][k_m] accumulated in fp32, so it must equal the 16-bit operand the
+on-chip dequant produces (q4k_operand16 restates its arithmetic) -- this pins
+the dequant, the 128-byte swizzled operand layout and the token/row mapping
+bit for bit.
 
 Float tolerance: the GEMM multiplies 16-bit operands (activations as given,
 weights rounded to the same 16-bit type) with fp32 accumulation.
@@ -56,12 +57,50 @@ def to16(a32, t):
     return torch.from_numpy(np.ascontiguousarray(a32, dtype=np.float32)).to(TDT[t])
 
 
+def q4k_operand16(w, n, k, xt):
+    """The 16-bit weights the tensor-core path multiplies, emulated exactly.
+    fp16 operands: w16 = fp16(q * fp16(d*sc) - fp16(dmin*m)), one rounding of
+    the fused multiply-add (q*DL - ML is exact in float64).  bf16 operands:
+    bf16 of the fp32 dequantized weight (d*sc*q exact, the subtraction
+    rounded once), i.e. the reference's dequant_row value rounded once."""
+    blk = np.ascontiguousarray(w).reshape(n, k // 256, 144)
+    d = blk[:, :, 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
+    dmin = blk[:, :, 2:4].copy().view(np.float16)[..., 0].astype(np.float32)
+    sp = blk[:, :, 4:16].astype(np.int32)
+    sc = np.empty((n, k // 256, 8), np.int32)
+    mn = np.empty_like(sc)
+    sc[..., :4] = sp[..., 0:4] & 63
+    mn[..., :4] = sp[..., 4:8] & 63
+    sc[..., 4:] = (sp[..., 8:12] & 15) | ((sp[..., 0:4] >> 6) << 4)
+    mn[..., 4:] = (sp[..., 8:12] >> 4) | ((sp[..., 4:8] >> 6) << 4)
+    DL = (d[..., None] * sc.astype(np.float32)).astype(np.float16).astype(np.float64)
+    ML = (dmin[..., None] * mn.astype(np.float32)).astype(np.float16).astype(np.float64)
+    qs = blk[:, :, 16:].astype(np.int64)
+    q = np.empty((n, k // 256, 256), np.int64)
+    for g in range(4):
+        q[:, :, 64 * g:64 * g + 32] = qs[:, :, 32 * g:32 * g + 32] & 15
+        q[:, :, 64 * g + 32:64 * g + 64] = qs[:, :, 32 * g:32 * g + 32] >> 4
+    sub = np.arange(256) // 32
+    if xt == F.BF16:
+        dl = (d[..., None] * sc.astype(np.float32)).astype(np.float32)
+        ml = (dmin[..., None] * mn.astype(np.float32)).astype(np.float32)
+        w32 = (q.astype(np.float32) * dl[:, :, sub] - ml[:, :, sub]).astype(np.float32)
+        return S.bf16_bits_to_f32(S.f32_to_bf16_bits(w32)).reshape(n, k)
+    w16 = (q * DL[:, :, sub] - ML[:, :, sub]).astype(np.float16).astype(np.float32)
+    return w16.reshape(n, k)
+
+
 @pytest.mark.parametrize("xt", [F.F16, F.BF16])
 @pytest.mark.parametrize("m,n,k", [(128, 256, 1024), (256, 384, 512), (200, 130, 256)])
 def test_gemm_one_hot_exact(ftc, oracle, xt, m, n, k):
     w = S.weight(F.Q4_K, n, k, seed=2, name="gemm.onehot")
+    w16 = q4k_operand16(w, n, k, xt)
+    # the operand is the exact dequantized weight to within one 16-bit ulp of
+    # the largest weight (d*sc and dmin*m are rounded to fp16 before the
+    # multiply-add, so cancelling weights carry that scale's rounding)
     deq = oracle.dequant_rows(w, F.Q4_K, k)
-    w16 = to16(deq, xt).float().numpy()            # one rounding to the operand type
+    ulp = 2.0 ** (-10 if xt == F.F16 else -7)
+    assert np.max(np.abs(w16 - deq)) <= ulp * np.abs(deq).max()
     ks = (np.arange(m) * 37 + 11) % k
     x = np.zeros((m, k), dtype=np.float32)
     x[np.arange(m), ks] = 1.0
@@ -72,13 +111,13 @@ def test_gemm_one_hot_exact(ftc, oracle, xt, m, n, k):
     assert np.array_equal(got, w16[:, ks].T)
 
 
-def _torch_ref(ftc, wd, n, k, x16):
-    """fp32 reference on the same 16-bit operands: dequantized weights
-    (bit-exact kernel, verified against the oracle) rounded to x's type."""
-    deq = ftc.dequant(wd, F.Q4_K, n, k)
+def _torch_ref(ftc, w, n, k, x16):
+    """fp32 reference on the same 16-bit operands the kernel multiplies."""
+    xt = F.F16 if x16.dtype == torch.float16 else F.BF16
+    w16 = torch.from_numpy(q4k_operand16(w, n, k, xt)).to(x16.device)
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
-    ref = x16.float() @ deq.to(x16.dtype).float().T
+    ref = x16.float() @ w16.T
     torch.backends.cuda.matmul.allow_tf32 = prev
     return ref
 
@@ -91,7 +130,7 @@ def test_gemm_random_vs_oracle(ftc, oracle, xt, m, n, k):
     x16 = to16(xb, xt)
     wd = torch.from_numpy(w).cuda()
     y = ftc.gemm(wd, F.Q4_K, n, k, x16.cuda(), y_dtype=F.F32)
-    ref16 = _torch_ref(ftc, wd, n, k, x16.cuda())
+    ref16 = _torch_ref(ftc, w, n, k, x16.cuda())
     torch.cuda.synchronize()
     assert ftc.device_status() == 0
     got = y.cpu().numpy()
@@ -113,7 +152,7 @@ def test_gemm_config3(ftc, oracle, n, k, m):
         torch.bfloat16)
     y = ftc.gemm(wd, F.Q4_K, n, k, x16, y_dtype=F.BF16)
     y32 = ftc.gemm(wd, F.Q4_K, n, k, x16, y_dtype=F.F32)
-    ref = _torch_ref(ftc, wd, n, k, x16)
+    ref = _torch_ref(ftc, w, n, k, x16)
     torch.cuda.synchronize()
     assert ftc.device_status() == 0
     # fp32 output against the same-operand fp32 reference

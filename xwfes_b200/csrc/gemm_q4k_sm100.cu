@@ -9,10 +9,11 @@
 // dequantized on the SM into shared memory right before the tensor cores
 // read it, so no dequantized copy of W ever exists in global memory.
 //
-// One persistent CTA per SM, warp-specialized (14 warps):
-//   warp 0      TMA: raw Q4_K tile (128 rows x one 144-byte super-block) into a
-//               2-slot ring; activation tiles (BN tokens x 64 k, 128-byte
-//               swizzle) into the NS-slot A/B ring.  Also owns TMEM.
+// One persistent CTA per SM, warp-specialized (15 warps):
+//   warp 0      TMA: activation tiles (BN tokens x 64 k, 128-byte swizzle)
+//               into the NB-slot B ring.  Also owns TMEM.
+//   warp 14     TMA: raw Q4_K tiles (128 rows x one 144-byte super-block)
+//               into a 3-slot ring, independently of the B ring.
 //   warp 1      one thread issues tcgen05.mma 128 x BN x 16 (A = weights,
 //               B = tokens, both K-major from shared memory) into a TMEM
 //               accumulator (two of them, so the epilogue of tile i overlaps
@@ -20,9 +21,10 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, convert, store
 //               Y[token][row] (a warp writes 32 consecutive n per token).
 //   warps 6-13  dequant: thread (row r, half h) decodes 32 weights of one
-//               64-wide k-step (codes of group g, both nibbles) with the
-//               block's scale/min into the 16-bit operand type and writes
-//               them in the 128-byte-swizzled K-major layout the MMA reads.
+//               64-wide k-step (codes of group g, both nibbles) -- packed fp16
+//               arithmetic for fp16 operands, fp32 with one rounding for bf16
+//               (see dequant_pairs) -- and writes them in the 128-byte-
+//               swizzled K-major layout the MMA reads.
 // Every pipeline wait is bounded in time (sm100.cuh); a kernel that gives up
 // records a status and returns.
 #include <cuda.h>
@@ -45,25 +47,30 @@ namespace {
 
 constexpr int BM = 128;       // weight rows per tile (MMA M)
 constexpr int BK = 64;        // k per stage: one 128-byte swizzle row of 16-bit values
-constexpr int kRawSlots = 2;  // raw super-block ring
+constexpr int kRawSlots = 3;  // raw super-block ring (12 k-steps of lookahead)
 constexpr int kRawBytes = BM * 144;
-constexpr int kThreads = 14 * 32;
+constexpr int kThreads = 15 * 32;
+constexpr int kRawWarp = 14;  // issues the raw weight tiles
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 4;
 
 template <int BN>
 struct Cfg {
-    static constexpr int NS = BN == 256 ? 3 : 4;  // A/B stages
+    // Separate rings: activation tiles come from L2/HBM by TMA and need deep
+    // lookahead; dequantized weight tiles are made on chip and need two.
+    static constexpr int NA = 3;                  // dequantized weight stages
+    static constexpr int NB = BN == 256 ? 3 : 5;  // activation stages
     static constexpr int A_BYTES = BM * BK * 2;   // 16 KB
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int TMEM_COLS = 2 * BN;      // two accumulators
     // shared layout (all tiles 1024-byte aligned)
     static constexpr int OFF_A = 0;
-    static constexpr int OFF_B = OFF_A + NS * A_BYTES;
-    static constexpr int OFF_RAW = OFF_B + NS * B_BYTES;
+    static constexpr int OFF_B = OFF_A + NA * A_BYTES;
+    static constexpr int OFF_RAW = OFF_B + NB * B_BYTES;
     static constexpr int OFF_BAR = OFF_RAW + kRawSlots * kRawBytes;
-    // barriers: a_full[NS] b_full[NS] ab_empty[NS] raw_full[2] raw_empty[2] acc_full[2] acc_empty[2]
-    static constexpr int N_BARS = 3 * NS + 8;
+    // barriers: a_full[NA] a_empty[NA] b_full[NB] b_empty[NB] raw_full[R]
+    // raw_empty[R] acc_full[2] acc_empty[2]
+    static constexpr int N_BARS = 2 * NA + 2 * NB + 2 * kRawSlots + 4;
     static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 16 + 1024;  // +1024: base alignment slack
 };
 
@@ -78,6 +85,115 @@ template <>
 __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Scale and min of all 8 sub-blocks of a Q4_K super-block header (d, dmin,
+// 12 packed bytes): fdl[j] = d*sc_j and fnml[j] = -dmin*m_j in fp32 (exact),
+// and for fp16 operands also as fp16 pairs dl2[j] / nml2[j] (one rounding).
+template <typename OP>
+__device__ __forceinline__ void decode_scales(const uint4 hd, float (&fdl)[8], float (&fnml)[8],
+                                              uint32_t (&dl2)[8], uint32_t (&nml2)[8]) {
+    const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        int sc, mn;
+        q4k_scale_min(hd.y, hd.z, hd.w, j, sc, mn);
+        fdl[j] = d * (float)sc;
+        fnml[j] = -(dmin * (float)mn);
+        if constexpr (std::is_same<OP, __half>::value) {
+            const __half2 a = __float2half2_rn(fdl[j]);
+            const __half2 b = __float2half2_rn(fnml[j]);
+            dl2[j] = *reinterpret_cast<const uint32_t*>(&a);
+            nml2[j] = *reinterpret_cast<const uint32_t*>(&b);
+        } else {
+            dl2[j] = nml2[j] = 0;
+        }
+    }
+}
+
+// packed fp32x2 arithmetic (two floats in one 64-bit register, low = first)
+__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
+    return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// (lo, hi) floats -> bf16x2 (round to nearest even), lo in the low half
+__device__ __forceinline__ uint32_t bf2_of(uint64_t v) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float((uint32_t)v),
+                                                   __uint_as_float((uint32_t)(v >> 32)));
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+    const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a),
+                              *reinterpret_cast<const __half2*>(&b),
+                              *reinterpret_cast<const __half2*>(&c));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a),
+                              *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+
+// Eight weights of one code word: byte i holds q_lo (k = 4u + i of the low
+// sub-block) and q_hi (same k of the high sub-block).
+//  fp16 operands: each pair of neighbouring bytes becomes half2(1024 + q0,
+//    1024 + q1) by placing the nibbles in the mantissa of 0x6400 (1024.0);
+//    subtracting 1024 is exact, and one fused multiply-add gives
+//    fp16(q * fp16(d*sc) - fp16(dmin*m)) with a single rounding.
+//  bf16 operands: w = (d*sc)*q - dmin*m in fp32 (the product is exact, the
+//    subtraction rounds once, as the reference's dequant_row) and one
+//    rounding to bf16 -- bf16's coarser grid leaves no room for the fp16
+//    rounding of the scales.
+template <typename OP>
+__device__ __forceinline__ void dequant_pairs(uint32_t w, uint32_t dl_lo, uint32_t nml_lo,
+                                              uint32_t dl_hi, uint32_t nml_hi, float fdl_lo,
+                                              float fml_lo, float fdl_hi, float fml_hi,
+                                              uint32_t& lo01, uint32_t& lo23, uint32_t& hi01,
+                                              uint32_t& hi23) {
+    if constexpr (std::is_same<OP, __half>::value) {
+        constexpr uint32_t kMagic = 0x64006400u;
+        const uint32_t p01 = __byte_perm(w, 0, 0x4140);  // byte1 << 16 | byte0
+        const uint32_t p23 = __byte_perm(w, 0, 0x4342);  // byte3 << 16 | byte2
+        const uint32_t q_lo01 = hsub2_u((p01 & 0x000F000Fu) | kMagic, kMagic);
+        const uint32_t q_lo23 = hsub2_u((p23 & 0x000F000Fu) | kMagic, kMagic);
+        const uint32_t q_hi01 = hsub2_u(((p01 >> 4) & 0x000F000Fu) | kMagic, kMagic);
+        const uint32_t q_hi23 = hsub2_u(((p23 >> 4) & 0x000F000Fu) | kMagic, kMagic);
+        lo01 = hfma2_u(q_lo01, dl_lo, nml_lo);
+        lo23 = hfma2_u(q_lo23, dl_lo, nml_lo);
+        hi01 = hfma2_u(q_hi01, dl_hi, nml_hi);
+        hi23 = hfma2_u(q_hi23, dl_hi, nml_hi);
+    } else {
+        // q -> float via the 2^23 magic (exact), then packed fp32x2 FMAs:
+        // fp32(q*dl - ml) with the product exact, one rounding, then bf16.
+        const uint32_t lo4 = w & 0x0F0F0F0Fu, hi4 = (w >> 4) & 0x0F0F0F0Fu;
+        auto fpair = [](uint32_t nib4, uint32_t sel_lo, uint32_t sel_hi) {
+            // 0x4B0000qq = 2^23 + q for the selected bytes
+            return (uint64_t)__byte_perm(nib4, 0x4B000000u, sel_lo) |
+                   ((uint64_t)__byte_perm(nib4, 0x4B000000u, sel_hi) << 32);
+        };
+        const uint64_t m23 = 0xCB000000CB000000ull;  // (-2^23, -2^23)
+        const uint64_t dll = pack_f2(fdl_lo, fdl_lo), mll = pack_f2(fml_lo, fml_lo);
+        const uint64_t dlh = pack_f2(fdl_hi, fdl_hi), mlh = pack_f2(fml_hi, fml_hi);
+        lo01 = bf2_of(fma_f2(add_f2(fpair(lo4, 0x7440, 0x7441), m23), dll, mll));
+        lo23 = bf2_of(fma_f2(add_f2(fpair(lo4, 0x7442, 0x7443), m23), dll, mll));
+        hi01 = bf2_of(fma_f2(add_f2(fpair(hi4, 0x7440, 0x7441), m23), dlh, mlh));
+        hi23 = bf2_of(fma_f2(add_f2(fpair(hi4, 0x7442, 0x7443), m23), dlh, mlh));
+    }
 }
 
 // y element store in the requested output type
@@ -100,25 +216,31 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     uint8_t* sRaw = smem + C::OFF_RAW;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* a_full = bars;
-    uint64_t* b_full = bars + C::NS;
-    uint64_t* ab_empty = bars + 2 * C::NS;
-    uint64_t* raw_full = bars + 3 * C::NS;
-    uint64_t* raw_empty = raw_full + 2;
-    uint64_t* acc_full = raw_full + 4;
-    uint64_t* acc_empty = raw_full + 6;
+    uint64_t* a_empty = a_full + C::NA;
+    uint64_t* b_full = a_empty + C::NA;
+    uint64_t* b_empty = b_full + C::NB;
+    uint64_t* raw_full = b_empty + C::NB;
+    uint64_t* raw_empty = raw_full + kRawSlots;
+    uint64_t* acc_full = raw_empty + kRawSlots;
+    uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::N_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::NS; ++s) {
+        for (int s = 0; s < C::NA; ++s) {
             mbar_init(&a_full[s], kDequantWarps);
-            mbar_init(&b_full[s], 1);
-            mbar_init(&ab_empty[s], 1);
+            mbar_init(&a_empty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < C::NB; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (int s = 0; s < kRawSlots; ++s) {
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_empty[s], kDequantWarps);
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
             mbar_init(&acc_empty[s], kEpiWarps);
         }
@@ -144,31 +266,41 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         if (lane == 0) {
             prefetch_tensormap(&tm_w);
             prefetch_tensormap(&tm_x);
-            const uint64_t pol_w = policy_evict_last();  // weights are re-read per token tile
             const uint64_t pol_x = policy_evict_last();
-            uint32_t kc = 0, rc = 0;
+            uint32_t kc = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-                const int nt = tile % n_tiles, tt = tile / n_tiles;
+                const int tt = tile / n_tiles;
+                for (int ks = 0; ks < nsb * 4; ++ks) {
+                    const int s = kc % C::NB;
+                    if (!mbar_wait(&b_empty[s], ((kc / C::NB) & 1) ^ 1)) { *abort_flag = 1; break; }
+                    mbar_arrive_expect_tx(&b_full[s], C::B_BYTES);
+                    tma_load_2d(sB + s * C::B_BYTES, &tm_x, ks * BK, tt * BN, &b_full[s], pol_x);
+                    ++kc;
+                }
+            }
+            if (*abort_flag) {  // let issued copies land before the CTA leaves
+                for (uint32_t j = kc > (uint32_t)C::NB ? kc - C::NB : 0; j < kc; ++j)
+                    mbar_wait(&b_full[j % C::NB], (j / C::NB) & 1);
+            }
+        }
+    } else if (warp == kRawWarp) {
+        // ------------------------------------------------------ raw TMA
+        // Raw weight tiles run up to kRawSlots super-blocks ahead of the
+        // dequant warps, independent of the activation ring.
+        if (lane == 0) {
+            const uint64_t pol_w = policy_evict_last();  // weights are re-read per token tile
+            uint32_t rc = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+                const int nt = tile % n_tiles;
                 for (int sb = 0; sb < nsb; ++sb) {
                     const int rs = rc % kRawSlots;
                     if (!mbar_wait(&raw_empty[rs], ((rc / kRawSlots) & 1) ^ 1)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
                     tma_load_2d(sRaw + rs * kRawBytes, &tm_w, sb * 144, nt * BM, &raw_full[rs], pol_w);
                     ++rc;
-                    for (int g = 0; g < 4; ++g) {
-                        const int s = kc % C::NS;
-                        if (!mbar_wait(&ab_empty[s], ((kc / C::NS) & 1) ^ 1)) { *abort_flag = 1; break; }
-                        mbar_arrive_expect_tx(&b_full[s], C::B_BYTES);
-                        tma_load_2d(sB + s * C::B_BYTES, &tm_x, (sb * 4 + g) * BK, tt * BN, &b_full[s],
-                                    pol_x);
-                        ++kc;
-                    }
-                    if (*abort_flag) break;
                 }
             }
-            if (*abort_flag) {  // let issued copies land before the CTA leaves
-                for (uint32_t j = kc > (uint32_t)C::NS ? kc - C::NS : 0; j < kc; ++j)
-                    mbar_wait(&b_full[j % C::NS], (j / C::NS) & 1);
+            if (*abort_flag) {
                 for (uint32_t j = rc > (uint32_t)kRawSlots ? rc - kRawSlots : 0; j < rc; ++j)
                     mbar_wait(&raw_full[j % kRawSlots], (j / kRawSlots) & 1);
             }
@@ -186,26 +318,27 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
                 for (int ks = 0; ks < nsb * 4; ++ks) {
-                    const int s = kc % C::NS;
-                    const uint32_t par = (kc / C::NS) & 1;
-                    if (!mbar_wait(&a_full[s], par) || !mbar_wait(&b_full[s], par)) {
+                    const int sa = kc % C::NA, s = kc % C::NB;
+                    if (!mbar_wait(&a_full[sa], (kc / C::NA) & 1) ||
+                        !mbar_wait(&b_full[s], (kc / C::NB) & 1)) {
                         *abort_flag = 1;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t da = smem_desc_k_sw128(sA + s * C::A_BYTES);
+                    const uint64_t da = smem_desc_k_sw128(sA + sa * C::A_BYTES);
                     const uint64_t db = smem_desc_k_sw128(sB + s * C::B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes along k per MMA
                         umma_f16_ss(d_tmem, da + 2 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
-                    umma_commit(&ab_empty[s]);
+                    umma_commit(&a_empty[sa]);
+                    umma_commit(&b_empty[s]);
                     ++kc;
                 }
                 if (*abort_flag) break;
                 umma_commit(&acc_full[b]);
             }
             // wait for the last MMAs to retire before TMEM can be released
-            if (kc > 0) mbar_wait(&ab_empty[(kc - 1) % C::NS], ((kc - 1) / C::NS) & 1);
+            if (kc > 0) mbar_wait(&b_empty[(kc - 1) % C::NB], ((kc - 1) / C::NB) & 1);
         }
     } else if (warp < 2 + kEpiWarps) {
         // ---------------------------------------------------------- epilogue
@@ -246,30 +379,22 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 const int rs = rc % kRawSlots;
                 if (!mbar_wait_warp(&raw_full[rs], (rc / kRawSlots) & 1)) { *abort_flag = 1; break; }
                 const uint8_t* blk = sRaw + rs * kRawBytes + r * 144;
-                const uint4 hd = *reinterpret_cast<const uint4*>(blk);
-                const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
+                float fdl[8], fnml[8];      // per sub-block: d*sc, -dmin*m
+                uint32_t dl2[8], nml2[8];   // the same as fp16 pairs (fp16 operands)
+                decode_scales<OP>(*reinterpret_cast<const uint4*>(blk), fdl, fnml, dl2, nml2);
+#pragma unroll
                 for (int g = 0; g < 4; ++g) {
-                    const int s = kc % C::NS;
-                    if (!mbar_wait_warp(&ab_empty[s], ((kc / C::NS) & 1) ^ 1)) { *abort_flag = 1; break; }
-                    int sc0, mn0, sc1, mn1;
-                    q4k_scale_min(hd.y, hd.z, hd.w, 2 * g, sc0, mn0);
-                    q4k_scale_min(hd.y, hd.z, hd.w, 2 * g + 1, sc1, mn1);
-                    const float dl = d * (float)sc0, ml = dmin * (float)mn0;
-                    const float dh = d * (float)sc1, mh = dmin * (float)mn1;
+                    const int s = kc % C::NA;
+                    if (!mbar_wait_warp(&a_empty[s], ((kc / C::NA) & 1) ^ 1)) { *abort_flag = 1; break; }
                     const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g + 16 * h);
                     const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-                    uint32_t lo[8], hi[8];  // packed 16-bit pairs, k = 16h + 2i (+32 for hi)
+                    uint32_t lo[8], hi[8];  // packed pairs, k = 16h + 2i (+32 for hi)
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const uint32_t b0 = (w[u] >> (16 * e)) & 0xFFu;
-                            const uint32_t b1 = (w[u] >> (16 * e + 8)) & 0xFFu;
-                            lo[2 * u + e] = pack2<OP>(fmaf(dl, (float)(b0 & 15u), -ml),
-                                                      fmaf(dl, (float)(b1 & 15u), -ml));
-                            hi[2 * u + e] = pack2<OP>(fmaf(dh, (float)(b0 >> 4), -mh),
-                                                      fmaf(dh, (float)(b1 >> 4), -mh));
-                        }
+                        dequant_pairs<OP>(w[u], dl2[2 * g], nml2[2 * g], dl2[2 * g + 1],
+                                          nml2[2 * g + 1], fdl[2 * g], fnml[2 * g],
+                                          fdl[2 * g + 1], fnml[2 * g + 1], lo[2 * u],
+                                          lo[2 * u + 1], hi[2 * u], hi[2 * u + 1]);
                     }
                     // 16-byte chunks c (8 values, k = 8c..8c+7) of row r, swizzled
                     uint8_t* arow = sA + s * C::A_BYTES + r * 128;

@@ -322,21 +322,27 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
         X.scale = scales[sb];
     }
 
-    // Rows past the end of a partial chunk and super-blocks past K are
-    // computed on in-bounds bytes (clamped) and discarded by a select: no
-    // divergent branches in the row loop.
+    // Super-blocks past K are computed on in-bounds bytes (clamped) and
+    // discarded by a select; rows past the chunk's end are skipped with a
+    // branch that is uniform across the warp (the row index depends on the
+    // warp only), so the row loop never diverges.
     const int sb_ld = valid ? sb : nsb - 1;
     int it = 0;
     for (int c = blockIdx.x; c < nchunks; c += gridDim.x, ++it) {
         const int s = it % kStages, rd = (it / kStages) & 1;
         if (!mbar_wait_warp(&full[s], (it / kStages) & 1)) break;
+        const int p = chunk_matrix(B, c);
+        const int rows = min(RC, B.N[p] - (c - B.first_chunk[p]) * RC);
         const uint8_t* base = stg + s * stage_bytes + sb_ld * 144 + wr * stride;
         float acc[RPW];
 #pragma unroll
         for (int i = 0; i < RPW; ++i) {
-            const float v = q4k_row_partial(base + (WR * i) * stride, t, use_s2, sh0, mask_a,
-                                            mask_b, X);
-            acc[i] = valid ? v : 0.f;
+            acc[i] = 0.f;
+            if (wr + WR * i < rows) {
+                const float v = q4k_row_partial(base + (WR * i) * stride, t, use_s2, sh0, mask_a,
+                                                mask_b, X);
+                acc[i] = valid ? v : 0.f;
+            }
         }
         // transposed butterfly: after log2(RPW) halving steps lane l holds one
         // row's partial (row index from its low bits), then a plain reduction

@@ -1,0 +1,63 @@
+// cuda_backend.cpp -- ft::IBackend over the ftc_backend_* C ABI.
+#include "cuda_backend.h"
+
+#include <stdexcept>
+#include <string>
+
+#include "ftc.h"
+
+namespace ft {
+namespace {
+
+// The reference reports backend failures as std::runtime_error
+// (e.g. ft/src/vulkan_backend.cpp:87-322); so does this adapter.
+void check(int rc, const char* what) {
+    if (rc != FTC_OK)
+        throw std::runtime_error(std::string("cuda backend: ") + what + ": " + ftc_last_error());
+}
+
+}  // namespace
+
+CudaBackend::CudaBackend(int device) {
+    check(ftc_backend_create(device, &be_), "create");
+    char name[256] = {0};
+    uint64_t mem = 0;
+    check(ftc_backend_info(be_, name, sizeof(name), &mem), "info");
+    info_.name = name;
+    info_.integrated = false;
+    info_.uma = false;
+    info_.mem_bytes = mem;
+}
+
+CudaBackend::~CudaBackend() { ftc_backend_destroy(be_); }
+
+void CudaBackend::matmul(const float* x, int64_t M, int64_t K, const HostTensor& W, float* y) {
+    if (K != W.cols()) throw std::runtime_error("cuda backend: matmul K != W.cols()");
+    check(ftc_backend_matmul(be_, x, M, K, W.data, (int)W.dtype, W.rows(), y), "matmul");
+}
+
+void CudaBackend::run_expert_chunk(const ExpertChunkJob& job) {
+    ftc_expert_chunk_job j;
+    j.x = job.x;
+    j.out = job.out;
+    j.gate = job.gate;
+    j.up = job.up;
+    j.down = job.down;
+    j.dtype = (int)job.dt;
+    j.M = job.M;
+    j.K = job.K;
+    j.IC = job.IC;
+    j.gate_up_row_stride = job.gate_up_row_stride;
+    j.down_row_stride = job.down_row_stride;
+    check(ftc_backend_run_expert_chunk(be_, &j), "run_expert_chunk");
+}
+
+void CudaBackend::sync() { check(ftc_backend_sync(be_), "sync"); }
+
+void CudaBackend::upload(const HostTensor& t) {
+    const size_t n = t.nbytes ? t.nbytes
+                              : t.slice_bytes() * (size_t)t.ne[2] * (size_t)t.ne[3];
+    check(ftc_backend_upload(be_, t.data, n), "upload");
+}
+
+}  // namespace ft
