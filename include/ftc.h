@@ -172,6 +172,47 @@ int ftc_mul_mat_vec_multi(int dtype, int n_mats, const void* const* w, const int
 int ftc_gemm(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x,
              int x_dtype, int64_t M, void* y, int y_dtype, void* stream);
 
+/* Routed-expert MoE FFN layer on the device: the reference's
+ * Engine::Impl::moe_ffn (ft/src/engine.cpp:179-241) after the router matmul,
+ * with each expert's FFN (ft/src/cpu_backend.cpp:106-149) in the standard
+ * GGUF layout (down_exps planes are [n_embd rows][n_ff cols]).
+ *   p = softmax(logits[t]); the top_k experts by p (ties: lower index);
+ *   w = p / sum of the chosen p;
+ *   out[t] = sum over chosen e of w_e * down_e . (silu(gate_e . x_t) * (up_e . x_t))
+ * Expert e's weights start at base + e * plane_stride.  Tokens are grouped by
+ * expert on the device and every expert matmul is a tcgen05 dequant-GEMM
+ * over all of its tokens with fp16 operands and fp32 accumulation: each row of
+ * x and of h is scaled by a power of two into fp16's range first (undone
+ * exactly afterwards), so no input range overflows.  Nothing returns to the
+ * host, so a call can be captured in a CUDA graph.  n_ff <= 49152. */
+typedef struct ftc_moe_desc {
+    int dtype;                 /* expert weight format: FTC_Q4_K */
+    int64_t n_experts;         /* E, 1..256 */
+    int64_t top_k;             /* experts per token, 1..min(8, E) */
+    int64_t n_embd;            /* model width K (multiple of 256) */
+    int64_t n_ff;              /* expert hidden width (multiple of 256) */
+    const void* gate_exps;     /* device: E planes of n_ff rows x n_embd */
+    const void* up_exps;       /* device: E planes of n_ff rows x n_embd */
+    const void* down_exps;     /* device: E planes of n_embd rows x n_ff */
+    int64_t gu_row_stride;     /* bytes per gate/up row (16-byte multiple) */
+    int64_t gu_plane_stride;   /* bytes per gate/up expert plane */
+    int64_t dn_row_stride;     /* bytes per down row */
+    int64_t dn_plane_stride;   /* bytes per down expert plane */
+} ftc_moe_desc;
+
+/* Device workspace bytes ftc_moe_ffn needs for T tokens (0 for a bad desc). */
+size_t ftc_moe_workspace_bytes(const ftc_moe_desc* desc, int64_t T);
+
+/* logits: device fp32 [T][E]; x: device [T][n_embd] in x_dtype (FTC_F32,
+ * FTC_BF16 or FTC_F16; 16-byte aligned); out: device fp32 [T][n_embd],
+ * overwritten.  workspace: 256-byte aligned device memory of at least
+ * ftc_moe_workspace_bytes.  After the call the workspace starts with the
+ * routing: int32 idx[T*top_k], then at the next 256-byte boundary fp32
+ * weights[T*top_k], then int32 counts[E] (tokens per expert), each region
+ * 256-byte aligned. */
+int ftc_moe_ffn(const ftc_moe_desc* desc, const float* logits, const void* x, int x_dtype,
+                int64_t T, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* The expert chunk of ftc_backend_run_expert_chunk on DEVICE buffers,
  * without allocating anything: for callers that cannot call cudaMalloc (an
  * engine whose HBM is owned by its own allocator, code inside someone

@@ -59,6 +59,39 @@ def test_kernel_entry_points_validate_before_launch(lib):
     assert rc == -1
 
 
+def _moe_desc(**kw):
+    rs, rd = F.row_bytes(F.Q4_K, 1024), F.row_bytes(F.Q4_K, 2048)
+    v = dict(dtype=F.Q4_K, n_experts=8, top_k=2, n_embd=1024, n_ff=2048, gate_exps=256,
+             up_exps=256, down_exps=256, gu_row_stride=rs, gu_plane_stride=rs * 2048,
+             dn_row_stride=rd, dn_plane_stride=rd * 1024)
+    v.update(kw)
+    return ftc.MoeDesc(**v)
+
+
+def test_moe_entry_validates_before_launch(lib):
+    import ctypes as C
+    d = _moe_desc()
+    need = lib.ftc_moe_workspace_bytes(C.byref(d), 64)
+    # routing arrays, row scales, gathered x, fp32 gate|up, fp16 h, fp32 expert outputs
+    assert need >= 128 * (1024 * 2 + 2 * 2048 * 4 + 2048 * 2 + 1024 * 4)
+    for bad in (dict(top_k=0), dict(top_k=9), dict(n_experts=2, top_k=3),
+                dict(n_experts=300), dict(n_ff=1000), dict(n_embd=100), dict(dtype=F.Q8_0),
+                dict(n_ff=65536)):
+        assert lib.ftc_moe_workspace_bytes(C.byref(_moe_desc(**bad)), 64) == 0, bad
+        rc = lib.ftc_moe_ffn(C.byref(_moe_desc(**bad)), 256, 256, F.BF16, 64, 256, 256, need, None)
+        assert rc in (-1, -2), bad
+    # T == 0 is a no-op that touches nothing
+    assert lib.ftc_moe_ffn(C.byref(d), None, None, F.BF16, 0, None, None, 0, None) == 0
+    assert lib.ftc_moe_ffn(C.byref(d), 256, None, F.BF16, 4, 256, 256, need, None) == -1
+    assert "null" in ftc.last_error()
+    rc = lib.ftc_moe_ffn(C.byref(d), 256, 256, F.BF16, 64, 256, 256, need - 256, None)
+    assert rc == -1 and "workspace too small" in ftc.last_error()
+    rc = lib.ftc_moe_ffn(C.byref(d), 256, 256, F.BF16, 64, 256, 128, need, None)
+    assert rc == -1 and "alignment" in ftc.last_error()
+    rc = lib.ftc_moe_ffn(C.byref(d), 256, 256, F.Q8_0, 64, 256, 256, need, None)
+    assert rc == -2
+
+
 def _run_child(code, env_extra):
     env = dict(os.environ, **env_extra)
     return subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env,

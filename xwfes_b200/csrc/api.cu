@@ -61,6 +61,9 @@ int expert_chunk_dev(int dtype, const float* x, float* out, const void* gate, co
 
 int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x, int x_dtype,
              int64_t M, void* y, int y_dtype, cudaStream_t st);
+size_t moe_workspace_bytes(const ftc_moe_desc* d, int64_t T);
+int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dtype, int64_t T,
+            float* out, void* ws, size_t ws_bytes, cudaStream_t st);
 
 // status readers of the translation units whose kernels use bounded waits
 int devstat_gemv_q4k(int clear);
@@ -412,6 +415,17 @@ int ftc_gemm(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
              int x_dtype, int64_t M, void* y, int y_dtype, void* stream) {
     FTC_REQUIRE(dtype == FTC_Q4_K, FTC_E_UNSUPPORTED, "ftc_gemm: only Q4_K weights");
     int rc = gemm_q4k(w, N, K, row_stride, x, x_dtype, M, y, y_dtype, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+size_t ftc_moe_workspace_bytes(const ftc_moe_desc* desc, int64_t T) {
+    return moe_workspace_bytes(desc, T);
+}
+
+int ftc_moe_ffn(const ftc_moe_desc* desc, const float* logits, const void* x, int x_dtype,
+                int64_t T, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = moe_ffn(desc, logits, x, x_dtype, T, out, workspace, workspace_bytes,
+                     (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

@@ -27,12 +27,21 @@
 //               swizzled K-major layout the MMA reads.
 // Every pipeline wait is bounded in time (sm100.cuh); a kernel that gives up
 // records a status and returns.
+//
+// Grouped mode (MoE experts).  Rows [offsets[g], offsets[g] + counts[g]) of X
+// and Y belong to group g and multiply weight plane g (expert g); counts and
+// offsets are read on the device, so a router kernel can produce them in the
+// same stream with no host round trip.  One or two weight sets (gate and up)
+// share the tokens; set s writes columns [s*N, (s+1)*N) of Y.  A tile with
+// fewer tokens than BN issues a narrower MMA (N rounded up to 16) and loads a
+// shorter activation box (32, 64, ... rows).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -43,7 +52,24 @@ namespace ftc {
 
 FTC_DEVSTAT_READER(devstat_gemm_q4k)
 
+constexpr int kGemmMaxGroups = 256;
+
+// Token groups of one launch (see the grouped mode above).
+struct GemmGroups {
+    const int32_t* counts;   // device [G] rows per group; nullptr: one group of all M rows
+    const int32_t* offsets;  // device [G] first row of each group
+    int G;                   // groups = weight planes
+    int n_sets;              // weight tensors sharing the tokens (1, or 2 for gate + up)
+    int64_t ldy;             // Y row pitch in elements
+};
+
 namespace {
+
+constexpr int kXMaps = 4;  // activation boxes of 32, 64, 128, 256 rows (up to BN)
+
+struct XMaps {
+    CUtensorMap m[kXMaps];
+};
 
 constexpr int BM = 128;       // weight rows per tile (MMA M)
 constexpr int BK = 64;        // k per stage: one 128-byte swizzle row of 16-bit values
@@ -71,8 +97,42 @@ struct Cfg {
     // barriers: a_full[NA] a_empty[NA] b_full[NB] b_empty[NB] raw_full[R]
     // raw_empty[R] acc_full[2] acc_empty[2]
     static constexpr int N_BARS = 2 * NA + 2 * NB + 2 * kRawSlots + 4;
-    static constexpr int SMEM = OFF_BAR + N_BARS * 8 + 16 + 1024;  // +1024: base alignment slack
+    // tile schedule: first tile, first row and row count of each group
+    static constexpr int OFF_SCHED = OFF_BAR + N_BARS * 8 + 16;
+    static constexpr int SMEM = OFF_SCHED + (3 * kGemmMaxGroups + 1) * 4 + 1024;  // +1024: alignment slack
 };
+
+// Tile t of the schedule: group, weight set, 128-row block of W, and the
+// group's token rows it covers.  Tiles of a group run token tile by token
+// tile, weight blocks fastest, so concurrent CTAs share the activation tile.
+struct TileRef {
+    int g, set, nt, row0, rows;
+};
+
+template <int BN>
+__device__ __forceinline__ TileRef tile_ref(int tile, const int* s_start, const int* s_base,
+                                            const int* s_cnt, int G, int n_tiles, int n_all) {
+    int lo = 0, hi = G - 1;  // last group whose first tile is <= tile
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_start[mid] <= tile) lo = mid;
+        else hi = mid - 1;
+    }
+    const int local = tile - s_start[lo];
+    const int tt = local / n_all, na = local - tt * n_all;
+    TileRef r;
+    r.g = lo;
+    r.set = na / n_tiles;
+    r.nt = na - r.set * n_tiles;
+    r.row0 = s_base[lo] + tt * BN;
+    r.rows = min(BN, s_cnt[lo] - tt * BN);
+    return r;
+}
+
+// smallest activation box (32 << i rows) that covers `rows`
+__device__ __forceinline__ int xbox_index(int rows) {
+    return rows <= 32 ? 0 : rows <= 64 ? 1 : rows <= 128 ? 2 : 3;
+}
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -205,8 +265,9 @@ __device__ __forceinline__ void store_out(void* y, int ytype, int64_t idx, float
 
 template <int BN, typename OP>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-            int M, int N, int K, void* __restrict__ y, int ytype) {
+gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
+            const __grid_constant__ XMaps tm_x, int M, int N, int K, void* __restrict__ y,
+            int ytype, const GemmGroups grp) {
     using C = Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -225,6 +286,17 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::N_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* s_start = reinterpret_cast<int*>(smem + C::OFF_SCHED);  // [G + 1]
+    int* s_base = s_start + kGemmMaxGroups + 1;                  // [G]
+    int* s_cnt = s_base + kGemmMaxGroups;                        // [G]
+    const int G = grp.G;
+    const int n_tiles = (N + BM - 1) / BM;
+    const int n_all = n_tiles * grp.n_sets;
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        const int base = grp.counts ? min(max(grp.offsets[g], 0), M) : 0;
+        s_base[g] = base;
+        s_cnt[g] = grp.counts ? min(max(grp.counts[g], 0), M - base) : M;
+    }
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -247,6 +319,15 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         *abort_flag = 0;
         mbar_fence_init();
     }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int g = 0; g < G; ++g) {
+            s_start[g] = acc;
+            acc += (s_cnt[g] + BN - 1) / BN * n_all;
+        }
+        s_start[G] = acc;
+    }
     if (warp == 0) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
@@ -256,25 +337,28 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int n_tiles = (N + BM - 1) / BM;
-    const int t_tiles = (M + BN - 1) / BN;
-    const int tiles = n_tiles * t_tiles;
+    const int tiles = s_start[G];
     const int nsb = K / 256;
+    auto tile_at = [&](int tile) {
+        return tile_ref<BN>(tile, s_start, s_base, s_cnt, G, n_tiles, n_all);
+    };
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA
         if (lane == 0) {
-            prefetch_tensormap(&tm_w);
-            prefetch_tensormap(&tm_x);
+            for (int i = 0; i < kXMaps && (32 << i) <= BN; ++i) prefetch_tensormap(&tm_x.m[i]);
             const uint64_t pol_x = policy_evict_last();
             uint32_t kc = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-                const int tt = tile / n_tiles;
+                const TileRef t = tile_at(tile);
+                const int xb = xbox_index(t.rows);
+                const CUtensorMap* xm = &tm_x.m[xb];
+                const uint32_t bytes = (uint32_t)(32 << xb) * BK * 2;
                 for (int ks = 0; ks < nsb * 4; ++ks) {
                     const int s = kc % C::NB;
                     if (!mbar_wait(&b_empty[s], ((kc / C::NB) & 1) ^ 1)) { *abort_flag = 1; break; }
-                    mbar_arrive_expect_tx(&b_full[s], C::B_BYTES);
-                    tma_load_2d(sB + s * C::B_BYTES, &tm_x, ks * BK, tt * BN, &b_full[s], pol_x);
+                    mbar_arrive_expect_tx(&b_full[s], bytes);
+                    tma_load_2d(sB + s * C::B_BYTES, xm, ks * BK, t.row0, &b_full[s], pol_x);
                     ++kc;
                 }
             }
@@ -288,15 +372,19 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         // Raw weight tiles run up to kRawSlots super-blocks ahead of the
         // dequant warps, independent of the activation ring.
         if (lane == 0) {
+            prefetch_tensormap(&tm_w);
+            prefetch_tensormap(&tm_w2);
             const uint64_t pol_w = policy_evict_last();  // weights are re-read per token tile
             uint32_t rc = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-                const int nt = tile % n_tiles;
+                const TileRef t = tile_at(tile);
+                const CUtensorMap* wm = t.set ? &tm_w2 : &tm_w;
                 for (int sb = 0; sb < nsb; ++sb) {
                     const int rs = rc % kRawSlots;
                     if (!mbar_wait(&raw_empty[rs], ((rc / kRawSlots) & 1) ^ 1)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
-                    tma_load_2d(sRaw + rs * kRawBytes, &tm_w, sb * 144, nt * BM, &raw_full[rs], pol_w);
+                    tma_load_3d(sRaw + rs * kRawBytes, wm, sb * 144, t.nt * BM, t.g, &raw_full[rs],
+                                pol_w);
                     ++rc;
                 }
             }
@@ -309,11 +397,12 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         // ---------------------------------------------------------- MMA
         if (lane == 0) {
             constexpr uint32_t fmt = std::is_same<OP, __half>::value ? 0u : 1u;
-            constexpr uint32_t idesc = idesc_f16(fmt, BM, BN);
             uint32_t kc = 0;
             int i = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++i) {
                 const int b = i & 1;
+                // MMA N = the tile's tokens rounded up to 16
+                const uint32_t idesc = idesc_f16(fmt, BM, (uint32_t)min(BN, (tile_at(tile).rows + 15) & ~15));
                 if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
@@ -346,21 +435,23 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         int i = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
             const int b = i & 1;
-            const int nt = tile % n_tiles, tt = tile / n_tiles;
+            const TileRef t = tile_at(tile);
             if (!mbar_wait_warp(&acc_full[b], (i >> 1) & 1)) { *abort_flag = 1; break; }
             tc_fence_after();
-            const int n = nt * BM + 32 * q + lane;
+            const int n = t.nt * BM + 32 * q + lane;
+            const int64_t col = (int64_t)t.set * N + n;
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = 0; c0 < t.rows; c0 += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(taddr + c0, r);
                 tmem_ld_wait();
-                const int t0 = tt * BN + c0;
+                const int64_t y0 = (int64_t)(t.row0 + c0) * grp.ldy + col;
+                const int jn = min(32, t.rows - c0);
                 if (n < N) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        if (t0 + j < M) store_out(y, ytype, (int64_t)(t0 + j) * N + n, __uint_as_float(r[j]));
+                        if (j < jn) store_out(y, ytype, y0 + (int64_t)j * grp.ldy, __uint_as_float(r[j]));
                 }
             }
             tc_fence_before();
@@ -444,8 +535,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <int BN, typename OP>
-int launch(const CUtensorMap& tw, const CUtensorMap& tx, int M, int N, int K, void* y, int ytype,
-           cudaStream_t st) {
+int launch(const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx, int M, int N, int K,
+           void* y, int ytype, const GemmGroups& grp, int64_t max_tiles, cudaStream_t st) {
     using C = Cfg<BN>;
     static bool configured = false;
     if (!configured) {
@@ -456,9 +547,71 @@ int launch(const CUtensorMap& tw, const CUtensorMap& tx, int M, int N, int K, vo
     }
     static int sms = 0;
     if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
-    const int grid = std::min(tiles, sms);
-    gemm_q4k_tc<BN, OP><<<grid, kThreads, C::SMEM, st>>>(tw, tx, M, N, K, y, ytype);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sms));
+    gemm_q4k_tc<BN, OP><<<grid, kThreads, C::SMEM, st>>>(tw, tw2, tx, M, N, K, y, ytype, grp);
+    return FTC_OK;
+}
+
+// W: G planes of N rows of Q4_K blocks, plane g at w + g * plane_stride.
+int weight_map(CUtensorMap* m, const void* w, int64_t N, int64_t K, int64_t row_stride, int64_t G,
+               int64_t plane_stride, const char* who) {
+    auto enc = encode_fn();
+    FTC_REQUIRE(enc, FTC_E_CUDA, std::string(who) + ": cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[3] = {(cuuint64_t)((K / 256) * 144), (cuuint64_t)N, (cuuint64_t)G};
+    const cuuint64_t strides[2] = {(cuuint64_t)row_stride, (cuuint64_t)plane_stride};
+    const cuuint32_t box[3] = {144, BM, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(w), dims, strides, box,
+                     es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    FTC_REQUIRE(r == CUDA_SUCCESS, FTC_E_CUDA, std::string(who) + ": weight tensor map rejected");
+    return FTC_OK;
+}
+
+// X: rows x K 16-bit activations; one map per box height 32, 64, ... BN.
+int act_maps(XMaps* mx, const void* x, int x_dtype, int64_t rows, int64_t K, int BN,
+             const char* who) {
+    auto enc = encode_fn();
+    FTC_REQUIRE(enc, FTC_E_CUDA, std::string(who) + ": cuTensorMapEncodeTiled unavailable");
+    std::memset(mx, 0, sizeof(*mx));
+    for (int i = 0; i < kXMaps && (32 << i) <= BN; ++i) {
+        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+        const cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
+        const cuuint32_t box[2] = {BK, (cuuint32_t)(32 << i)};
+        const cuuint32_t es[2] = {1, 1};
+        CUresult r = enc(&mx->m[i],
+                         x_dtype == FTC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, const_cast<void*>(x), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        FTC_REQUIRE(r == CUDA_SUCCESS, FTC_E_CUDA,
+                    std::string(who) + ": activation tensor map rejected");
+    }
+    return FTC_OK;
+}
+
+int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx,
+             int M, int N, int K, void* y, int y_dtype, const GemmGroups& grp, int64_t max_tiles,
+             cudaStream_t st) {
+    const bool bf = x_dtype == FTC_BF16;
+    int rc;
+    if (BN == 128)
+        rc = bf ? launch<128, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
+                : launch<128, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
+    else
+        rc = bf ? launch<256, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
+                : launch<256, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
+    if (rc != FTC_OK) return rc;
+    FTC_CUDA(cudaGetLastError());
+    return FTC_OK;
+}
+
+int check_types(int x_dtype, int y_dtype, const char* who) {
+    FTC_REQUIRE(x_dtype == FTC_BF16 || x_dtype == FTC_F16, FTC_E_UNSUPPORTED,
+                std::string(who) + ": activations must be bf16 or fp16");
+    FTC_REQUIRE(y_dtype == FTC_BF16 || y_dtype == FTC_F16 || y_dtype == FTC_F32, FTC_E_UNSUPPORTED,
+                std::string(who) + ": output must be bf16, fp16 or fp32");
     return FTC_OK;
 }
 
@@ -471,53 +624,61 @@ int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void
     FTC_REQUIRE(K % 256 == 0, FTC_E_INVALID, "ftc_gemm: K must be a multiple of 256 for Q4_K");
     FTC_REQUIRE(M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX, FTC_E_INVALID,
                 "ftc_gemm: shape too large");
-    FTC_REQUIRE(x_dtype == FTC_BF16 || x_dtype == FTC_F16, FTC_E_UNSUPPORTED,
-                "ftc_gemm: activations must be bf16 or fp16");
-    FTC_REQUIRE(y_dtype == FTC_BF16 || y_dtype == FTC_F16 || y_dtype == FTC_F32, FTC_E_UNSUPPORTED,
-                "ftc_gemm: output must be bf16, fp16 or fp32");
+    int rc = check_types(x_dtype, y_dtype, "ftc_gemm");
+    if (rc) return rc;
     FTC_REQUIRE(row_stride >= (K / 256) * 144 && row_stride % 16 == 0 && (uintptr_t)w % 16 == 0,
                 FTC_E_INVALID, "ftc_gemm: weight rows must be 16-byte aligned");
     FTC_REQUIRE((uintptr_t)x % 16 == 0, FTC_E_INVALID, "ftc_gemm: activations must be 16-byte aligned");
-    auto enc = encode_fn();
-    FTC_REQUIRE(enc, FTC_E_CUDA, "ftc_gemm: cuTensorMapEncodeTiled unavailable");
-
-    CUtensorMap tw, tx;
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)((K / 256) * 144), (cuuint64_t)N};
-        const cuuint64_t strides[1] = {(cuuint64_t)row_stride};
-        const cuuint32_t box[2] = {144, BM};
-        const cuuint32_t es[2] = {1, 1};
-        CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides,
-                         box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        FTC_REQUIRE(r == CUDA_SUCCESS, FTC_E_CUDA, "ftc_gemm: weight tensor map rejected");
-    }
     const int BN = M <= 128 ? 128 : 256;
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-        const cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-        const cuuint32_t box[2] = {BK, (cuuint32_t)BN};
-        const cuuint32_t es[2] = {1, 1};
-        CUresult r = enc(&tx,
-                         x_dtype == FTC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                         2, const_cast<void*>(x), dims, strides, box, es,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        FTC_REQUIRE(r == CUDA_SUCCESS, FTC_E_CUDA, "ftc_gemm: activation tensor map rejected");
-    }
+    CUtensorMap tw;
+    XMaps tx;
+    if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm"))) return rc;
+    if ((rc = act_maps(&tx, x, x_dtype, M, K, BN, "ftc_gemm"))) return rc;
     if (inject_fail("ftc_gemm")) return set_error(FTC_E_INJECTED, "ftc_gemm: injected failure");
-    int rc;
-    const bool bf = x_dtype == FTC_BF16;
-    if (BN == 128)
-        rc = bf ? launch<128, __nv_bfloat16>(tw, tx, (int)M, (int)N, (int)K, y, y_dtype, st)
-                : launch<128, __half>(tw, tx, (int)M, (int)N, (int)K, y, y_dtype, st);
-    else
-        rc = bf ? launch<256, __nv_bfloat16>(tw, tx, (int)M, (int)N, (int)K, y, y_dtype, st)
-                : launch<256, __half>(tw, tx, (int)M, (int)N, (int)K, y, y_dtype, st);
-    if (rc != FTC_OK) return rc;
-    FTC_CUDA(cudaGetLastError());
-    return FTC_OK;
+    const GemmGroups grp = {nullptr, nullptr, 1, 1, N};
+    const int64_t tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
+    return dispatch(BN, x_dtype, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles, st);
+}
+
+// Grouped form: rows of x are grouped by expert (device counts / offsets);
+// w (and w2 when n_sets == 2) hold G planes of N rows.  max_rows_per_group
+// bounds every count (it picks the token tile).
+int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64_t plane_stride,
+                     int64_t N, int64_t K, int64_t row_stride, const void* x, int x_dtype,
+                     int64_t rows, const int32_t* counts, const int32_t* offsets,
+                     int64_t max_rows_per_group, void* y, int y_dtype, int64_t ldy,
+                     cudaStream_t st) {
+    FTC_REQUIRE(w && x && y && counts && offsets && (n_sets == 1 || w2), FTC_E_INVALID,
+                "gemm_q4k_grouped: null pointer");
+    FTC_REQUIRE(n_sets == 1 || n_sets == 2, FTC_E_INVALID, "gemm_q4k_grouped: 1 or 2 weight sets");
+    FTC_REQUIRE(G >= 1 && G <= kGemmMaxGroups, FTC_E_INVALID, "gemm_q4k_grouped: 1..256 groups");
+    FTC_REQUIRE(rows > 0 && N > 0 && K > 0 && K % 256 == 0, FTC_E_INVALID,
+                "gemm_q4k_grouped: bad shape");
+    FTC_REQUIRE(rows <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX, FTC_E_INVALID,
+                "gemm_q4k_grouped: shape too large");
+    int rc = check_types(x_dtype, y_dtype, "gemm_q4k_grouped");
+    if (rc) return rc;
+    FTC_REQUIRE(row_stride >= (K / 256) * 144 && row_stride % 16 == 0 && plane_stride % 16 == 0 &&
+                    plane_stride >= N * row_stride && (uintptr_t)w % 16 == 0 &&
+                    (uintptr_t)w2 % 16 == 0,
+                FTC_E_INVALID, "gemm_q4k_grouped: weight rows and planes must be 16-byte aligned");
+    FTC_REQUIRE((uintptr_t)x % 16 == 0, FTC_E_INVALID,
+                "gemm_q4k_grouped: activations must be 16-byte aligned");
+    FTC_REQUIRE(ldy >= n_sets * N, FTC_E_INVALID, "gemm_q4k_grouped: output pitch too small");
+    const int BN = max_rows_per_group <= 128 ? 128 : 256;
+    CUtensorMap tw, tw2;
+    XMaps tx;
+    if ((rc = weight_map(&tw, w, N, K, row_stride, G, plane_stride, "gemm_q4k_grouped"))) return rc;
+    if (n_sets == 2 &&
+        (rc = weight_map(&tw2, w2, N, K, row_stride, G, plane_stride, "gemm_q4k_grouped")))
+        return rc;
+    if ((rc = act_maps(&tx, x, x_dtype, rows, K, BN, "gemm_q4k_grouped"))) return rc;
+    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy};
+    // upper bound on tiles: every non-empty group adds at most one partial token tile
+    const int64_t tok_tiles = (rows + BN - 1) / BN + std::min<int64_t>(G, rows);
+    const int64_t tiles = tok_tiles * ((N + BM - 1) / BM) * n_sets;
+    return dispatch(BN, x_dtype, tw, n_sets == 2 ? tw2 : tw, tx, (int)rows, (int)N, (int)K, y,
+                    y_dtype, grp, tiles, st);
 }
 
 }  // namespace ftc

@@ -1,0 +1,380 @@
+// moe.cu -- routed-expert MoE FFN on the device: the reference's
+// Engine::Impl::moe_ffn (ft/src/engine.cpp:179-241) with its expert FFN
+// (ft/src/cpu_backend.cpp:106-149) in the standard GGUF down layout.
+//
+//   route    p = softmax(logits[t]) over E experts (fp32 exps, double sum,
+//            ft/src/engine.cpp:62-72); the U most probable experts (ties to
+//            the lower index); w[t][u] = p / sum of the U chosen
+//            (ft/src/engine.cpp:198-215).
+//   group    the T*U (token, slot) pairs sorted by expert, tokens ascending
+//            within an expert (the reference's per-expert token lists,
+//            ft/src/engine.cpp:212-213); experts ranked by first use.
+//   gather   x rows into expert order as fp16, each row scaled by a power of
+//            two 2^-xs into [2^14, 2^15) (exact; fp16 keeps 11 bits for any
+//            input range).
+//   gate/up  one grouped dequant-GEMM launch over both weight sets
+//            (gemm_q4k_sm100.cu): gu[row] = [x.gate_e | x.up_e] in fp32.
+//   silu     h = silu(g) * u in fp32 (g / (1 + exp(-g)),
+//            ft/src/cpu_backend.cpp:127) after undoing 2^-xs, stored as fp16
+//            with its own row scale 2^-hs.
+//   down     grouped dequant-GEMM: yd[row] = h . down_e  (fp32).
+//   combine  out[t] = sum over t's slots of w * (yd * 2^hs), added in the
+//            experts' first-use order with separately rounded products and
+//            sums, as the reference's tmpo[m] += w * acb
+//            (ft/src/engine.cpp:229-236).
+//
+// Every step reads device-side counts: there is no host round trip, so the
+// whole layer can be captured in a CUDA graph.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace ftc {
+
+int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64_t plane_stride,
+                     int64_t N, int64_t K, int64_t row_stride, const void* x, int x_dtype,
+                     int64_t rows, const int32_t* counts, const int32_t* offsets,
+                     int64_t max_rows_per_group, void* y, int y_dtype, int64_t ldy,
+                     cudaStream_t st);
+
+namespace {
+
+constexpr int kRouteThreads = 1024;
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 8;
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Power-of-two row scale for fp16 operands: s with amax * 2^-s in
+// [2^14, 2^15) (below fp16's 65504), clamped so 2^s and 2^-s are normal
+// floats.  Scaling by 2^-s and back by 2^s is exact.
+__device__ __forceinline__ int row_scale_exp(float amax) {
+    if (!(amax > 0.f) || !isfinite(amax)) return 0;
+    const int e = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 127;  // floor(log2) for normals
+    return max(-126, min(126, e - 14));
+}
+
+__device__ __forceinline__ float exp2i(int s) { return __uint_as_float((uint32_t)(s + 127) << 23); }
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();  // red may still be read by a previous call
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    float m = 0.f;
+    for (int i = 0; i < nw; ++i) m = fmaxf(m, red[i]);
+    return m;
+}
+
+// One CTA routes all T tokens and builds the expert grouping:
+//   idx[t*U+u], w[t*U+u]  chosen experts and renormalised weights
+//   counts[e], offsets[e] rows of expert e in expert order (offsets[E] = T*U)
+//   rank[e]               order of first use (ft/src/engine.cpp:213-217)
+//   pos[t*U+u]            row of pair (t, u) in expert order
+//   row_token[row]        token of each row
+__global__ void __launch_bounds__(kRouteThreads)
+moe_route(const float* __restrict__ logits, int T, int E, int U, int32_t* __restrict__ idx,
+          float* __restrict__ wts, int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+          int32_t* __restrict__ rank, int32_t* __restrict__ pos, int32_t* __restrict__ row_token) {
+    __shared__ int s_count[kMaxExperts];
+    __shared__ int s_first[kMaxExperts];
+    __shared__ int s_off[kMaxExperts];
+    __shared__ int s_scan[kRouteThreads];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        s_count[e] = 0;
+        s_first[e] = INT32_MAX;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float* r = logits + (int64_t)t * E;
+        float mx = r[0];
+        for (int j = 1; j < E; ++j) mx = fmaxf(mx, r[j]);
+        double sum = 0.0;
+        for (int j = 0; j < E; ++j) sum += (double)expf(r[j] - mx);
+        const float inv = (float)(1.0 / sum);
+        int chosen[kMaxTopK];
+        float pr[kMaxTopK];
+        for (int u = 0; u < U; ++u) {
+            int best = -1;
+            float bp = 0.f;
+            for (int j = 0; j < E; ++j) {
+                bool taken = false;
+                for (int v = 0; v < u; ++v) taken |= (chosen[v] == j);
+                if (taken) continue;
+                const float pj = expf(r[j] - mx) * inv;
+                if (best < 0 || pj > bp) {
+                    best = j;
+                    bp = pj;
+                }
+            }
+            chosen[u] = best;
+            pr[u] = bp;
+        }
+        float wsum = 0.f;
+        for (int u = 0; u < U; ++u) wsum += pr[u];
+        const float winv = wsum > 0.f ? 1.f / wsum : 0.f;
+        for (int u = 0; u < U; ++u) {
+            idx[t * U + u] = chosen[u];
+            wts[t * U + u] = pr[u] * winv;
+            atomicAdd(&s_count[chosen[u]], 1);
+            atomicMin(&s_first[chosen[u]], t * U + u);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int e = 0; e < E; ++e) {
+            s_off[e] = acc;
+            offsets[e] = acc;
+            counts[e] = s_count[e];
+            acc += s_count[e];
+        }
+        offsets[E] = acc;
+    }
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int rk = 0;
+        if (s_first[e] != INT32_MAX)
+            for (int f = 0; f < E; ++f) rk += s_first[f] < s_first[e];
+        rank[e] = s_first[e] == INT32_MAX ? -1 : rk;
+    }
+    __syncthreads();
+    // rows in expert order, tokens ascending within an expert: the row of
+    // (t, e) is offsets[e] + #{t' < t routed to e}, one block scan per expert
+    for (int e = 0; e < E; ++e) {
+        if (s_count[e] == 0) continue;  // uniform: shared value
+        int carry = 0;
+        for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+            const int t = t0 + threadIdx.x;
+            int slot = -1;
+            if (t < T)
+                for (int u = 0; u < U; ++u)
+                    if (idx[t * U + u] == e) slot = u;
+            s_scan[threadIdx.x] = slot >= 0;
+            __syncthreads();
+            for (int o = 1; o < (int)blockDim.x; o <<= 1) {  // inclusive scan
+                const int v = (int)threadIdx.x >= o ? s_scan[threadIdx.x - o] : 0;
+                __syncthreads();
+                s_scan[threadIdx.x] += v;
+                __syncthreads();
+            }
+            if (slot >= 0) {
+                const int row = s_off[e] + carry + s_scan[threadIdx.x] - 1;
+                pos[t * U + slot] = row;
+                row_token[row] = t;
+            }
+            carry += s_scan[blockDim.x - 1];
+            __syncthreads();
+        }
+    }
+}
+
+// xg[row] = fp16(x[row_token[row]] * 2^-xs[row]), one CTA per row
+template <typename TI>
+__global__ void moe_gather_scale(const TI* __restrict__ x, const int32_t* __restrict__ row_token,
+                                 int K, __half* __restrict__ xg, int32_t* __restrict__ xs) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const TI* src = x + (int64_t)row_token[row] * K;
+    float amax = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(to_f(src[k])));
+    const int s = row_scale_exp(block_max(amax, red));
+    const float sc = exp2i(-s);
+    __half2* dst = reinterpret_cast<__half2*>(xg + (int64_t)row * K);
+    for (int k = 2 * threadIdx.x; k < K; k += 2 * blockDim.x)
+        dst[k >> 1] = __floats2half2_rn(to_f(src[k]) * sc, to_f(src[k + 1]) * sc);
+    if (threadIdx.x == 0) xs[row] = s;
+}
+
+// h = silu(g) * u with g, u = gu[row] * 2^xs[row] (fp32, exact rescale);
+// h[row] = fp16(h * 2^-hs[row]).  h is kept in shared memory between the
+// max pass and the store pass.
+__global__ void moe_silu_scale(const float* __restrict__ gu, const int32_t* __restrict__ xs,
+                               int n_ff, __half* __restrict__ h, int32_t* __restrict__ hs) {
+    extern __shared__ float sh[];
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const float* g = gu + (int64_t)row * 2 * n_ff;
+    const float* u = g + n_ff;
+    const float up = exp2i(xs[row]);
+    float amax = 0.f;
+    for (int i = threadIdx.x; i < n_ff; i += blockDim.x) {
+        const float gv = g[i] * up;
+        const float v = gv / (1.f + expf(-gv)) * (u[i] * up);
+        sh[i] = v;
+        amax = fmaxf(amax, fabsf(v));
+    }
+    const int s = row_scale_exp(block_max(amax, red));
+    const float sc = exp2i(-s);
+    __half2* dst = reinterpret_cast<__half2*>(h + (int64_t)row * n_ff);
+    for (int i = 2 * threadIdx.x; i < n_ff; i += 2 * blockDim.x)
+        dst[i >> 1] = __floats2half2_rn(sh[i] * sc, sh[i + 1] * sc);
+    if (threadIdx.x == 0) hs[row] = s;
+}
+
+// out[t][k] = sum over slots (in expert first-use order) of w * yd[pos][k]
+__global__ void moe_combine(const float* __restrict__ yd, const int32_t* __restrict__ hs,
+                            const int32_t* __restrict__ pos, const int32_t* __restrict__ idx,
+                            const float* __restrict__ wts, const int32_t* __restrict__ rank, int T,
+                            int U, int K, float* __restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)T * (K / 4);
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / (K / 4), k4 = i - t * (K / 4);
+        int order[kMaxTopK];
+        for (int u = 0; u < U; ++u) {  // insertion sort of the slots by expert rank
+            int v = u;
+            const int ru = rank[idx[t * U + u]];
+            while (v > 0 && rank[idx[t * U + order[v - 1]]] > ru) {
+                order[v] = order[v - 1];
+                --v;
+            }
+            order[v] = u;
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < U; ++j) {
+            const int u = order[j];
+            const float w = wts[t * U + u];
+            const int row = pos[t * U + u];
+            float4 y = reinterpret_cast<const float4*>(yd + (int64_t)row * K)[k4];
+            const float up = exp2i(hs[row]);  // undo the row scale of h (exact)
+            y.x *= up;
+            y.y *= up;
+            y.z *= up;
+            y.w *= up;
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, y.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, y.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, y.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, y.w));
+        }
+        reinterpret_cast<float4*>(out + t * K)[k4] = acc;
+    }
+}
+
+int grid_for(int64_t n) {
+    static int sms = 0;
+    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8));
+}
+
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// Workspace regions, in order (each 256-byte aligned).
+struct MoeLayout {
+    size_t idx, wts, counts, offsets, rank, pos, row_token, xs, hs, xg, gu, h, yd, total;
+};
+
+MoeLayout moe_layout(const ftc_moe_desc& d, int64_t T) {
+    const int64_t R = T * d.top_k, E = d.n_experts;
+    MoeLayout L;
+    size_t o = 0;
+    L.idx = o;       o += align256((size_t)R * 4);
+    L.wts = o;       o += align256((size_t)R * 4);
+    L.counts = o;    o += align256((size_t)E * 4);
+    L.offsets = o;   o += align256((size_t)(E + 1) * 4);
+    L.rank = o;      o += align256((size_t)E * 4);
+    L.pos = o;       o += align256((size_t)R * 4);
+    L.row_token = o; o += align256((size_t)R * 4);
+    L.xs = o;        o += align256((size_t)R * 4);
+    L.hs = o;        o += align256((size_t)R * 4);
+    L.xg = o;        o += align256((size_t)R * d.n_embd * 2);
+    L.gu = o;        o += align256((size_t)R * 2 * d.n_ff * 4);
+    L.h = o;         o += align256((size_t)R * d.n_ff * 2);
+    L.yd = o;        o += align256((size_t)R * d.n_embd * 4);
+    L.total = o;
+    return L;
+}
+
+constexpr int64_t kMaxFf = 49152;  // h row kept in shared memory by moe_silu_scale
+
+int check_desc(const ftc_moe_desc* d, const char* who) {
+    FTC_REQUIRE(d, FTC_E_INVALID, std::string(who) + ": null descriptor");
+    FTC_REQUIRE(d->dtype == FTC_Q4_K, FTC_E_UNSUPPORTED,
+                std::string(who) + ": expert weights must be Q4_K");
+    FTC_REQUIRE(d->n_experts >= 1 && d->n_experts <= kMaxExperts && d->top_k >= 1 &&
+                    d->top_k <= kMaxTopK && d->top_k <= d->n_experts,
+                FTC_E_INVALID, std::string(who) + ": need 1 <= top_k <= min(8, n_experts) <= 256");
+    FTC_REQUIRE(d->n_embd > 0 && d->n_ff > 0 && d->n_embd % 256 == 0 && d->n_ff % 256 == 0 &&
+                    d->n_embd <= INT32_MAX && d->n_ff <= kMaxFf,
+                FTC_E_INVALID,
+                std::string(who) + ": n_embd and n_ff must be multiples of 256, n_ff <= 49152");
+    return FTC_OK;
+}
+
+}  // namespace
+
+size_t moe_workspace_bytes(const ftc_moe_desc* d, int64_t T) {
+    if (check_desc(d, "ftc_moe_workspace_bytes") != FTC_OK || T < 0) return 0;
+    return moe_layout(*d, T).total;
+}
+
+int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dtype, int64_t T,
+            float* out, void* ws, size_t ws_bytes, cudaStream_t st) {
+    int rc = check_desc(d, "ftc_moe_ffn");
+    if (rc) return rc;
+    FTC_REQUIRE(T >= 0 && T * d->top_k <= INT32_MAX / 2, FTC_E_INVALID, "ftc_moe_ffn: bad T");
+    if (T == 0) return FTC_OK;
+    FTC_REQUIRE(logits && x && out && ws && d->gate_exps && d->up_exps && d->down_exps,
+                FTC_E_INVALID, "ftc_moe_ffn: null pointer");
+    FTC_REQUIRE(x_dtype == FTC_F32 || x_dtype == FTC_BF16 || x_dtype == FTC_F16,
+                FTC_E_UNSUPPORTED, "ftc_moe_ffn: x must be fp32, bf16 or fp16");
+    FTC_REQUIRE((uintptr_t)ws % 256 == 0 && (uintptr_t)out % 16 == 0 && (uintptr_t)x % 16 == 0,
+                FTC_E_INVALID, "ftc_moe_ffn: x and out need 16-byte, workspace 256-byte alignment");
+    const MoeLayout L = moe_layout(*d, T);
+    FTC_REQUIRE(ws_bytes >= L.total, FTC_E_INVALID, "ftc_moe_ffn: workspace too small");
+    if (inject_fail("ftc_moe_ffn")) return set_error(FTC_E_INJECTED, "ftc_moe_ffn: injected failure");
+
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    auto i32 = [&](size_t off) { return reinterpret_cast<int32_t*>(w + off); };
+    int32_t *idx = i32(L.idx), *counts = i32(L.counts), *offsets = i32(L.offsets);
+    int32_t *rank = i32(L.rank), *pos = i32(L.pos), *row_token = i32(L.row_token);
+    int32_t *xs = i32(L.xs), *hs = i32(L.hs);
+    float* wts = reinterpret_cast<float*>(w + L.wts);
+    __half* xg = reinterpret_cast<__half*>(w + L.xg);
+    float* gu = reinterpret_cast<float*>(w + L.gu);
+    __half* h = reinterpret_cast<__half*>(w + L.h);
+    float* yd = reinterpret_cast<float*>(w + L.yd);
+    const int E = (int)d->n_experts, U = (int)d->top_k, K = (int)d->n_embd, F = (int)d->n_ff;
+    const int R = (int)(T * U);
+
+    moe_route<<<1, kRouteThreads, 0, st>>>(logits, (int)T, E, U, idx, wts, counts, offsets, rank,
+                                           pos, row_token);
+    FTC_CUDA(cudaGetLastError());
+    if (x_dtype == FTC_F32)
+        moe_gather_scale<float><<<R, 256, 0, st>>>(static_cast<const float*>(x), row_token, K, xg, xs);
+    else if (x_dtype == FTC_BF16)
+        moe_gather_scale<__nv_bfloat16><<<R, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(x), row_token, K, xg, xs);
+    else
+        moe_gather_scale<__half><<<R, 256, 0, st>>>(static_cast<const __half*>(x), row_token, K,
+                                                    xg, xs);
+    FTC_CUDA(cudaGetLastError());
+    rc = gemm_q4k_grouped(d->gate_exps, d->up_exps, 2, E, d->gu_plane_stride, F, K,
+                          d->gu_row_stride, xg, FTC_F16, R, counts, offsets, T, gu, FTC_F32,
+                          2 * (int64_t)F, st);
+    if (rc) return rc;
+    {
+        static bool configured = false;
+        const size_t smem = (size_t)F * 4;
+        if (!configured) {
+            FTC_CUDA(cudaFuncSetAttribute(moe_silu_scale, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)(kMaxFf * 4)));
+            configured = true;
+        }
+        moe_silu_scale<<<R, 512, smem, st>>>(gu, xs, F, h, hs);
+        FTC_CUDA(cudaGetLastError());
+    }
+    rc = gemm_q4k_grouped(d->down_exps, nullptr, 1, E, d->dn_plane_stride, K, F, d->dn_row_stride,
+                          h, FTC_F16, R, counts, offsets, T, yd, FTC_F32, K, st);
+    if (rc) return rc;
+    moe_combine<<<grid_for((int64_t)T * K / 4), 256, 0, st>>>(yd, hs, pos, idx, wts, rank, (int)T,
+                                                              U, K, out);
+    FTC_CUDA(cudaGetLastError());
+    return FTC_OK;
+}
+
+}  // namespace ftc

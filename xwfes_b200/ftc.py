@@ -41,6 +41,8 @@ SIGNATURES = {
     "ftc_gemm": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, C.c_int, _i64, _p, C.c_int, _p]),
     "ftc_expert_chunk_static": (C.c_int, [C.c_int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                           _i64, _p]),
+    "ftc_moe_workspace_bytes": (C.c_size_t, [_p, _i64]),
+    "ftc_moe_ffn": (C.c_int, [_p, _p, _p, C.c_int, _i64, _p, _p, C.c_size_t, _p]),
 }
 
 
@@ -55,6 +57,14 @@ class ExpertChunkJob(C.Structure):
     _fields_ = [("x", _p), ("out", _p), ("gate", _p), ("up", _p), ("down", _p),
                 ("dtype", C.c_int), ("M", _i64), ("K", _i64), ("IC", _i64),
                 ("gate_up_row_stride", C.c_size_t), ("down_row_stride", C.c_size_t)]
+
+
+class MoeDesc(C.Structure):
+    """``ftc_moe_desc``: expert weights and shapes of one MoE layer."""
+    _fields_ = [("dtype", C.c_int), ("n_experts", _i64),
+                ("top_k", _i64), ("n_embd", _i64), ("n_ff", _i64), ("gate_exps", _p),
+                ("up_exps", _p), ("down_exps", _p), ("gu_row_stride", _i64),
+                ("gu_plane_stride", _i64), ("dn_row_stride", _i64), ("dn_plane_stride", _i64)]
 
 
 _lib = None
@@ -160,6 +170,69 @@ def gemm(w, dtype, n, k, x, y=None, y_dtype=F.BF16, row_stride=None, stream=None
     check(lib().ftc_gemm(t, w.data_ptr(), n, k, rs, x2.data_ptr(), xt, m, y.data_ptr(), yt,
                          _stream(stream)), "ftc_gemm")
     return y
+
+
+def _align(n, a=256):
+    return (n + a - 1) // a * a
+
+
+class MoeLayer:
+    """One MoE FFN layer on the device (``ftc_moe_ffn``).
+
+    ``gate_exps``/``up_exps``: uint8 CUDA tensors of E planes of n_ff Q4_K rows
+    of n_embd; ``down_exps``: E planes of n_embd rows of n_ff (standard GGUF
+    layout)."""
+
+    def __init__(self, gate_exps, up_exps, down_exps, n_experts, top_k, n_embd, n_ff,
+                 dtype=F.Q4_K):
+        t = F.dtype_id(dtype)
+        gu_rs, dn_rs = row_bytes(t, n_embd), row_bytes(t, n_ff)
+        self._keep = (gate_exps, up_exps, down_exps)
+        self.desc = MoeDesc(t, n_experts, top_k, n_embd, n_ff,
+                            gate_exps.data_ptr(), up_exps.data_ptr(), down_exps.data_ptr(),
+                            gu_rs, gu_rs * n_ff, dn_rs, dn_rs * n_embd)
+        self.n_experts, self.top_k, self.n_embd = n_experts, top_k, n_embd
+        self._ws = None
+
+    def workspace_bytes(self, T):
+        n = int(lib().ftc_moe_workspace_bytes(C.byref(self.desc), T))
+        if n == 0 and T > 0:
+            raise FtcError("ftc_moe_workspace_bytes", -1, last_error())
+        return n
+
+    def workspace(self, T, device="cuda"):
+        import torch
+        n = self.workspace_bytes(T)
+        if self._ws is None or self._ws.numel() < n:
+            self._ws = torch.empty(max(n, 256), dtype=torch.uint8, device=device)
+        return self._ws
+
+    def __call__(self, logits, x, out=None, stream=None):
+        """out[t] = routed-expert FFN of x[t]; logits fp32 [T, E], x [T, n_embd]
+        (fp32, bf16 or fp16 CUDA tensor); returns fp32 [T, n_embd]."""
+        import torch
+        T = x.shape[0]
+        xt = {torch.float32: F.F32, torch.bfloat16: F.BF16, torch.float16: F.F16}[x.dtype]
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device=x.device)
+        ws = self.workspace(T, x.device)
+        check(lib().ftc_moe_ffn(C.byref(self.desc), logits.data_ptr(), x.data_ptr(), xt, T,
+                                out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream)),
+              "ftc_moe_ffn")
+        return out
+
+    def routing(self, T):
+        """(idx [T, U] int32, weights [T, U] fp32, counts [E] int32) of the last
+        call, read from the start of the workspace."""
+        import torch
+        R = T * self.top_k
+        ws = self._ws
+        o_w = _align(R * 4)
+        o_c = o_w + _align(R * 4)
+        idx = ws[:R * 4].view(torch.int32).reshape(T, self.top_k)
+        w = ws[o_w:o_w + R * 4].view(torch.float32).reshape(T, self.top_k)
+        cnt = ws[o_c:o_c + self.n_experts * 4].view(torch.int32)
+        return idx, w, cnt
 
 
 def dequant(w, dtype, n_rows, k, out=None, row_stride=None, stream=None):
