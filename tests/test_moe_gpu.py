@@ -54,6 +54,9 @@ def x_input(T, K, xt, seed, scale=1.0):
     if xt == F.BF16:
         bits = S.f32_to_bf16_bits(x32)
         return torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16), S.bf16_bits_to_f32(bits)
+    if xt == F.F16:
+        x16 = x32.astype(np.float16)
+        return torch.from_numpy(x16), x16.astype(np.float32)
     return torch.from_numpy(x32), x32
 
 
@@ -77,8 +80,10 @@ def test_route_matches_oracle(ftc, oracle, T, E, U):
 # ------------------------------------------------- reduced shapes vs oracle
 
 @pytest.mark.parametrize("xt", [F.BF16, F.F32])
-@pytest.mark.parametrize("T", [1, 5, 64, 300])
+@pytest.mark.parametrize("T", [1, 2, 5, 64, 300])
 def test_moe_vs_oracle(ftc, oracle, T, xt):
+    """T * top_k <= 4 runs the decode path (a GEMV per (token, slot) pair on
+    the experts chosen on the device), larger T the grouped GEMMs."""
     E, U, K, FF = 8, 2, 1024, 2048
     layer, (g, u, d) = make_layer(ftc, E, K, FF, U, seed=5)
     logits = S.router_logits(T, E, seed=T)
@@ -86,6 +91,18 @@ def test_moe_vs_oracle(ftc, oracle, T, xt):
     out = layer(torch.from_numpy(logits).cuda(), x.cuda())
     torch.cuda.synchronize()
     assert ftc.device_status() == 0
+    ref = oracle.moe_ffn(x32, logits, g, u, d, F.Q4_K, K, FF, U, threads=THREADS)
+    assert norm_err(out.cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("T,E,U", [(3, 4, 1), (8, 4, 1), (1, 16, 4)])
+def test_moe_top_k(ftc, oracle, T, E, U):
+    K, FF = 512, 1024
+    layer, (g, u, d) = make_layer(ftc, E, K, FF, U, seed=13)
+    logits = S.router_logits(T, E, seed=5)
+    x, x32 = x_input(T, K, F.F16 if U == 1 else F.BF16, seed=6)
+    out = layer(torch.from_numpy(logits).cuda(), x.cuda())
+    torch.cuda.synchronize()
     ref = oracle.moe_ffn(x32, logits, g, u, d, F.Q4_K, K, FF, U, threads=THREADS)
     assert norm_err(out.cpu().numpy(), ref) <= TOL
 
@@ -122,10 +139,12 @@ def test_moe_input_range(ftc, oracle, scale):
     assert norm_err(out, ref) <= TOL
 
 
-def test_moe_deterministic_and_graph_capturable(ftc):
+@pytest.mark.parametrize("T", [1, 77])
+def test_moe_deterministic_and_graph_capturable(ftc, T):
     """No atomics on the data path: repeated calls agree bit for bit, and the
-    whole layer replays from a CUDA graph (no host round trip inside)."""
-    E, U, K, FF, T = 8, 2, 1024, 1024, 77
+    whole layer replays from a CUDA graph (no host round trip inside), for
+    the decode path (T=1) and the grouped-GEMM path."""
+    E, U, K, FF = 8, 2, 1024, 1024
     layer, _ = make_layer(ftc, E, K, FF, U, seed=12)
     logits = torch.from_numpy(S.router_logits(T, E, seed=2)).cuda()
     x = x_input(T, K, F.BF16, seed=5)[0].cuda()

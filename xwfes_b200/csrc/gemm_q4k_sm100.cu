@@ -73,19 +73,22 @@ struct XMaps {
 
 constexpr int BM = 128;       // weight rows per tile (MMA M)
 constexpr int BK = 64;        // k per stage: one 128-byte swizzle row of 16-bit values
-constexpr int kRawSlots = 3;  // raw super-block ring (12 k-steps of lookahead)
 constexpr int kRawBytes = BM * 144;
-constexpr int kThreads = 15 * 32;
-constexpr int kRawWarp = 14;  // issues the raw weight tiles
-constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 4;
+constexpr int kTeamWarps = 8;  // dequant warps per team
 
-template <int BN>
+// Kernel shape.  DT dequant teams of 8 warps take alternate super-blocks;
+// each team has its own NAT-stage slice of the dequantized weight ring and
+// its own RAWT-slot slice of the raw ring, so every ring has one producer and
+// one consumer and an mbarrier is never waited on more than one phase ahead.
+template <int BN_, int DT_, int NAT_, int NB_, int RAWT_>
 struct Cfg {
-    // Separate rings: activation tiles come from L2/HBM by TMA and need deep
-    // lookahead; dequantized weight tiles are made on chip and need two.
-    static constexpr int NA = 3;                  // dequantized weight stages
-    static constexpr int NB = BN == 256 ? 3 : 5;  // activation stages
+    static constexpr int BN = BN_, DT = DT_, NAT = NAT_, NB = NB_, RAWT = RAWT_;
+    static constexpr int NA = DT * NAT;           // dequantized weight stages
+    static constexpr int RAW = DT * RAWT;         // raw super-block slots
+    static constexpr int WARPS = 2 + kEpiWarps + DT * kTeamWarps + 1;
+    static constexpr int THREADS = 32 * WARPS;
+    static constexpr int RAW_WARP = WARPS - 1;    // issues the raw weight tiles
     static constexpr int A_BYTES = BM * BK * 2;   // 16 KB
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int TMEM_COLS = 2 * BN;      // two accumulators
@@ -93,13 +96,31 @@ struct Cfg {
     static constexpr int OFF_A = 0;
     static constexpr int OFF_B = OFF_A + NA * A_BYTES;
     static constexpr int OFF_RAW = OFF_B + NB * B_BYTES;
-    static constexpr int OFF_BAR = OFF_RAW + kRawSlots * kRawBytes;
-    // barriers: a_full[NA] a_empty[NA] b_full[NB] b_empty[NB] raw_full[R]
-    // raw_empty[R] acc_full[2] acc_empty[2]
-    static constexpr int N_BARS = 2 * NA + 2 * NB + 2 * kRawSlots + 4;
+    static constexpr int OFF_BAR = OFF_RAW + RAW * kRawBytes;
+    // barriers: a_full[NA] a_empty[NA] b_full[NB] b_empty[NB] raw_full[RAW]
+    // raw_empty[RAW] acc_full[2] acc_empty[2]
+    static constexpr int N_BARS = 2 * NA + 2 * NB + 2 * RAW + 4;
     // tile schedule: first tile, first row and row count of each group
     static constexpr int OFF_SCHED = OFF_BAR + N_BARS * 8 + 16;
     static constexpr int SMEM = OFF_SCHED + (3 * kGemmMaxGroups + 1) * 4 + 1024;  // +1024: alignment slack
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+// Ring positions of super-block rc (in kernel order) and its k-step g: the
+// owning team, its raw slot and that slot's phase, and the A stage / phase.
+template <class C>
+struct RingPos {
+    int team, raw_slot, a_stage;
+    uint32_t raw_phase, a_phase;
+    __device__ __forceinline__ RingPos(uint32_t rc, int g) {
+        team = (int)(rc % C::DT);
+        const uint32_t lr = rc / C::DT;            // team-local super-block
+        raw_slot = team * C::RAWT + (int)(lr % C::RAWT);
+        raw_phase = (lr / C::RAWT) & 1;
+        const uint32_t la = lr * 4 + (uint32_t)g;  // team-local k-step
+        a_stage = team * C::NAT + (int)(la % C::NAT);
+        a_phase = (la / C::NAT) & 1;
+    }
 };
 
 // Tile t of the schedule: group, weight set, 128-row block of W, and the
@@ -263,12 +284,12 @@ __device__ __forceinline__ void store_out(void* y, int ytype, int64_t idx, float
     else reinterpret_cast<__half*>(y)[idx] = __float2half_rn(v);
 }
 
-template <int BN, typename OP>
-__global__ void __launch_bounds__(kThreads, 1)
+template <class C, typename OP>
+__global__ void __launch_bounds__(C::THREADS, 1)
 gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
             const __grid_constant__ XMaps tm_x, int M, int N, int K, void* __restrict__ y,
             int ytype, const GemmGroups grp) {
-    using C = Cfg<BN>;
+    constexpr int BN = C::BN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -281,8 +302,8 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     uint64_t* b_full = a_empty + C::NA;
     uint64_t* b_empty = b_full + C::NB;
     uint64_t* raw_full = b_empty + C::NB;
-    uint64_t* raw_empty = raw_full + kRawSlots;
-    uint64_t* acc_full = raw_empty + kRawSlots;
+    uint64_t* raw_empty = raw_full + C::RAW;
+    uint64_t* acc_full = raw_empty + C::RAW;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::N_BARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -301,16 +322,16 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::NA; ++s) {
-            mbar_init(&a_full[s], kDequantWarps);
+            mbar_init(&a_full[s], kTeamWarps);
             mbar_init(&a_empty[s], 1);
         }
         for (int s = 0; s < C::NB; ++s) {
             mbar_init(&b_full[s], 1);
             mbar_init(&b_empty[s], 1);
         }
-        for (int s = 0; s < kRawSlots; ++s) {
+        for (int s = 0; s < C::RAW; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], kDequantWarps);
+            mbar_init(&raw_empty[s], kTeamWarps);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
@@ -367,7 +388,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                     mbar_wait(&b_full[j % C::NB], (j / C::NB) & 1);
             }
         }
-    } else if (warp == kRawWarp) {
+    } else if (warp == C::RAW_WARP) {
         // ------------------------------------------------------ raw TMA
         // Raw weight tiles run up to kRawSlots super-blocks ahead of the
         // dequant warps, independent of the activation ring.
@@ -380,17 +401,19 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 const TileRef t = tile_at(tile);
                 const CUtensorMap* wm = t.set ? &tm_w2 : &tm_w;
                 for (int sb = 0; sb < nsb; ++sb) {
-                    const int rs = rc % kRawSlots;
-                    if (!mbar_wait(&raw_empty[rs], ((rc / kRawSlots) & 1) ^ 1)) { *abort_flag = 1; break; }
-                    mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
-                    tma_load_3d(sRaw + rs * kRawBytes, wm, sb * 144, t.nt * BM, t.g, &raw_full[rs],
-                                pol_w);
+                    const RingPos<C> rp(rc, 0);
+                    if (!mbar_wait(&raw_empty[rp.raw_slot], rp.raw_phase ^ 1)) { *abort_flag = 1; break; }
+                    mbar_arrive_expect_tx(&raw_full[rp.raw_slot], kRawBytes);
+                    tma_load_3d(sRaw + rp.raw_slot * kRawBytes, wm, sb * 144, t.nt * BM, t.g,
+                                &raw_full[rp.raw_slot], pol_w);
                     ++rc;
                 }
             }
-            if (*abort_flag) {
-                for (uint32_t j = rc > (uint32_t)kRawSlots ? rc - kRawSlots : 0; j < rc; ++j)
-                    mbar_wait(&raw_full[j % kRawSlots], (j / kRawSlots) & 1);
+            if (*abort_flag) {  // let issued copies land before the CTA leaves
+                for (uint32_t j = rc > (uint32_t)C::RAW ? rc - C::RAW : 0; j < rc; ++j) {
+                    const RingPos<C> rp(j, 0);
+                    mbar_wait(&raw_full[rp.raw_slot], rp.raw_phase);
+                }
             }
         }
     } else if (warp == 1) {
@@ -407,8 +430,9 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
                 for (int ks = 0; ks < nsb * 4; ++ks) {
-                    const int sa = kc % C::NA, s = kc % C::NB;
-                    if (!mbar_wait(&a_full[sa], (kc / C::NA) & 1) ||
+                    const RingPos<C> rp(kc >> 2, (int)(kc & 3));
+                    const int sa = rp.a_stage, s = kc % C::NB;
+                    if (!mbar_wait(&a_full[sa], rp.a_phase) ||
                         !mbar_wait(&b_full[s], (kc / C::NB) & 1)) {
                         *abort_flag = 1;
                         break;
@@ -461,22 +485,32 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         }
     } else {
         // ---------------------------------------------------------- dequant
-        const int p = threadIdx.x - (2 + kEpiWarps) * 32;  // 0..255
-        const int r = p >> 1, h = p & 1;                   // weight row in tile, half of group
+        const int dw = warp - (2 + kEpiWarps);
+        const int team = dw / kTeamWarps;
+        // warp covers rows 16*wi .. 16*wi + 15, both halves of the group; a
+        // quarter-warp takes 8 consecutive rows of one half, so its 16-byte
+        // stores hit 8 different swizzled chunks (all 32 banks) and its raw
+        // loads (rows 144 bytes apart) 8 different bank quads
+        const int wi = dw % kTeamWarps;
+        const int h = (lane >> 3) & 1;                             // half of the group
+        const int r = 16 * wi + 8 * (lane >> 4) + (lane & 7);      // weight row in tile
         const int swz = r & 7;
-        uint32_t kc = 0, rc = 0;
+        uint32_t rc = 0;  // super-blocks in kernel order; this team takes rc % DT == team
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            for (int sb = 0; sb < nsb; ++sb) {
-                const int rs = rc % kRawSlots;
-                if (!mbar_wait_warp(&raw_full[rs], (rc / kRawSlots) & 1)) { *abort_flag = 1; break; }
+            for (int sb = 0; sb < nsb; ++sb, ++rc) {
+                if ((int)(rc % C::DT) != team) continue;
+                const RingPos<C> rp0(rc, 0);
+                const int rs = rp0.raw_slot;
+                if (!mbar_wait_warp(&raw_full[rs], rp0.raw_phase)) { *abort_flag = 1; break; }
                 const uint8_t* blk = sRaw + rs * kRawBytes + r * 144;
                 float fdl[8], fnml[8];      // per sub-block: d*sc, -dmin*m
                 uint32_t dl2[8], nml2[8];   // the same as fp16 pairs (fp16 operands)
                 decode_scales<OP>(*reinterpret_cast<const uint4*>(blk), fdl, fnml, dl2, nml2);
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
-                    const int s = kc % C::NA;
-                    if (!mbar_wait_warp(&a_empty[s], ((kc / C::NA) & 1) ^ 1)) { *abort_flag = 1; break; }
+                    const RingPos<C> rp(rc, g);
+                    const int s = rp.a_stage;
+                    if (!mbar_wait_warp(&a_empty[s], rp.a_phase ^ 1)) { *abort_flag = 1; break; }
                     const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g + 16 * h);
                     const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
                     uint32_t lo[8], hi[8];  // packed pairs, k = 16h + 2i (+32 for hi)
@@ -501,11 +535,9 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&a_full[s]);
-                    ++kc;
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_empty[rs]);
-                ++rc;
                 if (*abort_flag) break;
             }
             if (*abort_flag) break;
@@ -534,13 +566,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <int BN, typename OP>
+template <class C, typename OP>
 int launch(const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx, int M, int N, int K,
            void* y, int ytype, const GemmGroups& grp, int64_t max_tiles, cudaStream_t st) {
-    using C = Cfg<BN>;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc<BN, OP>,
+        cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc<C, OP>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm_q4k_tc)");
         configured = true;
@@ -548,7 +579,7 @@ int launch(const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx, int M
     static int sms = 0;
     if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sms));
-    gemm_q4k_tc<BN, OP><<<grid, kThreads, C::SMEM, st>>>(tw, tw2, tx, M, N, K, y, ytype, grp);
+    gemm_q4k_tc<C, OP><<<grid, C::THREADS, C::SMEM, st>>>(tw, tw2, tx, M, N, K, y, ytype, grp);
     return FTC_OK;
 }
 
@@ -595,13 +626,15 @@ int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2,
              int M, int N, int K, void* y, int y_dtype, const GemmGroups& grp, int64_t max_tiles,
              cudaStream_t st) {
     const bool bf = x_dtype == FTC_BF16;
+    using C128 = Cfg<128, 1, 3, 5, 3>;
+    using C256 = Cfg<256, 1, 3, 3, 3>;
     int rc;
     if (BN == 128)
-        rc = bf ? launch<128, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
-                : launch<128, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
+        rc = bf ? launch<C128, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
+                : launch<C128, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
     else
-        rc = bf ? launch<256, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
-                : launch<256, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
+        rc = bf ? launch<C256, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
+                : launch<C256, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
     if (rc != FTC_OK) return rc;
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;

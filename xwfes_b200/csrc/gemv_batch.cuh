@@ -1,0 +1,34 @@
+// gemv_batch.cuh -- host description of a batched Q4_K decode GEMV launch
+// (gemv_q4k.cu), shared with the MoE decode path (moe.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ftc {
+
+constexpr int kGemvMaxMats = 8;
+
+// P matrices with the same K and row pitch in one launch:
+//   y_p[n] = sum_k x_p[k] * W_p[n][k]
+// x_p = x[0] for every p unless per_matrix_x.  With sel set, matrix p with
+// sel_slot[p] >= 0 starts at W[p] + sel[sel_slot[p]] * sel_stride (expert
+// ids read on the device after the preceding kernel, clamped to [0, sel_max]).
+struct GemvSpec {
+    int P;
+    int64_t K, stride;
+    const uint8_t* W[kGemvMaxMats];
+    int64_t N[kGemvMaxMats];
+    float* y[kGemvMaxMats];
+    const float* x[kGemvMaxMats];
+    int per_matrix_x;
+    const int32_t* sel;
+    int64_t sel_stride;
+    int sel_max;
+    int sel_slot[kGemvMaxMats];
+};
+
+// FTC_E_UNSUPPORTED when the shape or alignment does not fit the kernel.
+int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st);
+
+}  // namespace ftc

@@ -33,13 +33,12 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemv_batch.cuh"
 #include "sm100.cuh"
 
 namespace ftc {
 
 FTC_DEVSTAT_READER(devstat_gemv_q4k)
-
-constexpr int kGemvMaxMats = 8;
 
 namespace {
 
@@ -49,14 +48,28 @@ constexpr int kMaxThreads = 608; // 18 consumer warps + 1 producer at <= 107 reg
 
 }  // namespace
 
-// Up to kGemvMaxMats weight matrices with the same K that read the same
-// activation vector (q/k/v, gate/up): one launch walks all their row chunks.
+// Up to kGemvMaxMats weight matrices with the same K in one launch.
+//  * shared activations (q/k/v, gate/up): every CTA walks all row chunks of
+//    all matrices with x[0];
+//  * per-matrix activations (per_matrix_x): CTAs [cta_first[p],
+//    cta_first[p+1]) serve matrix p only, with x[p] (MoE experts, each with
+//    its own token or hidden vector).
+// Device-side expert selection: when sel is set, matrix p with
+// sel_slot[p] >= 0 starts at W[p] + sel[sel_slot[p]] * sel_stride (the id
+// clamped to [0, sel_max]); sel is read after the preceding kernel finishes.
 struct GemvBatch {
     const uint8_t* W[kGemvMaxMats];
     float* y[kGemvMaxMats];
+    const float* x[kGemvMaxMats];
     int N[kGemvMaxMats];
     int first_chunk[kGemvMaxMats + 1];  // prefix sums of ceil(N / RC)
+    int cta_first[kGemvMaxMats + 1];    // per-matrix activations: CTA ranges
     int P;
+    int per_matrix_x;
+    const int32_t* sel;
+    int64_t sel_stride;
+    int sel_max;
+    int sel_slot[kGemvMaxMats];
 };
 
 namespace {
@@ -206,10 +219,44 @@ __device__ __forceinline__ int chunk_matrix(const GemvBatch& B, int c) {
     return p;
 }
 
+// This CTA's chunks: c0, c0 + step, ... < cend (global chunk indices), and
+// the activation vector they use.
+struct ChunkWalk {
+    int c0, step, cend;
+    const float* x;
+};
+
+__device__ __forceinline__ ChunkWalk chunk_walk(const GemvBatch& B) {
+    ChunkWalk w;
+    if (!B.per_matrix_x) {
+        w.c0 = blockIdx.x;
+        w.step = gridDim.x;
+        w.cend = B.first_chunk[B.P];
+        w.x = B.x[0];
+    } else {
+        int p = 0;
+        while (p + 1 < B.P && (int)blockIdx.x >= B.cta_first[p + 1]) ++p;
+        w.c0 = B.first_chunk[p] + ((int)blockIdx.x - B.cta_first[p]);
+        w.step = B.cta_first[p + 1] - B.cta_first[p];
+        w.cend = B.first_chunk[p + 1];
+        w.x = B.x[p];
+    }
+    return w;
+}
+
+__device__ __forceinline__ const uint8_t* matrix_base(const GemvBatch& B, int p) {
+    const uint8_t* w = B.W[p];
+    if (B.sel && B.sel_slot[p] >= 0) {
+        const int e = min(max(B.sel[B.sel_slot[p]], 0), B.sel_max);
+        w += (int64_t)e * B.sel_stride;
+    }
+    return w;
+}
+
 template <int RPW>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int WK, int WR,
-              int RC, const float* __restrict__ x) {
+              int RC) {
     extern __shared__ __align__(128) uint8_t smem[];
     // RC rows per chunk (<= RPW * WR, chosen by the host to balance CTAs);
     // stages and partial slots are sized for RPW * WR rows
@@ -235,17 +282,18 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
     }
     __syncthreads();
     grid_launch_dependents();
-    const int nchunks = B.first_chunk[B.P];
+    const ChunkWalk cw = chunk_walk(B);
 
     if (warp == NCW) {
         // ------------------------------------------------ producer warp
-        // (weights do not depend on the preceding kernel: no dependency wait)
+        // (weights do not depend on the preceding kernel, the expert ids do)
+        if (B.sel) grid_dependency_wait();
         const uint64_t pol = policy_evict_first();
         bool ok = true;
         int it = 0;
         auto reduce = [&](int j) {  // partials of iteration j -> y
             const int s = j % kStages, rd = (j / kStages) & 1;
-            const int c = blockIdx.x + j * gridDim.x;
+            const int c = cw.c0 + j * cw.step;
             const int p = chunk_matrix(B, c);
             const int lc = c - B.first_chunk[p];
             const int rows = min(RC, B.N[p] - lc * RC);
@@ -263,12 +311,12 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
                 const int rows = min(RC, B.N[p] - lc * RC);
                 const uint32_t bytes = (uint32_t)(rows * stride);
                 mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_g2s(stg + s * stage_bytes, B.W[p] + (int64_t)lc * RC * stride, bytes, &full[s],
-                         pol);
+                bulk_g2s(stg + s * stage_bytes, matrix_base(B, p) + (int64_t)lc * RC * stride, bytes,
+                         &full[s], pol);
             }
             __syncwarp();
         };
-        for (int c = blockIdx.x; c < nchunks; c += gridDim.x, ++it) {
+        for (int c = cw.c0; c < cw.cend; c += cw.step, ++it) {
             const int s = it % kStages;
             if (it >= kStages) {
                 // consumers are done with iteration it - kStages: refill the
@@ -296,7 +344,7 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
 
     // ---------------------------------------------------- consumer warps
     grid_dependency_wait();  // x may be the preceding kernel's output
-    build_planes(x, nsb, warp, NCW, lane, planes, sums, scales);
+    build_planes(cw.x, nsb, warp, NCW, lane, planes, sums, scales);
     named_barrier(1, NCW * 32);
 
     const int wr = warp / WK, wk = warp % WK;
@@ -328,7 +376,7 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
     // warp only), so the row loop never diverges.
     const int sb_ld = valid ? sb : nsb - 1;
     int it = 0;
-    for (int c = blockIdx.x; c < nchunks; c += gridDim.x, ++it) {
+    for (int c = cw.c0; c < cw.cend; c += cw.step, ++it) {
         const int s = it % kStages, rd = (it / kStages) & 1;
         if (!mbar_wait_warp(&full[s], (it / kStages) & 1)) break;
         const int p = chunk_matrix(B, c);
@@ -414,34 +462,64 @@ int balance_rc(int P, const int64_t* N, int rc_max, int sms) {
 
 }  // namespace
 
-// Fast path for Q4_K, M == 1, over one or more matrices sharing x.  Returns
-// FTC_E_UNSUPPORTED when the shape or alignment does not fit (the caller then
-// uses the general kernels).
-int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y,
-                        int64_t stride, int64_t K, const float* x, cudaStream_t st) {
+// Fast path for Q4_K, M == 1.  Returns FTC_E_UNSUPPORTED when the shape or
+// alignment does not fit (the caller then uses the general kernels).
+int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
+    const int P = g.P;
     if (P < 1 || P > kGemvMaxMats) return FTC_E_UNSUPPORTED;
-    if (stride % 16 || (uintptr_t)x % 16 || K % 256) return FTC_E_UNSUPPORTED;
+    if (g.stride % 16 || g.K % 256) return FTC_E_UNSUPPORTED;
     int64_t ntot = 0;
     for (int i = 0; i < P; ++i) {
-        if ((uintptr_t)W[i] % 16 || N[i] <= 0 || N[i] > (1 << 30)) return FTC_E_UNSUPPORTED;
-        ntot += N[i];
+        if ((uintptr_t)g.W[i] % 16 || g.N[i] <= 0 || g.N[i] > (1 << 30)) return FTC_E_UNSUPPORTED;
+        if ((uintptr_t)g.x[g.per_matrix_x ? i : 0] % 16) return FTC_E_UNSUPPORTED;
+        ntot += g.N[i];
     }
+    if (g.sel && (g.sel_stride % 16 || g.sel_max < 0)) return FTC_E_UNSUPPORTED;
     Q4kPlan p;
-    if (!plan_q4k(ntot, K, stride, p)) return FTC_E_UNSUPPORTED;
+    if (!plan_q4k(ntot, g.K, g.stride, p)) return FTC_E_UNSUPPORTED;
     static int sms = 0;
     if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int RC = balance_rc(P, N, p.RPW * p.WR, sms);
+    const int RC = balance_rc(P, g.N, p.RPW * p.WR, sms);
     GemvBatch B = {};
     B.P = P;
+    B.per_matrix_x = g.per_matrix_x;
+    B.sel = g.sel;
+    B.sel_stride = g.sel_stride;
+    B.sel_max = g.sel_max;
     B.first_chunk[0] = 0;
     for (int i = 0; i < P; ++i) {
-        B.W[i] = W[i];
-        B.y[i] = y[i];
-        B.N[i] = (int)N[i];
-        B.first_chunk[i + 1] = B.first_chunk[i] + (int)((N[i] + RC - 1) / RC);
+        B.W[i] = g.W[i];
+        B.y[i] = g.y[i];
+        B.x[i] = g.x[g.per_matrix_x ? i : 0];
+        B.N[i] = (int)g.N[i];
+        B.sel_slot[i] = g.sel ? g.sel_slot[i] : -1;
+        B.first_chunk[i + 1] = B.first_chunk[i] + (int)((g.N[i] + RC - 1) / RC);
     }
-    p.grid = std::min(B.first_chunk[P], sms);
-    const int nsb = (int)(K / 256);
+    const int nchunks = B.first_chunk[P];
+    p.grid = std::min(nchunks, sms);
+    if (g.per_matrix_x) {
+        // one CTA per matrix, then each further CTA to the matrix with the
+        // most chunks per CTA (no CTA without a chunk)
+        int cnt[kGemvMaxMats], used = P;
+        for (int i = 0; i < P; ++i) cnt[i] = 1;
+        for (const int grid = std::max(p.grid, P); used < grid; ++used) {
+            int best = -1;
+            double load = 0.0;
+            for (int i = 0; i < P; ++i) {
+                const int ch = B.first_chunk[i + 1] - B.first_chunk[i];
+                if (cnt[i] < ch && (double)ch / cnt[i] > load) {
+                    load = (double)ch / cnt[i];
+                    best = i;
+                }
+            }
+            if (best < 0) break;
+            ++cnt[best];
+        }
+        B.cta_first[0] = 0;
+        for (int i = 0; i < P; ++i) B.cta_first[i + 1] = B.cta_first[i] + cnt[i];
+        p.grid = B.cta_first[P];
+    }
+    const int nsb = (int)(g.K / 256);
     // opt in to large dynamic shared memory once per instantiation
     static bool configured[3] = {false, false, false};
     auto launch = [&](auto kern, int idx) -> int {
@@ -461,7 +539,7 @@ int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float*
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, B, stride, nsb, p.WK, p.WR, RC, x);
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, B, g.stride, nsb, p.WK, p.WR, RC);
         if (e != cudaSuccess) return cuda_error(e, "launch gemv_q4k_dp4a");
         return FTC_OK;
     };
@@ -471,6 +549,23 @@ int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float*
     if (rc != FTC_OK) return rc;
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;
+}
+
+// Several matrices sharing x (q/k/v, gate/up).
+int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y,
+                        int64_t stride, int64_t K, const float* x, cudaStream_t st) {
+    if (P < 1 || P > kGemvMaxMats) return FTC_E_UNSUPPORTED;
+    GemvSpec g = {};
+    g.P = P;
+    g.K = K;
+    g.stride = stride;
+    g.x[0] = x;
+    for (int i = 0; i < P; ++i) {
+        g.W[i] = W[i];
+        g.N[i] = N[i];
+        g.y[i] = y[i];
+    }
+    return gemv_q4k_batch(g, st);
 }
 
 int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,

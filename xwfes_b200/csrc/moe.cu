@@ -31,6 +31,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemv_batch.cuh"
 
 namespace ftc {
 
@@ -239,9 +240,9 @@ __global__ void moe_combine(const float* __restrict__ yd, const int32_t* __restr
         for (int j = 0; j < U; ++j) {
             const int u = order[j];
             const float w = wts[t * U + u];
-            const int row = pos[t * U + u];
+            const int row = pos ? pos[t * U + u] : (int)(t * U + u);
             float4 y = reinterpret_cast<const float4*>(yd + (int64_t)row * K)[k4];
-            const float up = exp2i(hs[row]);  // undo the row scale of h (exact)
+            const float up = hs ? exp2i(hs[row]) : 1.f;  // undo the row scale of h (exact)
             y.x *= up;
             y.y *= up;
             y.z *= up;
@@ -255,6 +256,25 @@ __global__ void moe_combine(const float* __restrict__ yd, const int32_t* __restr
     }
 }
 
+// xf = fp32 copy of x (exact for bf16 / fp16)
+template <typename TI>
+__global__ void moe_to_f32(const TI* __restrict__ x, int64_t n, float* __restrict__ xf) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        xf[i] = to_f(x[i]);
+}
+
+// h[r][i] = silu(gu[r][i]) * gu[r][n_ff + i], all fp32
+__global__ void moe_silu_f32(const float* __restrict__ gu, int rows, int n_ff,
+                             float* __restrict__ h) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)rows * n_ff;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / n_ff, c = i - r * n_ff;
+        const float g = gu[r * 2 * n_ff + c];
+        h[i] = g / (1.f + expf(-g)) * gu[r * 2 * n_ff + n_ff + c];
+    }
+}
+
 int grid_for(int64_t n) {
     static int sms = 0;
     if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
@@ -262,6 +282,19 @@ int grid_for(int64_t n) {
 }
 
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+constexpr int64_t kMaxFf = 49152;  // h row kept in shared memory by moe_silu_scale
+
+// Decode (few tokens): every (token, slot) pair is a GEMV over its expert's
+// weights, which streams each chosen expert once at HBM speed; the
+// tensor-core GEMM pays a fixed cost per 128-row MMA that dominates there.
+// (The GEMV covers K up to 15 * 2048.)
+bool decode_path(const ftc_moe_desc& d, int64_t T) {
+    return T * d.top_k * 2 <= kGemvMaxMats && d.n_embd <= 30720 && d.n_ff <= 30720 &&
+           d.gu_row_stride % 16 == 0 &&
+           d.dn_row_stride % 16 == 0 && d.gu_plane_stride % 16 == 0 &&
+           d.dn_plane_stride % 16 == 0;
+}
 
 // Workspace regions, in order (each 256-byte aligned).
 struct MoeLayout {
@@ -281,15 +314,15 @@ MoeLayout moe_layout(const ftc_moe_desc& d, int64_t T) {
     L.row_token = o; o += align256((size_t)R * 4);
     L.xs = o;        o += align256((size_t)R * 4);
     L.hs = o;        o += align256((size_t)R * 4);
-    L.xg = o;        o += align256((size_t)R * d.n_embd * 2);
+    // xg: fp16 rows (GEMM path) or the fp32 tokens (decode path)
+    L.xg = o;        o += align256(std::max((size_t)R * 2, (size_t)T * 4) * d.n_embd);
     L.gu = o;        o += align256((size_t)R * 2 * d.n_ff * 4);
-    L.h = o;         o += align256((size_t)R * d.n_ff * 2);
+    // h: fp16 rows (GEMM path) or fp32 rows (decode path)
+    L.h = o;         o += align256((size_t)R * d.n_ff * (decode_path(d, T) ? 4 : 2));
     L.yd = o;        o += align256((size_t)R * d.n_embd * 4);
     L.total = o;
     return L;
 }
-
-constexpr int64_t kMaxFf = 49152;  // h row kept in shared memory by moe_silu_scale
 
 int check_desc(const ftc_moe_desc* d, const char* who) {
     FTC_REQUIRE(d, FTC_E_INVALID, std::string(who) + ": null descriptor");
@@ -344,6 +377,62 @@ int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dty
     moe_route<<<1, kRouteThreads, 0, st>>>(logits, (int)T, E, U, idx, wts, counts, offsets, rank,
                                            pos, row_token);
     FTC_CUDA(cudaGetLastError());
+    if (decode_path(*d, T)) {
+        // fp32 tokens, then one GEMV launch for gate and up of every (token,
+        // slot) pair, SiLU, one GEMV launch for the pairs' down projections
+        const float* xf = static_cast<const float*>(x);
+        if (x_dtype != FTC_F32) {
+            float* dst = reinterpret_cast<float*>(w + L.xg);
+            const int64_t n = T * (int64_t)K;
+            if (x_dtype == FTC_BF16)
+                moe_to_f32<<<grid_for(n), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, dst);
+            else
+                moe_to_f32<<<grid_for(n), 256, 0, st>>>(static_cast<const __half*>(x), n, dst);
+            FTC_CUDA(cudaGetLastError());
+            xf = dst;
+        }
+        float* h32 = reinterpret_cast<float*>(w + L.h);
+        GemvSpec g = {};
+        g.P = 2 * R;
+        g.K = K;
+        g.stride = d->gu_row_stride;
+        g.per_matrix_x = T > 1;
+        g.sel = idx;
+        g.sel_stride = d->gu_plane_stride;
+        g.sel_max = E - 1;
+        for (int r = 0; r < R; ++r)
+            for (int j = 0; j < 2; ++j) {
+                const int i = 2 * r + j;
+                g.W[i] = static_cast<const uint8_t*>(j ? d->up_exps : d->gate_exps);
+                g.N[i] = F;
+                g.y[i] = gu + (int64_t)r * 2 * F + (int64_t)j * F;
+                g.x[i] = xf + (int64_t)(r / U) * K;
+                g.sel_slot[i] = r;
+            }
+        if ((rc = gemv_q4k_batch(g, st))) return rc;
+        moe_silu_f32<<<grid_for((int64_t)R * F), 256, 0, st>>>(gu, R, F, h32);
+        FTC_CUDA(cudaGetLastError());
+        GemvSpec dn = {};
+        dn.P = R;
+        dn.K = F;
+        dn.stride = d->dn_row_stride;
+        dn.per_matrix_x = R > 1;
+        dn.sel = idx;
+        dn.sel_stride = d->dn_plane_stride;
+        dn.sel_max = E - 1;
+        for (int r = 0; r < R; ++r) {
+            dn.W[r] = static_cast<const uint8_t*>(d->down_exps);
+            dn.N[r] = K;
+            dn.y[r] = yd + (int64_t)r * K;
+            dn.x[r] = h32 + (int64_t)r * F;
+            dn.sel_slot[r] = r;
+        }
+        if ((rc = gemv_q4k_batch(dn, st))) return rc;
+        moe_combine<<<grid_for((int64_t)T * K / 4), 256, 0, st>>>(yd, nullptr, nullptr, idx, wts,
+                                                                  rank, (int)T, U, K, out);
+        FTC_CUDA(cudaGetLastError());
+        return FTC_OK;
+    }
     if (x_dtype == FTC_F32)
         moe_gather_scale<float><<<R, 256, 0, st>>>(static_cast<const float*>(x), row_token, K, xg, xs);
     else if (x_dtype == FTC_BF16)
