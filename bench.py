@@ -288,6 +288,8 @@ def run_ours(args, rank, world, local_rank):
 
     prefill = time_prefill(dev)
     gemm_status = ftc.device_status()
+    tp_block = time_tp(dev, world, rank)
+    moe = time_moe(dev) if world == 1 else None
 
     # max over ranks
     t = torch.tensor([ms, e2e_ms, k_ms], device=dev, dtype=torch.float64)
@@ -352,11 +354,118 @@ def run_ours(args, rank, world, local_rank):
             "api": "ftc_backend_matmul (ft::IBackend::matmul), pinned staging, sync per call",
         },
         "prefill_dequant_gemm": prefill_summary(prefill, gemm_status),
+        "tp_block": tp_block,
+        "moe": moe,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
         "setup_s": round(setup_s, 1),
     }
     return line
+
+
+TP_M = [1, 16, 1024]
+L2_BYTES = 126 * 2**20
+
+
+def time_tp(dev, world, rank, seed=0):
+    """Config 4: the Llama-3-70B-shaped Q4_K block (q, k, v, o, gate, up,
+    down), tensor-parallel over the `world` GPUs (strong scaling: the block's
+    work is split).  Each rank holds its shards (rank_shards); enough weight
+    copies rotate through the timed passes that each pass streams its shards
+    from HBM.  Time per pass = max over ranks (CUDA events, barrier before)."""
+    import torch
+    import torch.distributed as dist
+    from xwfes_b200 import tp
+    d = tp.DIMS_70B
+    ops = tp.CudaOps(dev)
+    shard_b = tp.weight_bytes(d) // world
+    copies = min(4, max(1, -(-2 * L2_BYTES // shard_b)))
+    blocks = [tp.TPBlock.build(d, world, rank, ops, tp.rank_shards(d, world, rank, seed=seed + c))
+              for c in range(copies)]
+    out = {}
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream()
+    for M in TP_M:
+        x = torch.from_numpy(S.activations_f32(M, d["n_embd"], seed=seed, name=f"tp.x{M}")).to(dev)
+        reps = 60 if M <= 16 else 12
+        for i in range(3 * copies):
+            blocks[i % copies].forward(x)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        ev0.record(st)
+        for i in range(reps):
+            blocks[i % copies].forward(x)
+        ev1.record(st)
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1) / reps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = t.item() * 1e3
+        out[str(M)] = {"us": round(us, 1), "tokens_per_s": round(M / (us * 1e-6), 1),
+                       "weight_GBps": round(tp.weight_bytes(d) / (us * 1e-6) / 1e9, 1),
+                       "tflops": round(tp.flops(d, M) / (us * 1e-6) / 1e12, 2)}
+    del blocks
+    return {"workload": "config 4: Llama-3-70B-shaped Q4_K block (q 8192x8192, k/v 1024x8192, "
+                        "o 8192x8192, gate/up 28672x8192, down 8192x28672), fp32 activations",
+            "parallelism": f"tp{world} (column-parallel q/k/v/gate/up, row-parallel o/down, "
+                           "NCCL allreduce of fp32 partials after o and down)",
+            "scaling": "strong (the whole block's work is split over the GPUs)",
+            "weight_bytes": tp.weight_bytes(d), "weight_copies_rotated": copies,
+            "kernels": "M<=8: decode GEMV (fp32); M>8: tcgen05 GEMM on row-scaled fp16",
+            "per_M": out}
+
+
+MOE_T = [1, 64, 1024]
+
+
+def time_moe(dev):
+    """Config 5: Mixtral-8x7B-shaped MoE layer (8 experts, top-2) through
+    ftc_moe_ffn, graph-replayed; L2 flushed (256 MB write) before every timed
+    replay."""
+    import torch
+    from xwfes_b200 import ftc
+    E, U, K, FF = 8, 2, 4096, 14336
+    mk = lambda nm, n, k: torch.from_numpy(
+        S.expert_weights(F.Q4_K, E, n, k, seed=0, name=f"moe.{nm}")).to(dev)
+    layer = ftc.MoeLayer(mk("gate", FF, K), mk("up", FF, K), mk("down", K, FF), n_experts=E,
+                         top_k=U, n_embd=K, n_ff=FF)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    per_expert = 3 * FF * F.row_bytes(F.Q4_K, K)
+    out = {}
+    st = torch.cuda.Stream(device=dev)
+    for T in MOE_T:
+        logits = torch.from_numpy(S.router_logits(T, E, seed=0)).to(dev)
+        x = torch.from_numpy(S.activations_bf16(T, K, seed=0, name="moe.x").view(np.int16)).to(
+            dev).view(torch.bfloat16)
+        with torch.cuda.stream(st):
+            y = layer(logits, x, stream=st)
+            for _ in range(3):
+                layer(logits, x, out=y, stream=st)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                layer(logits, x, out=y, stream=st)
+            ts = []
+            for _ in range(15):
+                flush.add_(1)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                g.replay()
+                e1.record(st)
+                e1.synchronize()
+                ts.append(e0.elapsed_time(e1) * 1e3)
+        used = int((layer.routing(T)[2] > 0).sum().item())
+        us = statistics.median(ts)
+        out[str(T)] = {"us": round(us, 1), "tokens_per_s": round(T / (us * 1e-6), 1),
+                       "experts_used": used,
+                       "weight_GBps": round(used * per_expert / (us * 1e-6) / 1e9, 1),
+                       "tflops": round(2.0 * T * U * 3 * FF * K / (us * 1e-6) / 1e12, 2),
+                       "path": "decode GEMVs" if 2 * T * U <= 8 else "grouped tcgen05 GEMMs"}
+        del g
+    return {"workload": "config 5: 8 experts x Q4_K gate/up 14336x4096 + down 4096x14336, "
+                        "top-2 softmax routing of N(0,1) fp32 logits, bf16 N(0,1) tokens",
+            "api": "ftc_moe_ffn (routing, grouping, expert FFNs, combine on the device)",
+            "per_T": out, "status": ftc.device_status()}
 
 
 PREFILL_SHAPES = [(14336, 4096), (4096, 14336)]

@@ -172,6 +172,24 @@ int ftc_mul_mat_vec_multi(int dtype, int n_mats, const void* const* w, const int
 int ftc_gemm(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x,
              int x_dtype, int64_t M, void* y, int y_dtype, void* stream);
 
+/* The prefill GEMM on fp16 rows produced by ftc_rows_to_f16: output row m is
+ * multiplied by 2^row_exp[m] (exact), undoing the input row's scale.  Same
+ * weight and output rules as ftc_gemm; x16: [M][K] fp16, 16-byte aligned. */
+int ftc_gemm_rowscaled(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
+                       const void* x16, int64_t M, void* y, int y_dtype, const int32_t* row_exp,
+                       void* stream);
+
+/* Activation rows to fp16 tensor-core operands without overflow or loss of
+ * precision: out[m][k] = fp16(x[m][k] * 2^-row_exp[m]), row_exp[m] chosen so
+ * the row's largest magnitude lands in [2^14, 2^15).  x: [rows][ld] in
+ * x_dtype (FTC_F32, FTC_BF16, FTC_F16); out: [rows][K] fp16; K even. */
+int ftc_rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
+                    int32_t* row_exp, void* stream);
+
+/* h[i] = silu(g[i]) * u[i] = g / (1 + exp(-g)) * u in fp32, the expert FFN's
+ * activation (ft/src/cpu_backend.cpp:127). */
+int ftc_silu_mul(const float* g, const float* u, int64_t n, float* h, void* stream);
+
 /* Routed-expert MoE FFN layer on the device: the reference's
  * Engine::Impl::moe_ffn (ft/src/engine.cpp:179-241) after the router matmul,
  * with each expert's FFN (ft/src/cpu_backend.cpp:106-149) in the standard

@@ -61,6 +61,11 @@ int expert_chunk_dev(int dtype, const float* x, float* out, const void* gate, co
 
 int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x, int x_dtype,
              int64_t M, void* y, int y_dtype, cudaStream_t st);
+int gemm_q4k_rowscaled(const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x16,
+                       int64_t M, void* y, int y_dtype, const int32_t* row_exp, cudaStream_t st);
+int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
+                int32_t* row_exp, cudaStream_t st);
+int silu_mul(const float* g, const float* u, int64_t n, float* h, cudaStream_t st);
 size_t moe_workspace_bytes(const ftc_moe_desc* d, int64_t T);
 int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dtype, int64_t T,
             float* out, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -415,6 +420,26 @@ int ftc_gemm(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
              int x_dtype, int64_t M, void* y, int y_dtype, void* stream) {
     FTC_REQUIRE(dtype == FTC_Q4_K, FTC_E_UNSUPPORTED, "ftc_gemm: only Q4_K weights");
     int rc = gemm_q4k(w, N, K, row_stride, x, x_dtype, M, y, y_dtype, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_gemm_rowscaled(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stride,
+                       const void* x16, int64_t M, void* y, int y_dtype, const int32_t* row_exp,
+                       void* stream) {
+    FTC_REQUIRE(dtype == FTC_Q4_K, FTC_E_UNSUPPORTED, "ftc_gemm_rowscaled: only Q4_K weights");
+    int rc = gemm_q4k_rowscaled(w, N, K, row_stride, x16, M, y, y_dtype, row_exp,
+                                (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
+                    int32_t* row_exp, void* stream) {
+    int rc = rows_to_f16(x, x_dtype, rows, K, ld, out, row_exp, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_silu_mul(const float* g, const float* u, int64_t n, float* h, void* stream) {
+    int rc = silu_mul(g, u, n, h, (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

@@ -35,6 +35,10 @@
 // share the tokens; set s writes columns [s*N, (s+1)*N) of Y.  A tile with
 // fewer tokens than BN issues a narrower MMA (N rounded up to 16) and loads a
 // shorter activation box (32, 64, ... rows).
+//
+// Row scales.  With row_exp set, output row m is multiplied by 2^row_exp[m]
+// in the epilogue (exact): callers feed fp16 rows scaled by 2^-row_exp into
+// fp16's range (ftc_rows_to_f16) and get unscaled results.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -61,6 +65,7 @@ struct GemmGroups {
     int G;                   // groups = weight planes
     int n_sets;              // weight tensors sharing the tokens (1, or 2 for gate + up)
     int64_t ldy;             // Y row pitch in elements
+    const int32_t* row_exp;  // optional: Y row m is multiplied by 2^row_exp[m] (exact)
 };
 
 namespace {
@@ -472,6 +477,13 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 tmem_ld_wait();
                 const int64_t y0 = (int64_t)(t.row0 + c0) * grp.ldy + col;
                 const int jn = min(32, t.rows - c0);
+                if (grp.row_exp) {  // exact power-of-two row scales (warp-uniform branch)
+                    float f = 0.f;
+                    if (lane < jn) f = __uint_as_float((uint32_t)(grp.row_exp[t.row0 + c0 + lane] + 127) << 23);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, f, j));
+                }
                 if (n < N) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
@@ -668,9 +680,34 @@ int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void
     if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm"))) return rc;
     if ((rc = act_maps(&tx, x, x_dtype, M, K, BN, "ftc_gemm"))) return rc;
     if (inject_fail("ftc_gemm")) return set_error(FTC_E_INJECTED, "ftc_gemm: injected failure");
-    const GemmGroups grp = {nullptr, nullptr, 1, 1, N};
+    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, nullptr};
     const int64_t tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
     return dispatch(BN, x_dtype, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles, st);
+}
+
+// Dense GEMM on fp16 rows scaled by 2^-row_exp (ftc_rows_to_f16), output
+// rows scaled back by 2^row_exp.
+int gemm_q4k_rowscaled(const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x16,
+                       int64_t M, void* y, int y_dtype, const int32_t* row_exp, cudaStream_t st) {
+    FTC_REQUIRE(w && x16 && y && row_exp, FTC_E_INVALID, "ftc_gemm_rowscaled: null pointer");
+    FTC_REQUIRE(M > 0 && N > 0 && K > 0 && K % 256 == 0, FTC_E_INVALID,
+                "ftc_gemm_rowscaled: bad shape (K must be a multiple of 256)");
+    FTC_REQUIRE(M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX, FTC_E_INVALID,
+                "ftc_gemm_rowscaled: shape too large");
+    int rc = check_types(FTC_F16, y_dtype, "ftc_gemm_rowscaled");
+    if (rc) return rc;
+    FTC_REQUIRE(row_stride >= (K / 256) * 144 && row_stride % 16 == 0 && (uintptr_t)w % 16 == 0 &&
+                    (uintptr_t)x16 % 16 == 0,
+                FTC_E_INVALID, "ftc_gemm_rowscaled: operands must be 16-byte aligned");
+    const int BN = M <= 128 ? 128 : 256;
+    CUtensorMap tw;
+    XMaps tx;
+    if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm_rowscaled")))
+        return rc;
+    if ((rc = act_maps(&tx, x16, FTC_F16, M, K, BN, "ftc_gemm_rowscaled"))) return rc;
+    GemmGroups grp = {nullptr, nullptr, 1, 1, N, row_exp};
+    const int64_t tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
+    return dispatch(BN, FTC_F16, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles, st);
 }
 
 // Grouped form: rows of x are grouped by expert (device counts / offsets);
@@ -706,7 +743,7 @@ int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64
         (rc = weight_map(&tw2, w2, N, K, row_stride, G, plane_stride, "gemm_q4k_grouped")))
         return rc;
     if ((rc = act_maps(&tx, x, x_dtype, rows, K, BN, "gemm_q4k_grouped"))) return rc;
-    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy};
+    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy, nullptr};
     // upper bound on tiles: every non-empty group adds at most one partial token tile
     const int64_t tok_tiles = (rows + BN - 1) / BN + std::min<int64_t>(G, rows);
     const int64_t tiles = tok_tiles * ((N + BM - 1) / BM) * n_sets;

@@ -41,6 +41,10 @@ SIGNATURES = {
     "ftc_gemm": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, C.c_int, _i64, _p, C.c_int, _p]),
     "ftc_expert_chunk_static": (C.c_int, [C.c_int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                           _i64, _p]),
+    "ftc_gemm_rowscaled": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, C.c_int, _p,
+                                     _p]),
+    "ftc_rows_to_f16": (C.c_int, [_p, C.c_int, _i64, _i64, _i64, _p, _p, _p]),
+    "ftc_silu_mul": (C.c_int, [_p, _p, _i64, _p, _p]),
     "ftc_moe_workspace_bytes": (C.c_size_t, [_p, _i64]),
     "ftc_moe_ffn": (C.c_int, [_p, _p, _p, C.c_int, _i64, _p, _p, C.c_size_t, _p]),
 }
@@ -170,6 +174,48 @@ def gemm(w, dtype, n, k, x, y=None, y_dtype=F.BF16, row_stride=None, stream=None
     check(lib().ftc_gemm(t, w.data_ptr(), n, k, rs, x2.data_ptr(), xt, m, y.data_ptr(), yt,
                          _stream(stream)), "ftc_gemm")
     return y
+
+
+def rows_to_f16(x, out=None, row_exp=None, stream=None):
+    """fp16 copy of the rows of ``x`` (fp32 / bf16 / fp16 CUDA tensor [M, K]),
+    each scaled by 2**-row_exp[m] into fp16's range; returns (out, row_exp)."""
+    import torch
+    x2 = x.reshape(x.shape[0], -1)
+    m, k = x2.shape
+    xt = {torch.float32: F.F32, torch.bfloat16: F.BF16, torch.float16: F.F16}[x2.dtype]
+    if out is None:
+        out = torch.empty((m, k), dtype=torch.float16, device=x.device)
+    if row_exp is None:
+        row_exp = torch.empty((m,), dtype=torch.int32, device=x.device)
+    check(lib().ftc_rows_to_f16(x2.data_ptr(), xt, m, k, x2.stride(0), out.data_ptr(),
+                                row_exp.data_ptr(), _stream(stream)), "ftc_rows_to_f16")
+    return out, row_exp
+
+
+def gemm_rowscaled(w, dtype, n, k, x16, row_exp, y=None, y_dtype=F.F32, row_stride=None,
+                   stream=None):
+    """y = (x16 @ W^T) with row m multiplied by 2**row_exp[m]: the GEMM on the
+    output of :func:`rows_to_f16`, giving the unscaled product."""
+    import torch
+    t = F.dtype_id(dtype)
+    m = x16.shape[0]
+    yt = F.dtype_id(y_dtype)
+    if y is None:
+        y = torch.empty((m, n), dtype=getattr(torch, _TORCH_OUT[yt]), device=x16.device)
+    rs = row_stride if row_stride is not None else row_bytes(t, k)
+    check(lib().ftc_gemm_rowscaled(t, w.data_ptr(), n, k, rs, x16.data_ptr(), m, y.data_ptr(), yt,
+                                   row_exp.data_ptr(), _stream(stream)), "ftc_gemm_rowscaled")
+    return y
+
+
+def silu_mul(g, u, out=None, stream=None):
+    """silu(g) * u elementwise (fp32 CUDA tensors)."""
+    import torch
+    if out is None:
+        out = torch.empty_like(g)
+    check(lib().ftc_silu_mul(g.data_ptr(), u.data_ptr(), g.numel(), out.data_ptr(),
+                             _stream(stream)), "ftc_silu_mul")
+    return out
 
 
 def _align(n, a=256):

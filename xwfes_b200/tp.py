@@ -1,0 +1,175 @@
+"""Tensor-parallel Llama-3-70B-shaped linear block (config 4), one process per
+GPU, NCCL over NVLink for the exchange.
+
+The reference engine runs every layer in one process (ft/src/engine.cpp:
+485-600: q/k/v, o, gate/up, down matmuls through IBackend::matmul); this is
+the same chain of Q4_K matmuls split across G GPUs:
+
+  column-parallel  q, k, v, gate, up: rank r holds rows [r*N/G, (r+1)*N/G)
+                   of W, computes that slice of the outputs, no exchange;
+  row-parallel     o, down: rank r holds the 256-aligned column slice
+                   [r*K/G, (r+1)*K/G) of every row (whole GGUF super-blocks,
+                   K/G a multiple of 256), multiplies the matching slice of
+                   its input, and the partial [M, n_embd] outputs are summed
+                   by an allreduce.
+
+  h   = allreduce_r( q_r . o_r )              (q_r stands in for the rank's
+                                               attention heads: attention is
+                                               not part of this path)
+  a_r = silu(h . gate_r) * (h . up_r)
+  out = allreduce_r( a_r . down_r )
+
+Every rank uploads only its own shard (contiguous GGUF blocks; a K slice of a
+row is a run of whole super-blocks).  Matmuls: M <= 8 tokens use the decode
+GEMV (fp32 activations), larger M the tcgen05 GEMM on fp16 rows with
+power-of-two row scales (ftc_rows_to_f16 / ftc_gemm_rowscaled), fp32 outputs.
+The allreduce sums fp32 partials (NCCL on GPUs; any torch.distributed group).
+
+The compute is injected (``ops``): :class:`CudaOps` runs the library's
+kernels; tests run the same orchestration with the CPU oracle under gloo.
+"""
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import formats as F, synth as S
+
+# config 4: Llama-3-70B layer shapes
+DIMS_70B = {"n_embd": 8192, "n_ff": 28672, "n_q": 8192, "n_kv": 1024}
+QK = 256  # Q4_K super-block
+
+
+def col_rows(n, G, r):
+    """Rows [r0, r1) of an n-row column-parallel weight held by rank r."""
+    if n % G:
+        raise ValueError(f"{n} rows do not split evenly over {G} ranks")
+    return r * n // G, (r + 1) * n // G
+
+
+def k_slice(k, G, r):
+    """Columns [k0, k1) of a row-parallel weight held by rank r; whole
+    super-blocks only."""
+    if k % (G * QK):
+        raise ValueError(f"K={k} does not split into whole super-blocks over {G} ranks")
+    return r * k // G, (r + 1) * k // G
+
+
+def shard_rows(w, n, G, r):
+    r0, r1 = col_rows(n, G, r)
+    return np.ascontiguousarray(w[r0:r1])
+
+
+def shard_k(w, k, G, r, dtype=F.Q4_K):
+    """The rank's K slice of every row as contiguous rows of whole blocks."""
+    eb, bb = F.BLOCK[F.dtype_id(dtype)]
+    k0, k1 = k_slice(k, G, r)
+    return np.ascontiguousarray(w[:, (k0 // eb) * bb:(k1 // eb) * bb])
+
+
+# (name, rows N, cols K, kind) of the block's weights
+def layout(d):
+    return [("q", d["n_q"], d["n_embd"], "col"), ("k", d["n_kv"], d["n_embd"], "col"),
+            ("v", d["n_kv"], d["n_embd"], "col"), ("o", d["n_embd"], d["n_q"], "row"),
+            ("gate", d["n_ff"], d["n_embd"], "col"), ("up", d["n_ff"], d["n_embd"], "col"),
+            ("down", d["n_embd"], d["n_ff"], "row")]
+
+
+def full_weights(d, seed=0):
+    """Unsharded synthetic Q4_K weights of one block (host uint8 arrays)."""
+    return {nm: S.weight(F.Q4_K, n, k, seed=seed, name=f"tp.{nm}") for nm, n, k, _ in layout(d)}
+
+
+def shard(weights, d, G, r):
+    """Rank r's shards of full weights: {name: (array, rows, cols)}."""
+    out = {}
+    for nm, n, k, kind in layout(d):
+        if kind == "col":
+            r0, r1 = col_rows(n, G, r)
+            out[nm] = (shard_rows(weights[nm], n, G, r), r1 - r0, k)
+        else:
+            k0, k1 = k_slice(k, G, r)
+            out[nm] = (shard_k(weights[nm], k, G, r), n, k1 - k0)
+    return out
+
+
+def rank_shards(d, G, r, seed=0):
+    """Rank r's shards drawn directly (synthetic weights of the right shapes
+    and distributions without building the full block: for benchmarks)."""
+    out = {}
+    for nm, n, k, kind in layout(d):
+        if kind == "col":
+            r0, r1 = col_rows(n, G, r)
+            out[nm] = (S.weight(F.Q4_K, r1 - r0, k, seed=seed, name=f"tp.{nm}.{G}.{r}"), r1 - r0, k)
+        else:
+            k0, k1 = k_slice(k, G, r)
+            out[nm] = (S.weight(F.Q4_K, n, k1 - k0, seed=seed, name=f"tp.{nm}.{G}.{r}"), n, k1 - k0)
+    return out
+
+
+def weight_bytes(d):
+    return sum(F.row_bytes(F.Q4_K, k) * n for _, n, k, _ in layout(d))
+
+
+def flops(d, M):
+    return 2.0 * M * sum(n * k for _, n, k, _ in layout(d))
+
+
+class CudaOps:
+    """The block's matmuls on this GPU through the library's kernels."""
+
+    def __init__(self, device):
+        import torch
+        from . import ftc
+        self.torch, self.ftc, self.device = torch, ftc, device
+
+    def upload(self, arr):
+        return self.torch.from_numpy(arr).to(self.device)
+
+    def matmuls(self, x, ws):
+        """[x . W^T for (W, n, k) in ws], x fp32 [M, k] shared by all."""
+        ftc, M = self.ftc, x.shape[0]
+        k = ws[0][2]
+        if M <= 8:
+            if len(ws) == 1:
+                w, n, _ = ws[0]
+                return [ftc.mul_mat_vec(w, F.Q4_K, n, k, x)]
+            return ftc.mul_mat_vec_multi([w for w, _, _ in ws], F.Q4_K, [n for _, n, _ in ws], k, x)
+        x16, e = ftc.rows_to_f16(x)
+        return [ftc.gemm_rowscaled(w, F.Q4_K, n, k, x16, e) for w, n, _ in ws]
+
+    def silu_mul(self, g, u):
+        return self.ftc.silu_mul(g, u)
+
+
+@dataclass
+class TPBlock:
+    """Rank r of G: its uploaded shards and the forward pass."""
+    dims: dict
+    G: int
+    rank: int
+    ops: object
+    shards: dict
+    group: object = None
+
+    @classmethod
+    def build(cls, dims, G, rank, ops, host_shards, group=None):
+        dev = {nm: (ops.upload(a), n, k) for nm, (a, n, k) in host_shards.items()}
+        return cls(dims, G, rank, ops, dev, group)
+
+    def _allreduce(self, t):
+        if self.G > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        return t
+
+    def forward(self, x):
+        """x: fp32 [M, n_embd] on this rank's device (replicated); returns the
+        block output (fp32 [M, n_embd], identical on every rank) and this
+        rank's q/k/v slices."""
+        W = self.shards
+        q, k, v = self.ops.matmuls(x, [W["q"], W["k"], W["v"]])
+        h = self._allreduce(self.ops.matmuls(q, [W["o"]])[0])
+        g, u = self.ops.matmuls(h, [W["gate"], W["up"]])
+        a = self.ops.silu_mul(g, u)
+        out = self._allreduce(self.ops.matmuls(a, [W["down"]])[0])
+        return out, (q, k, v)
