@@ -176,16 +176,28 @@ def run_ours(args, rank, world, local_rank):
                 xs[X_OF[members[0]]].data_ptr(),
                 (C.c_void_p * P)(*[ys[m].data_ptr() for m in members]))
 
-    def launch(li, gname, s):
+    # prefetch hints: the weight regions of the launch that follows
+    hint_args = {}
+    for li in range(N_LAYERS):
+        for gname, members in GROUPS:
+            P = len(members)
+            hint_args[(li, gname)] = (
+                P, (C.c_void_p * P)(*[dptr[(li, m)] for m in members]),
+                (C.c_int64 * P)(*[SHAPE[m][0] * F.row_bytes(F.Q4_K, SHAPE[m][1]) for m in members]))
+
+    def launch(li, gname, s, nxt=None):
         P, wa, na, k, xp, ya = group_args[(li, gname)]
-        rc = L.ftc_mul_mat_vec_multi(F.Q4_K, P, wa, na, k, F.row_bytes(F.Q4_K, k), xp, 1, ya, s)
+        nn, nw, nb = hint_args[nxt] if nxt else (0, None, None)
+        rc = L.ftc_mul_mat_vec_multi_hint(F.Q4_K, P, wa, na, k, F.row_bytes(F.Q4_K, k), xp, 1, ya,
+                                          nn, nw, nb, s)
         if rc:
-            raise ftc.FtcError("ftc_mul_mat_vec_multi", rc, ftc.last_error())
+            raise ftc.FtcError("ftc_mul_mat_vec_multi_hint", rc, ftc.last_error())
+
+    order = [(li, g) for li in range(N_LAYERS) for g, _ in GROUPS]
 
     def step(s):
-        for li in range(N_LAYERS):
-            for gname, _ in GROUPS:
-                launch(li, gname, s)
+        for i, key in enumerate(order):
+            launch(*key, s, nxt=order[(i + 1) % len(order)])
 
     sp = stream.cuda_stream
     with torch.cuda.stream(stream):
@@ -226,7 +238,7 @@ def run_ours(args, rank, world, local_rank):
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2, stream=stream):
         for li in range(N_LAYERS):
-            launch(li, "gate_up", sp)
+            launch(li, "gate_up", sp, nxt=((li + 1) % N_LAYERS, "gate_up"))
     reps = 200
     with torch.cuda.stream(stream):
         for _ in range(3):
@@ -246,7 +258,7 @@ def run_ours(args, rank, world, local_rank):
         gg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gg, stream=stream):
             for li in range(N_LAYERS):
-                launch(li, gname, sp)
+                launch(li, gname, sp, nxt=((li + 1) % N_LAYERS, gname))
         with torch.cuda.stream(stream):
             for _ in range(3):
                 gg.replay()
@@ -325,7 +337,9 @@ def run_ours(args, rank, world, local_rank):
             "l2": "inputs larger than L2: 8 distinct layer copies (982 MB) per step",
             "parallelism": f"replicas x{world}",
             "graph": "CUDA graph of the step: 8 layers x 4 launches (q/k/v grouped, o, "
-                     "gate/up grouped, down), programmatic dependent launch between them",
+                     "gate/up grouped, down), programmatic dependent launch between them; "
+                     "each launch prefetches the first 24 MB of the next one's weights into L2 "
+                     "(ftc_mul_mat_vec_multi_hint)",
         },
         "pct_of_peak": round(100 * gbs / world / hbm, 1),
         "tokens_per_s": round(world * 1e3 / (ms / N_LAYERS * 32), 1),
@@ -372,7 +386,8 @@ def time_tp(dev, world, rank, seed=0):
     down), tensor-parallel over the `world` GPUs (strong scaling: the block's
     work is split).  Each rank holds its shards (rank_shards); enough weight
     copies rotate through the timed passes that each pass streams its shards
-    from HBM.  Time per pass = max over ranks (CUDA events, barrier before)."""
+    from HBM.  Each pass is a CUDA graph of the forward (NCCL allreduces
+    included).  Time per pass = max over ranks (CUDA events, barrier before)."""
     import torch
     import torch.distributed as dist
     from xwfes_b200 import tp
@@ -385,19 +400,36 @@ def time_tp(dev, world, rank, seed=0):
     out = {}
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     st = torch.cuda.current_stream()
+    cs = torch.cuda.Stream(device=dev)
     for M in TP_M:
         x = torch.from_numpy(S.activations_f32(M, d["n_embd"], seed=seed, name=f"tp.x{M}")).to(dev)
         reps = 60 if M <= 16 else 12
-        for i in range(3 * copies):
-            blocks[i % copies].forward(x)
+        with torch.cuda.stream(cs):
+            for i in range(3 * copies):  # eager warm-up (NCCL, kernel attributes) before capture
+                blocks[i % copies].forward(x)
+        torch.cuda.synchronize()
+        # one CUDA graph per weight copy: the forward's launches and both
+        # allreduces replay without host work in between
+        graphs = []
+        for b in blocks:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cs):
+                b.forward(x)
+            graphs.append(g)
+        with torch.cuda.stream(cs):
+            for i in range(3 * copies):
+                graphs[i % copies].replay()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier(device_ids=[dev.index])
+        st = cs
         ev0.record(st)
-        for i in range(reps):
-            blocks[i % copies].forward(x)
+        with torch.cuda.stream(cs):
+            for i in range(reps):
+                graphs[i % copies].replay()
         ev1.record(st)
         torch.cuda.synchronize()
+        del graphs
         t = torch.tensor([ev0.elapsed_time(ev1) / reps], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)

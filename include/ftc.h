@@ -161,6 +161,19 @@ int ftc_mul_mat_vec_multi(int dtype, int n_mats, const void* const* w, const int
                           int64_t K, int64_t row_stride, const float* x, int64_t M,
                           float* const* y, void* stream);
 
+/* ftc_mul_mat_vec_multi plus a prefetch hint for the launch that follows on
+ * the same stream: next_w[i] / next_bytes[i] (i < n_next <= 8) are the
+ * weight regions that launch reads, in the order it reads them.  Once this
+ * launch has issued its last weight copy, its CTAs pull the first 24 MB of
+ * those regions into L2, so the next launch's first copies hit L2 instead of
+ * waiting on HBM while this one drains (batch 1, Q4_K; otherwise the hint is
+ * ignored).  Regions must stay valid until the next launch has run.  No
+ * counterpart in the reference (it has no device-side pipeline). */
+int ftc_mul_mat_vec_multi_hint(int dtype, int n_mats, const void* const* w, const int64_t* N,
+                               int64_t K, int64_t row_stride, const float* x, int64_t M,
+                               float* const* y, int n_next, const void* const* next_w,
+                               const int64_t* next_bytes, void* stream);
+
 /* Prefill dequant-GEMM on the tcgen05 tensor cores:
  *   y[m][n] = sum_k x[m][k] * W[n][k]      m < M, n < N
  * W: Q4_K rows (16-byte aligned, row_stride % 16 == 0, K % 256 == 0).

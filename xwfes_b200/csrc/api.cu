@@ -54,7 +54,8 @@ int dequant(int dtype, const void* w, int64_t n_rows, int64_t k, int64_t row_str
             cudaStream_t st);
 int mul_mat_vec_multi(int dtype, int P, const void* const* w, const int64_t* N, int64_t K,
                       int64_t row_stride, const float* x, int64_t M, float* const* y,
-                      cudaStream_t st);
+                      cudaStream_t st, int n_next, const void* const* next_w,
+                      const int64_t* next_bytes);
 int expert_chunk_dev(int dtype, const float* x, float* out, const void* gate, const void* up,
                      const void* down, int64_t M, int64_t K, int64_t IC, int64_t gu_stride,
                      int64_t dn_stride, float* gbuf, float* ubuf, float* hbuf, cudaStream_t st);
@@ -412,7 +413,17 @@ int ftc_mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_
 int ftc_mul_mat_vec_multi(int dtype, int n_mats, const void* const* w, const int64_t* N,
                           int64_t K, int64_t row_stride, const float* x, int64_t M,
                           float* const* y, void* stream) {
-    int rc = mul_mat_vec_multi(dtype, n_mats, w, N, K, row_stride, x, M, y, (cudaStream_t)stream);
+    int rc = mul_mat_vec_multi(dtype, n_mats, w, N, K, row_stride, x, M, y, (cudaStream_t)stream,
+                               0, nullptr, nullptr);
+    return rc ? rc : ok();
+}
+
+int ftc_mul_mat_vec_multi_hint(int dtype, int n_mats, const void* const* w, const int64_t* N,
+                               int64_t K, int64_t row_stride, const float* x, int64_t M,
+                               float* const* y, int n_next, const void* const* next_w,
+                               const int64_t* next_bytes, void* stream) {
+    int rc = mul_mat_vec_multi(dtype, n_mats, w, N, K, row_stride, x, M, y, (cudaStream_t)stream,
+                               n_next, next_w, next_bytes);
     return rc ? rc : ok();
 }
 

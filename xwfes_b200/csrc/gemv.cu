@@ -369,7 +369,8 @@ int launch_staged(const uint8_t* W, int64_t stride, int N, int nblk, const float
 int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
                   float* y, cudaStream_t st);
 int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y,
-                        int64_t stride, int64_t K, const float* x, cudaStream_t st);
+                        int64_t stride, int64_t K, const float* x, cudaStream_t st, int n_next,
+                        const uint8_t* const* next_w, const int64_t* next_bytes);
 
 namespace {
 
@@ -428,9 +429,12 @@ int mul_mat_vec(int dtype, const void* w, int64_t N, int64_t K, int64_t row_stri
 
 int mul_mat_vec_multi(int dtype, int P, const void* const* w, const int64_t* N, int64_t K,
                       int64_t row_stride, const float* x, int64_t M, float* const* y,
-                      cudaStream_t st) {
+                      cudaStream_t st, int n_next, const void* const* next_w,
+                      const int64_t* next_bytes) {
     FTC_REQUIRE(P >= 1 && P <= 8, FTC_E_INVALID, "ftc_mul_mat_vec_multi: n_mats must be 1..8");
     FTC_REQUIRE(w && N && y, FTC_E_INVALID, "ftc_mul_mat_vec_multi: null array");
+    FTC_REQUIRE(n_next >= 0 && n_next <= 8 && (n_next == 0 || (next_w && next_bytes)),
+                FTC_E_INVALID, "ftc_mul_mat_vec_multi: prefetch hint needs 0..8 regions");
     if (dtype == FTC_Q4_K && M == 1) {
         bool args_ok = row_stride >= row_bytes(dtype, K) && x != nullptr;
         for (int i = 0; i < P && args_ok; ++i) args_ok = w[i] && y[i] && N[i] > 0;
@@ -438,7 +442,9 @@ int mul_mat_vec_multi(int dtype, int P, const void* const* w, const int64_t* N, 
             if (inject_fail("ftc_mul_mat_vec"))
                 return set_error(FTC_E_INJECTED, "ftc_mul_mat_vec_multi: injected failure");
             const int rc = gemv_q4k_fast_multi(P, reinterpret_cast<const uint8_t* const*>(w), N, y,
-                                               row_stride, K, x, st);
+                                               row_stride, K, x, st, n_next,
+                                               reinterpret_cast<const uint8_t* const*>(next_w),
+                                               next_bytes);
             if (rc != FTC_E_UNSUPPORTED) return rc;
         }
     }

@@ -26,7 +26,17 @@ struct GemvSpec {
     int64_t sel_stride;
     int sel_max;
     int sel_slot[kGemvMaxMats];
+    // Prefetch hint: the weight regions the NEXT launch on the stream reads,
+    // in the order it reads them (its first chunks first).  After issuing its
+    // own last copy, every CTA prefetches its share of their first
+    // kGemvPrefetchWindow bytes into L2, so the next launch starts on L2 hits
+    // while this one drains.
+    int pf_n;
+    const uint8_t* pf_ptr[kGemvMaxMats];
+    int64_t pf_len[kGemvMaxMats];
 };
+
+constexpr int64_t kGemvPrefetchWindow = 24ll << 20;
 
 // FTC_E_UNSUPPORTED when the shape or alignment does not fit the kernel.
 int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st);

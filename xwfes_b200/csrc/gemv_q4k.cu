@@ -70,6 +70,11 @@ struct GemvBatch {
     int64_t sel_stride;
     int sel_max;
     int sel_slot[kGemvMaxMats];
+    // prefetch hint (see GemvSpec): regions of the next launch, window bytes
+    int pf_n;
+    const uint8_t* pf_ptr[kGemvMaxMats];
+    int64_t pf_len[kGemvMaxMats];
+    int64_t pf_total;
 };
 
 namespace {
@@ -329,6 +334,22 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
                 issue(c, s);
             }
         }
+        if (B.pf_n > 0 && lane == 0) {
+            // this CTA's slice of the next launch's first bytes, into L2
+            const int64_t per = ((B.pf_total / gridDim.x) + 15) & ~int64_t(15);
+            int64_t lo = (int64_t)blockIdx.x * per;
+            const int64_t hi = min(lo + per, B.pf_total);
+            int64_t base = 0;
+            for (int r = 0; r < B.pf_n && lo < hi; ++r) {
+                const int64_t end = base + B.pf_len[r];
+                while (lo < hi && lo < end) {
+                    const int64_t n = min(min(hi, end) - lo, (int64_t)1 << 20);
+                    bulk_prefetch_l2(B.pf_ptr[r] + (lo - base), (uint32_t)n);
+                    lo += n;
+                }
+                base = end;
+            }
+        }
         if (ok) {
             for (int j = max(0, it - kStages); j < it; ++j) {
                 if (!mbar_wait_warp(&empty[j % kStages], (j / kStages) & 1)) { ok = false; break; }
@@ -495,6 +516,18 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
         B.sel_slot[i] = g.sel ? g.sel_slot[i] : -1;
         B.first_chunk[i + 1] = B.first_chunk[i] + (int)((g.N[i] + RC - 1) / RC);
     }
+    // prefetch hint: the first kGemvPrefetchWindow bytes of the next launch,
+    // in 16-byte multiples (a region's tail below 16 bytes is left out)
+    B.pf_n = 0;
+    B.pf_total = 0;
+    for (int r = 0; r < g.pf_n && r < kGemvMaxMats && B.pf_total < kGemvPrefetchWindow; ++r) {
+        if (!g.pf_ptr[r] || (uintptr_t)g.pf_ptr[r] % 16 || g.pf_len[r] < 16) continue;
+        const int64_t n = std::min(g.pf_len[r] & ~int64_t(15), kGemvPrefetchWindow - B.pf_total);
+        B.pf_ptr[B.pf_n] = g.pf_ptr[r];
+        B.pf_len[B.pf_n] = n;
+        B.pf_total += n;
+        ++B.pf_n;
+    }
     const int nchunks = B.first_chunk[P];
     p.grid = std::min(nchunks, sms);
     if (g.per_matrix_x) {
@@ -551,9 +584,12 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     return FTC_OK;
 }
 
-// Several matrices sharing x (q/k/v, gate/up).
+// Several matrices sharing x (q/k/v, gate/up); optional prefetch hint for
+// the next launch (n_next regions, see GemvSpec).
 int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y,
-                        int64_t stride, int64_t K, const float* x, cudaStream_t st) {
+                        int64_t stride, int64_t K, const float* x, cudaStream_t st,
+                        int n_next = 0, const uint8_t* const* next_w = nullptr,
+                        const int64_t* next_bytes = nullptr) {
     if (P < 1 || P > kGemvMaxMats) return FTC_E_UNSUPPORTED;
     GemvSpec g = {};
     g.P = P;
@@ -564,6 +600,11 @@ int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float*
         g.W[i] = W[i];
         g.N[i] = N[i];
         g.y[i] = y[i];
+    }
+    g.pf_n = std::min(n_next, kGemvMaxMats);
+    for (int i = 0; i < g.pf_n; ++i) {
+        g.pf_ptr[i] = next_w[i];
+        g.pf_len[i] = next_bytes[i];
     }
     return gemv_q4k_batch(g, st);
 }

@@ -1,7 +1,7 @@
 // sm100.cuh -- thin inline-PTX wrappers for the sm_100a features the kernels
 // use: mbarriers with bounded waits, bulk (TMA) copies, tensor-map loads,
-// and the tcgen05 tensor-memory / MMA instructions.  No cluster multicast
-// form of any load appears anywhere in this library.
+// and the tcgen05 tensor-memory / MMA instructions.  Every copy is issued
+// for the calling CTA alone.
 #pragma once
 
 #include <cuda.h>
@@ -132,6 +132,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
         : "memory");
 }
 
+// Pull [src, src + bytes) into L2 without a destination (16-byte aligned,
+// bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // L2 policy for data read exactly once (streamed weights).
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
@@ -145,7 +151,7 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
     return p;
 }
 
-// 2-D tiled tensor-map load (no multicast): box at (x, y) -> dst_smem.
+// 2-D tiled tensor-map load for this CTA: box at (x, y) -> dst_smem.
 __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar, uint64_t policy) {
     asm volatile(

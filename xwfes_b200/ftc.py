@@ -38,6 +38,9 @@ SIGNATURES = {
     "ftc_mul_mat_vec": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "ftc_mul_mat_vec_multi": (C.c_int, [C.c_int, C.c_int, C.POINTER(_p), C.POINTER(_i64), _i64,
                                         _i64, _p, _i64, C.POINTER(_p), _p]),
+    "ftc_mul_mat_vec_multi_hint": (C.c_int, [C.c_int, C.c_int, C.POINTER(_p), C.POINTER(_i64),
+                                             _i64, _i64, _p, _i64, C.POINTER(_p), C.c_int,
+                                             C.POINTER(_p), C.POINTER(_i64), _p]),
     "ftc_gemm": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, C.c_int, _i64, _p, C.c_int, _p]),
     "ftc_expert_chunk_static": (C.c_int, [C.c_int, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                           _i64, _p]),
