@@ -23,8 +23,11 @@
 //   warps 6-13  dequant: thread (row r, half h) decodes 32 weights of one
 //               64-wide k-step (codes of group g, both nibbles) -- packed fp16
 //               arithmetic for fp16 operands, fp32 with one rounding for bf16
-//               (see dequant_pairs) -- and writes them in the 128-byte-
-//               swizzled K-major layout the MMA reads.
+//               (see dequant_pairs) -- and writes them either in the
+//               128-byte-swizzled K-major shared-memory layout the MMA reads
+//               (256-token tiles), or with tcgen05.st into tensor memory after
+//               the accumulators, where the MMA reads its A operand (128-token
+//               tiles: row r in TMEM lane r, two k per 32-bit column).
 // Every pipeline wait is bounded in time (sm100.cuh); a kernel that gives up
 // records a status and returns.
 //
@@ -70,7 +73,7 @@ struct GemmGroups {
 
 namespace {
 
-constexpr int kXMaps = 4;  // activation boxes of 32, 64, 128, 256 rows (up to BN)
+constexpr int kXMaps = 4;  // activation boxes of 32, 64, 128 and BN rows
 
 struct XMaps {
     CUtensorMap m[kXMaps];
@@ -86,9 +89,13 @@ constexpr int kTeamWarps = 8;  // dequant warps per team
 // each team has its own NAT-stage slice of the dequantized weight ring and
 // its own RAWT-slot slice of the raw ring, so every ring has one producer and
 // one consumer and an mbarrier is never waited on more than one phase ahead.
-template <int BN_, int DT_, int NAT_, int NB_, int RAWT_>
+template <int BN_, int DT_, int NAT_, int NB_, int RAWT_, bool ATM_ = false>
 struct Cfg {
     static constexpr int BN = BN_, DT = DT_, NAT = NAT_, NB = NB_, RAWT = RAWT_;
+    // ATM: dequantized weight stages live in tensor memory (tcgen05.st by the
+    // dequant warps, read by the MMA as its A operand), after the two
+    // accumulators; otherwise in shared memory (128-byte swizzle).
+    static constexpr bool ATM = ATM_;
     static constexpr int NA = DT * NAT;           // dequantized weight stages
     static constexpr int RAW = DT * RAWT;         // raw super-block slots
     static constexpr int WARPS = 2 + kEpiWarps + DT * kTeamWarps + 1;
@@ -96,10 +103,13 @@ struct Cfg {
     static constexpr int RAW_WARP = WARPS - 1;    // issues the raw weight tiles
     static constexpr int A_BYTES = BM * BK * 2;   // 16 KB
     static constexpr int B_BYTES = BN * BK * 2;
-    static constexpr int TMEM_COLS = 2 * BN;      // two accumulators
+    static constexpr int A_COL0 = 2 * BN;         // first TMEM column of the A stages (ATM)
+    static constexpr int A_COLS = BK / 2;         // 32 columns: 64 16-bit k per lane
+    static constexpr int TMEM_COLS = ATM ? 512 : 2 * BN;  // two accumulators (+ A stages)
+    static_assert(!ATM || A_COL0 + NA * A_COLS <= 512, "tensor memory");
     // shared layout (all tiles 1024-byte aligned)
     static constexpr int OFF_A = 0;
-    static constexpr int OFF_B = OFF_A + NA * A_BYTES;
+    static constexpr int OFF_B = OFF_A + (ATM ? 0 : NA * A_BYTES);
     static constexpr int OFF_RAW = OFF_B + NB * B_BYTES;
     static constexpr int OFF_BAR = OFF_RAW + RAW * kRawBytes;
     // barriers: a_full[NA] a_empty[NA] b_full[NB] b_empty[NB] raw_full[RAW]
@@ -155,10 +165,12 @@ __device__ __forceinline__ TileRef tile_ref(int tile, const int* s_start, const 
     return r;
 }
 
-// smallest activation box (32 << i rows) that covers `rows`
-__device__ __forceinline__ int xbox_index(int rows) {
-    return rows <= 32 ? 0 : rows <= 64 ? 1 : rows <= 128 ? 2 : 3;
+// rows of activation box i: 32, 64, 128, then BN (every box at most BN)
+__host__ __device__ constexpr int xbox_rows(int i, int BN) {
+    return (32 << i) < BN && i < kXMaps - 1 ? (32 << i) : BN;
 }
+
+
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -372,14 +384,15 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     if (warp == 0) {
         // ---------------------------------------------------------- TMA
         if (lane == 0) {
-            for (int i = 0; i < kXMaps && (32 << i) <= BN; ++i) prefetch_tensormap(&tm_x.m[i]);
+            for (int i = 0; i < kXMaps; ++i) prefetch_tensormap(&tm_x.m[i]);
             const uint64_t pol_x = policy_evict_last();
             uint32_t kc = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
                 const TileRef t = tile_at(tile);
-                const int xb = xbox_index(t.rows);
+                int xb = 0;  // smallest box covering the tile's rows
+                while (xb < kXMaps - 1 && xbox_rows(xb, BN) < t.rows) ++xb;
                 const CUtensorMap* xm = &tm_x.m[xb];
-                const uint32_t bytes = (uint32_t)(32 << xb) * BK * 2;
+                const uint32_t bytes = (uint32_t)xbox_rows(xb, BN) * BK * 2;
                 for (int ks = 0; ks < nsb * 4; ++ks) {
                     const int s = kc % C::NB;
                     if (!mbar_wait(&b_empty[s], ((kc / C::NB) & 1) ^ 1)) { *abort_flag = 1; break; }
@@ -443,11 +456,18 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t da = smem_desc_k_sw128(sA + sa * C::A_BYTES);
                     const uint64_t db = smem_desc_k_sw128(sB + s * C::B_BYTES);
+                    if constexpr (C::ATM) {
+                        const uint32_t a_tmem = tmem_base + (uint32_t)(C::A_COL0 + sa * C::A_COLS);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes along k per MMA
-                        umma_f16_ss(d_tmem, da + 2 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
+                        for (int kk = 0; kk < BK / 16; ++kk)  // 8 columns (16 k) per MMA
+                            umma_f16_ts(d_tmem, a_tmem + 8 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
+                    } else {
+                        const uint64_t da = smem_desc_k_sw128(sA + sa * C::A_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes along k per MMA
+                            umma_f16_ss(d_tmem, da + 2 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
+                    }
                     umma_commit(&a_empty[sa]);
                     umma_commit(&b_empty[s]);
                     ++kc;
@@ -499,13 +519,18 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         // ---------------------------------------------------------- dequant
         const int dw = warp - (2 + kEpiWarps);
         const int team = dw / kTeamWarps;
-        // warp covers rows 16*wi .. 16*wi + 15, both halves of the group; a
-        // quarter-warp takes 8 consecutive rows of one half, so its 16-byte
-        // stores hit 8 different swizzled chunks (all 32 banks) and its raw
-        // loads (rows 144 bytes apart) 8 different bank quads
+        // shared-memory stages: a warp covers rows 16*wi .. 16*wi + 15, both
+        // halves of the group; a quarter-warp takes 8 consecutive rows of one
+        // half, so its 16-byte stores hit 8 different swizzled chunks (all 32
+        // banks) and its raw loads (rows 144 bytes apart) 8 different bank
+        // quads.  Tensor-memory stages: a warp may only write the 32 TMEM
+        // lanes of its quadrant (warp % 4), so it takes those 32 rows (lane =
+        // row) and one half of the group (the other warp of the quadrant the
+        // other half).
         const int wi = dw % kTeamWarps;
-        const int h = (lane >> 3) & 1;                             // half of the group
-        const int r = 16 * wi + 8 * (lane >> 4) + (lane & 7);      // weight row in tile
+        const int h = C::ATM ? wi / 4 : (lane >> 3) & 1;           // half of the group
+        const int r = C::ATM ? 32 * (warp & 3) + lane
+                             : 16 * wi + 8 * (lane >> 4) + (lane & 7);  // weight row in tile
         const int swz = r & 7;
         uint32_t rc = 0;  // super-blocks in kernel order; this team takes rc % DT == team
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -523,6 +548,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                     const RingPos<C> rp(rc, g);
                     const int s = rp.a_stage;
                     if (!mbar_wait_warp(&a_empty[s], rp.a_phase ^ 1)) { *abort_flag = 1; break; }
+                    if constexpr (C::ATM) tc_fence_after();  // the MMA that read the stage is done
                     const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g + 16 * h);
                     const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
                     uint32_t lo[8], hi[8];  // packed pairs, k = 16h + 2i (+32 for hi)
@@ -532,6 +558,19 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                                           nml2[2 * g + 1], fdl[2 * g], fnml[2 * g],
                                           fdl[2 * g + 1], fnml[2 * g + 1], lo[2 * u],
                                           lo[2 * u + 1], hi[2 * u], hi[2 * u + 1]);
+                    }
+                    if constexpr (C::ATM) {
+                        // columns (two k each): low nibbles k = 16h + 2i -> 8h + i,
+                        // high nibbles k = 32 + 16h + 2i -> 16 + 8h + i
+                        const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) +
+                                              (uint32_t)(C::A_COL0 + s * C::A_COLS);
+                        tmem_st_32x32b_x8(tcol + 8 * h, lo);
+                        tmem_st_32x32b_x8(tcol + 16 + 8 * h, hi);
+                        tmem_st_wait();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&a_full[s]);
+                        continue;
                     }
                     // 16-byte chunks c (8 values, k = 8c..8c+7) of row r, swizzled
                     uint8_t* arow = sA + s * C::A_BYTES + r * 128;
@@ -617,10 +656,10 @@ int act_maps(XMaps* mx, const void* x, int x_dtype, int64_t rows, int64_t K, int
     auto enc = encode_fn();
     FTC_REQUIRE(enc, FTC_E_CUDA, std::string(who) + ": cuTensorMapEncodeTiled unavailable");
     std::memset(mx, 0, sizeof(*mx));
-    for (int i = 0; i < kXMaps && (32 << i) <= BN; ++i) {
+    for (int i = 0; i < kXMaps; ++i) {
         const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
         const cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
-        const cuuint32_t box[2] = {BK, (cuuint32_t)(32 << i)};
+        const cuuint32_t box[2] = {BK, (cuuint32_t)xbox_rows(i, BN)};
         const cuuint32_t es[2] = {1, 1};
         CUresult r = enc(&mx->m[i],
                          x_dtype == FTC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -638,7 +677,11 @@ int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2,
              int M, int N, int K, void* y, int y_dtype, const GemmGroups& grp, int64_t max_tiles,
              cudaStream_t st) {
     const bool bf = x_dtype == FTC_BF16;
-    using C128 = Cfg<128, 1, 3, 5, 3>;
+    // small token counts: A stages in tensor memory (no shared-memory A
+    // stores or A reads by the MMA); large: the 256-token tile, which halves
+    // the weight traffic per FLOP and needs all 512 TMEM columns for its two
+    // accumulators
+    using C128 = Cfg<128, 1, 4, 5, 3, true>;
     using C256 = Cfg<256, 1, 3, 3, 3>;
     int rc;
     if (BN == 128)
