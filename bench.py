@@ -302,6 +302,7 @@ def run_ours(args, rank, world, local_rank):
     gemm_status = ftc.device_status()
     tp_block = time_tp(dev, world, rank)
     moe = time_moe(dev) if world == 1 else None
+    ep_layer = time_ep(dev, world, rank)
 
     # max over ranks
     t = torch.tensor([ms, e2e_ms, k_ms], device=dev, dtype=torch.float64)
@@ -370,6 +371,7 @@ def run_ours(args, rank, world, local_rank):
         "prefill_dequant_gemm": prefill_summary(prefill, gemm_status),
         "tp_block": tp_block,
         "moe": moe,
+        "ep_moe": ep_layer,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
         "setup_s": round(setup_s, 1),
@@ -498,6 +500,60 @@ def time_moe(dev):
                         "top-2 softmax routing of N(0,1) fp32 logits, bf16 N(0,1) tokens",
             "api": "ftc_moe_ffn (routing, grouping, expert FFNs, combine on the device)",
             "per_T": out, "status": ftc.device_status()}
+
+
+EP_T = [64, 1024]
+
+
+def time_ep(dev, world, rank):
+    """Config 5 expert-parallel: each rank holds 8/world experts (full
+    Mixtral-8x7B expert shapes) and T/world of the tokens; one forward =
+    routing, count and row all-to-alls, local grouped expert GEMMs, reverse
+    all-to-all, combine (NCCL).  Eager (the split sizes go to the host once
+    per forward); time = max over ranks, CUDA events, barrier before."""
+    import torch
+    import torch.distributed as dist
+    from xwfes_b200 import ep
+    d = ep.DIMS_MIXTRAL
+    E, U, K, FF = d["n_experts"], d["top_k"], d["n_embd"], d["n_ff"]
+    e0, e1 = ep.expert_range(E, world, rank)
+    mk = lambda nm, n, k: torch.from_numpy(np.stack(
+        [S.weight(F.Q4_K, n, k, seed=0, name=f"moe.{nm}.{e}") for e in range(e0, e1)])).to(dev)
+    ops = ep.CudaEPOps(dev, mk("gate", FF, K), mk("up", FF, K), mk("down", K, FF), e1 - e0, U, K,
+                       FF)
+    layer = ep.EPMoE(E, U, K, world, rank, ops)
+    per_expert = 3 * FF * F.row_bytes(F.Q4_K, K)
+    out = {}
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for T in EP_T:
+        t0, t1 = ep.token_range(T, world, rank)
+        logits = torch.from_numpy(S.router_logits(T, E, seed=0)[t0:t1]).to(dev)
+        x = torch.from_numpy(S.activations_bf16(T, K, seed=0, name="moe.x")[t0:t1].view(
+            np.int16)).to(dev).view(torch.bfloat16)
+        for _ in range(3):
+            layer.forward(logits, x)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        reps = 10
+        ev0.record()
+        for _ in range(reps):
+            layer.forward(logits, x)
+        ev1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1) / reps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = t.item() * 1e3
+        out[str(T)] = {"us": round(us, 1), "tokens_per_s": round(T / (us * 1e-6), 1),
+                       "weight_GBps": round(E * per_expert / (us * 1e-6) / 1e9, 1),
+                       "tflops": round(2.0 * T * U * 3 * FF * K / (us * 1e-6) / 1e12, 2)}
+    return {"workload": "config 5: Mixtral-8x7B-shaped MoE layer, expert-parallel, T tokens "
+                        "split over the ranks",
+            "parallelism": f"ep{world} ({E // world} experts per GPU; NCCL all-to-all of counts, "
+                           "token rows (bf16) and expert outputs (fp32))",
+            "scaling": "strong (T and the 8 experts are split over the GPUs)",
+            "per_T": out}
 
 
 PREFILL_SHAPES = [(14336, 4096), (4096, 14336)]

@@ -244,6 +244,37 @@ size_t ftc_moe_workspace_bytes(const ftc_moe_desc* desc, int64_t T);
 int ftc_moe_ffn(const ftc_moe_desc* desc, const float* logits, const void* x, int x_dtype,
                 int64_t T, float* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The routing half of ftc_moe_ffn (ft/src/engine.cpp:198-217): per token the
+ * top_k experts (idx[T][top_k]) and renormalised weights (w[T][top_k]), the
+ * rows of each expert in expert order (counts[E], offsets[E + 1]), each
+ * expert's rank by first use (first_use_rank[E], -1 when unused), the row of
+ * every (token, slot) pair (pos[T][top_k]) and the token of every row
+ * (row_token[T * top_k]).  All device int32 / fp32 arrays. */
+int ftc_moe_route(const float* logits, int64_t T, int64_t n_experts, int64_t top_k, int32_t* idx,
+                  float* w, int32_t* counts, int32_t* offsets, int32_t* first_use_rank,
+                  int32_t* pos, int32_t* row_token, void* stream);
+
+/* The combine of ftc_moe_ffn: out[t] = sum over t's slots, in the experts'
+ * first-use order, of w[t][u] * y[pos[t][u]] (separately rounded products
+ * and sums, as ft/src/engine.cpp:229-236); y, out: device fp32, row pitch
+ * n_embd (a multiple of 4). */
+int ftc_moe_combine(const float* y, const int32_t* pos, const int32_t* idx, const float* w,
+                    const int32_t* first_use_rank, int64_t T, int64_t top_k, int64_t n_embd,
+                    float* out, void* stream);
+
+/* The expert half of ftc_moe_ffn on rows already grouped by expert (the
+ * local step of an expert-parallel layer, after the token exchange): rows
+ * [offsets[e], offsets[e] + counts[e]) of x (device [rows][n_embd], x_dtype
+ * FTC_F32 / FTC_BF16 / FTC_F16) go through expert e of desc (gate/up, silu,
+ * down; same operand rules as ftc_moe_ffn) into y (device fp32
+ * [rows][n_embd]).  counts / offsets: device int32 [n_experts]; max_rows:
+ * an upper bound on every count.  workspace: 256-byte aligned device memory
+ * of at least ftc_moe_experts_workspace_bytes(desc, rows). */
+size_t ftc_moe_experts_workspace_bytes(const ftc_moe_desc* desc, int64_t rows);
+int ftc_moe_experts(const ftc_moe_desc* desc, const void* x, int x_dtype, int64_t rows,
+                    const int32_t* counts, const int32_t* offsets, int64_t max_rows, float* y,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* The expert chunk of ftc_backend_run_expert_chunk on DEVICE buffers,
  * without allocating anything: for callers that cannot call cudaMalloc (an
  * engine whose HBM is owned by its own allocator, code inside someone

@@ -1,0 +1,147 @@
+"""Expert-parallel MoE (config 5) host logic on the CPU: expert and token
+shards, the regrouping of received rows, and the whole exchange (count
+all-to-all, row all-to-all, reverse all-to-all, combine) between gloo ranks.
+The per-rank compute here is the oracle's (the reference's routing and
+expert FFN arithmetic), so the expert-parallel result must equal the oracle's
+single-process moe_ffn."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from xwfes_b200 import ep, formats as F, synth as S
+
+torch = pytest.importorskip("torch")
+
+E, U, K, FF, T = 4, 2, 256, 512, 10
+
+
+def test_ranges():
+    assert [ep.expert_range(8, 4, r) for r in range(4)] == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    with pytest.raises(ValueError):
+        ep.expert_range(8, 3, 0)
+    spans = [ep.token_range(10, 4, r) for r in range(4)]
+    assert spans == [(0, 3), (3, 6), (6, 8), (8, 10)]
+    assert ep.token_range(1, 8, 0) == (0, 1) and ep.token_range(1, 8, 5) == (1, 1)
+
+
+def test_regroup_orders_rows_by_expert():
+    rc = np.array([[2, 0, 1], [1, 3, 0]])  # [source][local expert]
+    perm, counts, offsets = ep.regroup(rc)
+    # received rows: s0: e0 e0 e2, s1: e0 e1 e1 e1 -> indices 0..6
+    assert perm.tolist() == [0, 1, 3, 4, 5, 6, 2]
+    assert counts.tolist() == [3, 3, 1] and offsets.tolist() == [0, 3, 6]
+    perm, counts, _ = ep.regroup(np.zeros((2, 2), np.int64))
+    assert perm.size == 0 and counts.tolist() == [0, 0]
+
+
+def np_route(oracle, logits, u):
+    """The device routing (ftc_moe_route) restated on the oracle's top-k."""
+    idx, w = oracle.route_topk(logits, u)
+    t, e = logits.shape
+    counts = np.bincount(idx.ravel(), minlength=e).astype(np.int32)
+    pos = np.zeros_like(idx)
+    row_token = np.zeros(t * u, np.int32)
+    row = 0
+    for ex in range(e):
+        for tk in range(t):
+            for s in range(u):
+                if idx[tk, s] == ex:
+                    pos[tk, s] = row
+                    row_token[row] = tk
+                    row += 1
+    first = {}
+    for k, ex in enumerate(idx.ravel()):
+        first.setdefault(int(ex), k)
+    order = sorted(first, key=first.get)
+    rank = np.full(e, -1, np.int32)
+    for r, ex in enumerate(order):
+        rank[ex] = r
+    return {"idx": idx, "w": w, "counts": torch.from_numpy(counts), "pos": pos,
+            "row_token": row_token, "rank": rank}
+
+
+class OracleEPOps:
+    def __init__(self, oracle, gate, up, down):
+        self.O, self.gate, self.up, self.down = oracle, gate, up, down
+
+    def route(self, logits, u):
+        return np_route(self.O, logits.numpy(), u)
+
+    def gather(self, x, route, rows):
+        return x[torch.from_numpy(route["row_token"][:rows].astype(np.int64))]
+
+    def experts(self, x, counts, offsets):
+        xn = x.numpy().astype(np.float32)
+        y = np.zeros_like(xn)
+        for e, (c, o) in enumerate(zip(counts, offsets)):
+            if c:
+                out = np.zeros((c, K), np.float32)
+                self.O.expert_ffn(xn[o:o + c], out, self.gate[e], self.up[e], self.down[e],
+                                  F.Q4_K, K, FF, threads=2)
+                y[o:o + c] = out
+        return torch.from_numpy(y)
+
+    def combine(self, y, route):
+        yn = y.numpy()
+        idx, w, pos, rank = route["idx"], route["w"], route["pos"], route["rank"]
+        out = np.zeros((idx.shape[0], K), np.float32)
+        for t in range(idx.shape[0]):
+            for s in sorted(range(idx.shape[1]), key=lambda s: rank[idx[t, s]]):
+                out[t] = out[t] + np.float32(w[t, s]) * yn[pos[t, s]]
+        return torch.from_numpy(out)
+
+    def to_host(self, *ts):
+        return [t.numpy() for t in ts]
+
+    def index(self, n):
+        return torch.from_numpy(n)
+
+
+def _weights():
+    return (S.expert_weights(F.Q4_K, E, FF, K, seed=3, name="ep.gate"),
+            S.expert_weights(F.Q4_K, E, FF, K, seed=3, name="ep.up"),
+            S.expert_weights(F.Q4_K, E, K, FF, seed=3, name="ep.down"))
+
+
+def _inputs():
+    return (S.router_logits(T, E, seed=7),
+            S.activations_f32(T, K, seed=7, name="ep.x"))
+
+
+def _rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from oracle import oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g, u, d = _weights()
+        e0, e1 = ep.expert_range(E, world, rank)
+        layer = ep.EPMoE(E, U, K, world, rank, OracleEPOps(O, g[e0:e1], u[e0:e1], d[e0:e1]))
+        logits, x = _inputs()
+        t0, t1 = ep.token_range(T, world, rank)
+        out = layer.forward(torch.from_numpy(logits[t0:t1]), torch.from_numpy(x[t0:t1]))
+        np.save(os.path.join(out_dir, f"out{rank}.npy"), out.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_two_ranks_match_single_process_moe(tmp_path, oracle):
+    import torch.multiprocessing as mp
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn", join=True)
+    got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(2)])
+    g, u, d = _weights()
+    logits, x = _inputs()
+    ref = oracle.moe_ffn(x, logits, g, u, d, F.Q4_K, K, FF, U, threads=2)
+    np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6 * np.abs(ref).max())

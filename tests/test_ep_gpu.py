@@ -1,0 +1,109 @@
+"""GPU parity of the expert-parallel MoE layer (config 5 structure, reduced
+sizes).  With one rank the layer is routing + grouped expert GEMMs + combine
+and must reproduce ftc_moe_ffn's grouped path bit for bit (each output row
+depends only on its own token and experts); across two GPUs (NCCL) the rows
+exchanged between ranks must give the same bits again."""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from xwfes_b200 import ep, formats as F, synth as S
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+E, U, K, FF = 8, 2, 1024, 2048
+
+
+def weights():
+    return (S.expert_weights(F.Q4_K, E, FF, K, seed=4, name="epg.gate"),
+            S.expert_weights(F.Q4_K, E, FF, K, seed=4, name="epg.up"),
+            S.expert_weights(F.Q4_K, E, K, FF, seed=4, name="epg.down"))
+
+
+def inputs(T):
+    x = S.activations_bf16(T, K, seed=T, name="epg.x")
+    return S.router_logits(T, E, seed=T), x
+
+
+def to_dev(logits, xbits):
+    return (torch.from_numpy(logits).cuda(),
+            torch.from_numpy(xbits.view(np.int16)).cuda().view(torch.bfloat16))
+
+
+def single_gpu(T):
+    from xwfes_b200 import ftc
+    g, u, d = (torch.from_numpy(a).cuda() for a in weights())
+    layer = ftc.MoeLayer(g, u, d, n_experts=E, top_k=U, n_embd=K, n_ff=FF)
+    lg, x = to_dev(*inputs(T))
+    return layer(lg, x).cpu().numpy()
+
+
+@pytest.mark.parametrize("T", [64, 300])
+def test_one_rank_equals_moe_layer(T):
+    g, u, d = (torch.from_numpy(a).cuda() for a in weights())
+    ops = ep.CudaEPOps(torch.device("cuda", 0), g, u, d, E, U, K, FF)
+    layer = ep.EPMoE(E, U, K, 1, 0, ops)
+    lg, x = to_dev(*inputs(T))
+    out = layer.forward(lg, x)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), single_gpu(T))
+
+
+_CHILD = r"""
+import os, sys, datetime, numpy as np, torch, torch.distributed as dist
+sys.path.insert(0, {root!r})
+sys.path.insert(0, os.path.join({root!r}, "tests"))
+from xwfes_b200 import ep
+import test_ep_gpu as T
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                        device_id=torch.device("cuda", rank))
+g, u, d = T.weights()
+e0, e1 = ep.expert_range(T.E, world, rank)
+dev = torch.device("cuda", rank)
+ops = ep.CudaEPOps(dev, *(torch.from_numpy(a[e0:e1]).to(dev) for a in (g, u, d)),
+                   e1 - e0, T.U, T.K, T.FF)
+layer = ep.EPMoE(T.E, T.U, T.K, world, rank, ops)
+for n in (64, 300):
+    logits, x = T.inputs(n)
+    t0, t1 = ep.token_range(n, world, rank)
+    lg = torch.from_numpy(logits[t0:t1]).to(dev)
+    xb = torch.from_numpy(x[t0:t1].view(np.int16)).to(dev).view(torch.bfloat16)
+    out = layer.forward(lg, xb)
+    torch.cuda.synchronize()
+    np.save(os.path.join({out!r}, f"out{{n}}_{{rank}}.npy"), out.cpu().numpy())
+dist.barrier()
+dist.destroy_process_group()
+"""
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_two_gpus_nccl(tmp_path):
+    code = _CHILD.format(root=ROOT, out=str(tmp_path))
+    port = _free_port()
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r),
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, "-c", code], env=env, cwd=ROOT))
+    for p in procs:
+        assert p.wait(timeout=300) == 0
+    for n in (64, 300):
+        got = np.concatenate([np.load(tmp_path / f"out{n}_{r}.npy") for r in range(2)])
+        assert np.array_equal(got, single_gpu(n))

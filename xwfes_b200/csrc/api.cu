@@ -68,6 +68,16 @@ int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld,
                 int32_t* row_exp, cudaStream_t st);
 int silu_mul(const float* g, const float* u, int64_t n, float* h, cudaStream_t st);
 size_t moe_workspace_bytes(const ftc_moe_desc* d, int64_t T);
+size_t moe_experts_workspace_bytes(const ftc_moe_desc* d, int64_t rows);
+int moe_route_only(const float* logits, int64_t T, int64_t E, int64_t U, int32_t* idx, float* w,
+                   int32_t* counts, int32_t* offsets, int32_t* rank, int32_t* pos,
+                   int32_t* row_token, cudaStream_t st);
+int moe_combine_only(const float* y, const int32_t* pos, const int32_t* idx, const float* w,
+                     const int32_t* rank, int64_t T, int64_t U, int64_t K, float* out,
+                     cudaStream_t st);
+int moe_experts(const ftc_moe_desc* d, const void* x, int x_dtype, int64_t rows,
+                const int32_t* counts, const int32_t* offsets, int64_t max_rows, float* y,
+                void* ws, size_t ws_bytes, cudaStream_t st);
 int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dtype, int64_t T,
             float* out, void* ws, size_t ws_bytes, cudaStream_t st);
 
@@ -451,6 +461,34 @@ int ftc_rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t
 
 int ftc_silu_mul(const float* g, const float* u, int64_t n, float* h, void* stream) {
     int rc = silu_mul(g, u, n, h, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_moe_route(const float* logits, int64_t T, int64_t n_experts, int64_t top_k, int32_t* idx,
+                  float* w, int32_t* counts, int32_t* offsets, int32_t* first_use_rank,
+                  int32_t* pos, int32_t* row_token, void* stream) {
+    int rc = moe_route_only(logits, T, n_experts, top_k, idx, w, counts, offsets, first_use_rank,
+                            pos, row_token, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_moe_combine(const float* y, const int32_t* pos, const int32_t* idx, const float* w,
+                    const int32_t* first_use_rank, int64_t T, int64_t top_k, int64_t n_embd,
+                    float* out, void* stream) {
+    int rc = moe_combine_only(y, pos, idx, w, first_use_rank, T, top_k, n_embd, out,
+                              (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+size_t ftc_moe_experts_workspace_bytes(const ftc_moe_desc* desc, int64_t rows) {
+    return moe_experts_workspace_bytes(desc, rows);
+}
+
+int ftc_moe_experts(const ftc_moe_desc* desc, const void* x, int x_dtype, int64_t rows,
+                    const int32_t* counts, const int32_t* offsets, int64_t max_rows, float* y,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = moe_experts(desc, x, x_dtype, rows, counts, offsets, max_rows, y, workspace,
+                         workspace_bytes, (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

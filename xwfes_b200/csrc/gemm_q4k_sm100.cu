@@ -760,7 +760,7 @@ int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64
                      int64_t N, int64_t K, int64_t row_stride, const void* x, int x_dtype,
                      int64_t rows, const int32_t* counts, const int32_t* offsets,
                      int64_t max_rows_per_group, void* y, int y_dtype, int64_t ldy,
-                     cudaStream_t st) {
+                     cudaStream_t st, const int32_t* row_exp) {
     FTC_REQUIRE(w && x && y && counts && offsets && (n_sets == 1 || w2), FTC_E_INVALID,
                 "gemm_q4k_grouped: null pointer");
     FTC_REQUIRE(n_sets == 1 || n_sets == 2, FTC_E_INVALID, "gemm_q4k_grouped: 1 or 2 weight sets");
@@ -786,7 +786,7 @@ int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64
         (rc = weight_map(&tw2, w2, N, K, row_stride, G, plane_stride, "gemm_q4k_grouped")))
         return rc;
     if ((rc = act_maps(&tx, x, x_dtype, rows, K, BN, "gemm_q4k_grouped"))) return rc;
-    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy, nullptr};
+    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy, row_exp};
     // upper bound on tiles: every non-empty group adds at most one partial token tile
     const int64_t tok_tiles = (rows + BN - 1) / BN + std::min<int64_t>(G, rows);
     const int64_t tiles = tok_tiles * ((N + BM - 1) / BM) * n_sets;

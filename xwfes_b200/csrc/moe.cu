@@ -39,7 +39,7 @@ int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64
                      int64_t N, int64_t K, int64_t row_stride, const void* x, int x_dtype,
                      int64_t rows, const int32_t* counts, const int32_t* offsets,
                      int64_t max_rows_per_group, void* y, int y_dtype, int64_t ldy,
-                     cudaStream_t st);
+                     cudaStream_t st, const int32_t* row_exp = nullptr);
 
 namespace {
 
@@ -176,12 +176,13 @@ moe_route(const float* __restrict__ logits, int T, int E, int U, int32_t* __rest
 }
 
 // xg[row] = fp16(x[row_token[row]] * 2^-xs[row]), one CTA per row
+// (row_token nullptr: x is already in row order)
 template <typename TI>
 __global__ void moe_gather_scale(const TI* __restrict__ x, const int32_t* __restrict__ row_token,
                                  int K, __half* __restrict__ xg, int32_t* __restrict__ xs) {
     __shared__ float red[32];
     const int row = blockIdx.x;
-    const TI* src = x + (int64_t)row_token[row] * K;
+    const TI* src = x + (int64_t)(row_token ? row_token[row] : row) * K;
     float amax = 0.f;
     for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(to_f(src[k])));
     const int s = row_scale_exp(block_max(amax, red));
@@ -464,6 +465,107 @@ int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dty
                                                               U, K, out);
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;
+}
+
+
+// Routing and grouping alone (moe_route): outputs as in the kernel's header.
+int moe_route_only(const float* logits, int64_t T, int64_t E, int64_t U, int32_t* idx, float* w,
+                   int32_t* counts, int32_t* offsets, int32_t* rank, int32_t* pos,
+                   int32_t* row_token, cudaStream_t st) {
+    FTC_REQUIRE(E >= 1 && E <= kMaxExperts && U >= 1 && U <= kMaxTopK && U <= E, FTC_E_INVALID,
+                "ftc_moe_route: need 1 <= top_k <= min(8, n_experts) <= 256");
+    FTC_REQUIRE(T >= 0 && T * U <= INT32_MAX / 2, FTC_E_INVALID, "ftc_moe_route: bad T");
+    FTC_REQUIRE(logits && idx && w && counts && offsets && rank && pos && row_token,
+                FTC_E_INVALID, "ftc_moe_route: null pointer");
+    moe_route<<<1, kRouteThreads, 0, st>>>(logits, (int)T, (int)E, (int)U, idx, w, counts, offsets,
+                                           rank, pos, row_token);
+    FTC_CUDA(cudaGetLastError());
+    return FTC_OK;
+}
+
+// out[t] = sum over t's slots (in expert first-use order) of w * y[pos]
+int moe_combine_only(const float* y, const int32_t* pos, const int32_t* idx, const float* w,
+                     const int32_t* rank, int64_t T, int64_t U, int64_t K, float* out,
+                     cudaStream_t st) {
+    FTC_REQUIRE(y && pos && idx && w && rank && out, FTC_E_INVALID, "ftc_moe_combine: null pointer");
+    FTC_REQUIRE(T >= 0 && U >= 1 && U <= kMaxTopK && K > 0 && K % 4 == 0 && (uintptr_t)y % 16 == 0 &&
+                    (uintptr_t)out % 16 == 0,
+                FTC_E_INVALID, "ftc_moe_combine: bad shape or alignment");
+    if (T == 0) return FTC_OK;
+    moe_combine<<<grid_for(T * K / 4), 256, 0, st>>>(y, nullptr, pos, idx, w, rank, (int)T, (int)U,
+                                                   (int)K, out);
+    FTC_CUDA(cudaGetLastError());
+    return FTC_OK;
+}
+
+// Expert FFNs on rows already grouped by expert (the local half of an
+// expert-parallel MoE layer): rows [offsets[e], offsets[e] + counts[e]) of x
+// go through expert e of d (gate/up, silu, down) into y (fp32, unscaled).
+// counts / offsets: device int32 [E]; rows: total rows; max_rows: bound on
+// any count.  Workspace: moe_experts_workspace_bytes.
+size_t moe_experts_workspace_bytes(const ftc_moe_desc* d, int64_t rows) {
+    if (check_desc(d, "ftc_moe_experts_workspace_bytes") != FTC_OK || rows < 0) return 0;
+    size_t o = 0;
+    o += align256((size_t)rows * 4);                    // xs
+    o += align256((size_t)rows * 4);                    // hs
+    o += align256((size_t)rows * d->n_embd * 2);        // xg
+    o += align256((size_t)rows * 2 * d->n_ff * 4);      // gu
+    o += align256((size_t)rows * d->n_ff * 2);          // h
+    return o;
+}
+
+int moe_experts(const ftc_moe_desc* d, const void* x, int x_dtype, int64_t rows,
+                const int32_t* counts, const int32_t* offsets, int64_t max_rows, float* y,
+                void* ws, size_t ws_bytes, cudaStream_t st) {
+    int rc = check_desc(d, "ftc_moe_experts");
+    if (rc) return rc;
+    FTC_REQUIRE(rows >= 0 && rows <= INT32_MAX / 2 && max_rows >= 0, FTC_E_INVALID,
+                "ftc_moe_experts: bad row count");
+    if (rows == 0) return FTC_OK;
+    FTC_REQUIRE(x && y && ws && counts && offsets && d->gate_exps && d->up_exps && d->down_exps,
+                FTC_E_INVALID, "ftc_moe_experts: null pointer");
+    FTC_REQUIRE(x_dtype == FTC_F32 || x_dtype == FTC_BF16 || x_dtype == FTC_F16,
+                FTC_E_UNSUPPORTED, "ftc_moe_experts: x must be fp32, bf16 or fp16");
+    FTC_REQUIRE((uintptr_t)ws % 256 == 0 && (uintptr_t)y % 16 == 0 && (uintptr_t)x % 16 == 0,
+                FTC_E_INVALID, "ftc_moe_experts: x and y need 16-byte, workspace 256-byte alignment");
+    FTC_REQUIRE(ws_bytes >= moe_experts_workspace_bytes(d, rows), FTC_E_INVALID,
+                "ftc_moe_experts: workspace too small");
+    const int E = (int)d->n_experts, K = (int)d->n_embd, F = (int)d->n_ff, R = (int)rows;
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    int32_t* xs = reinterpret_cast<int32_t*>(w);
+    w += align256((size_t)R * 4);
+    int32_t* hs = reinterpret_cast<int32_t*>(w);
+    w += align256((size_t)R * 4);
+    __half* xg = reinterpret_cast<__half*>(w);
+    w += align256((size_t)R * K * 2);
+    float* gu = reinterpret_cast<float*>(w);
+    w += align256((size_t)R * 2 * F * 4);
+    __half* h = reinterpret_cast<__half*>(w);
+    if (x_dtype == FTC_F32)
+        moe_gather_scale<float><<<R, 256, 0, st>>>(static_cast<const float*>(x), nullptr, K, xg, xs);
+    else if (x_dtype == FTC_BF16)
+        moe_gather_scale<__nv_bfloat16><<<R, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(x), nullptr, K, xg, xs);
+    else
+        moe_gather_scale<__half><<<R, 256, 0, st>>>(static_cast<const __half*>(x), nullptr, K, xg, xs);
+    FTC_CUDA(cudaGetLastError());
+    const int64_t mr = std::max<int64_t>(1, std::min<int64_t>(max_rows, rows));
+    rc = gemm_q4k_grouped(d->gate_exps, d->up_exps, 2, E, d->gu_plane_stride, F, K,
+                          d->gu_row_stride, xg, FTC_F16, R, counts, offsets, mr, gu, FTC_F32,
+                          2 * (int64_t)F, st);
+    if (rc) return rc;
+    static bool configured = false;
+    if (!configured) {
+        FTC_CUDA(cudaFuncSetAttribute(moe_silu_scale, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)(kMaxFf * 4)));
+        configured = true;
+    }
+    moe_silu_scale<<<R, 512, (size_t)F * 4, st>>>(gu, xs, F, h, hs);
+    FTC_CUDA(cudaGetLastError());
+    // down projection; the epilogue undoes h's row scales (exact)
+    return gemm_q4k_grouped(d->down_exps, nullptr, 1, E, d->dn_plane_stride, K, F,
+                            d->dn_row_stride, h, FTC_F16, R, counts, offsets, mr, y, FTC_F32, K,
+                            st, hs);
 }
 
 }  // namespace ftc

@@ -48,6 +48,10 @@ SIGNATURES = {
                                      _p]),
     "ftc_rows_to_f16": (C.c_int, [_p, C.c_int, _i64, _i64, _i64, _p, _p, _p]),
     "ftc_silu_mul": (C.c_int, [_p, _p, _i64, _p, _p]),
+    "ftc_moe_route": (C.c_int, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "ftc_moe_combine": (C.c_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p]),
+    "ftc_moe_experts_workspace_bytes": (C.c_size_t, [_p, _i64]),
+    "ftc_moe_experts": (C.c_int, [_p, _p, C.c_int, _i64, _p, _p, _i64, _p, _p, C.c_size_t, _p]),
     "ftc_moe_workspace_bytes": (C.c_size_t, [_p, _i64]),
     "ftc_moe_ffn": (C.c_int, [_p, _p, _p, C.c_int, _i64, _p, _p, C.c_size_t, _p]),
 }
@@ -225,6 +229,38 @@ def _align(n, a=256):
     return (n + a - 1) // a * a
 
 
+def moe_route(logits, top_k, stream=None):
+    """Device routing (ftc_moe_route) of fp32 logits [T, E]: returns a dict of
+    int32 / fp32 CUDA tensors idx, w, counts, offsets, rank, pos, row_token."""
+    import torch
+    T, E = logits.shape
+    dev = logits.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    r = {"idx": torch.empty((T, top_k), **i32), "w": torch.empty((T, top_k), dtype=torch.float32,
+                                                                  device=dev),
+         "counts": torch.empty((E,), **i32), "offsets": torch.empty((E + 1,), **i32),
+         "rank": torch.empty((E,), **i32), "pos": torch.empty((T, top_k), **i32),
+         "row_token": torch.empty((max(1, T * top_k),), **i32)}
+    check(lib().ftc_moe_route(logits.data_ptr(), T, E, top_k, r["idx"].data_ptr(),
+                              r["w"].data_ptr(), r["counts"].data_ptr(), r["offsets"].data_ptr(),
+                              r["rank"].data_ptr(), r["pos"].data_ptr(), r["row_token"].data_ptr(),
+                              _stream(stream)), "ftc_moe_route")
+    return r
+
+
+def moe_combine(y, route, out=None, stream=None):
+    """out[t] = sum_u w[t][u] * y[pos[t][u]] in expert first-use order."""
+    import torch
+    T, U = route["idx"].shape
+    K = y.shape[1]
+    if out is None:
+        out = torch.empty((T, K), dtype=torch.float32, device=y.device)
+    check(lib().ftc_moe_combine(y.data_ptr(), route["pos"].data_ptr(), route["idx"].data_ptr(),
+                                route["w"].data_ptr(), route["rank"].data_ptr(), T, U, K,
+                                out.data_ptr(), _stream(stream)), "ftc_moe_combine")
+    return out
+
+
 class MoeLayer:
     """One MoE FFN layer on the device (``ftc_moe_ffn``).
 
@@ -242,6 +278,7 @@ class MoeLayer:
                             gu_rs, gu_rs * n_ff, dn_rs, dn_rs * n_embd)
         self.n_experts, self.top_k, self.n_embd = n_experts, top_k, n_embd
         self._ws = None
+        self._ews = None
 
     def workspace_bytes(self, T):
         n = int(lib().ftc_moe_workspace_bytes(C.byref(self.desc), T))
@@ -268,6 +305,23 @@ class MoeLayer:
         check(lib().ftc_moe_ffn(C.byref(self.desc), logits.data_ptr(), x.data_ptr(), xt, T,
                                 out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream)),
               "ftc_moe_ffn")
+        return out
+
+    def experts(self, x, counts, offsets, max_rows, out=None, stream=None):
+        """Expert FFNs on rows of x already grouped by expert (ftc_moe_experts):
+        counts / offsets int32 CUDA tensors [E]; returns fp32 [rows, n_embd]."""
+        import torch
+        R = x.shape[0]
+        xt = {torch.float32: F.F32, torch.bfloat16: F.BF16, torch.float16: F.F16}[x.dtype]
+        if out is None:
+            out = torch.empty((R, self.n_embd), dtype=torch.float32, device=x.device)
+        n = int(lib().ftc_moe_experts_workspace_bytes(C.byref(self.desc), R))
+        if self._ews is None or self._ews.numel() < n:
+            self._ews = torch.empty(max(n, 256), dtype=torch.uint8, device=x.device)
+        check(lib().ftc_moe_experts(C.byref(self.desc), x.data_ptr(), xt, R, counts.data_ptr(),
+                                    offsets.data_ptr(), max_rows, out.data_ptr(),
+                                    self._ews.data_ptr(), self._ews.numel(), _stream(stream)),
+              "ftc_moe_experts")
         return out
 
     def routing(self, T):
