@@ -57,8 +57,6 @@
 
 namespace ftc {
 
-FTC_DEVSTAT_READER(devstat_gemm_q4k)
-
 constexpr int kGemmMaxGroups = 256;
 
 // Token groups of one launch (see the grouped mode above).
@@ -69,6 +67,12 @@ struct GemmGroups {
     int n_sets;              // weight tensors sharing the tokens (1, or 2 for gate + up)
     int64_t ldy;             // Y row pitch in elements
     const int32_t* row_exp;  // optional: Y row m is multiplied by 2^row_exp[m] (exact)
+    // split-K (set by the launcher): K is cut into `splits` super-block
+    // ranges; each (range, tile) unit writes an fp32 partial and the last
+    // unit of a tile to finish sums them in range order
+    int splits;
+    uint32_t* counters;  // [tiles][kEpiWarps] arrivals (zero between launches)
+    float* part;         // [tiles * splits][BN][BM] fp32 partials
 };
 
 namespace {
@@ -171,19 +175,6 @@ __host__ __device__ constexpr int xbox_rows(int i, int BN) {
 }
 
 
-
-template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b);
-template <>
-__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-template <>
-__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 // Scale and min of all 8 sub-blocks of a Q4_K super-block header (d, dmin,
 // 12 packed bytes): fdl[j] = d*sc_j and fnml[j] = -dmin*m_j in fp32 (exact),
@@ -377,8 +368,18 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
 
     const int tiles = s_start[G];
     const int nsb = K / 256;
+    const int S = grp.splits;
+    const int units = tiles * S;  // split-major: concurrent CTAs share k ranges
     auto tile_at = [&](int tile) {
         return tile_ref<BN>(tile, s_start, s_base, s_cnt, G, n_tiles, n_all);
+    };
+    // unit u: tile and its super-block range [sb0, sb1) (never empty: the
+    // host keeps at least two super-blocks per split)
+    auto unit_at = [&](int u, int& split, int& sb0, int& sb1) {
+        split = u / tiles;
+        sb0 = split * nsb / S;
+        sb1 = (split + 1) * nsb / S;
+        return u - split * tiles;
     };
 
     if (warp == 0) {
@@ -387,13 +388,14 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             for (int i = 0; i < kXMaps; ++i) prefetch_tensormap(&tm_x.m[i]);
             const uint64_t pol_x = policy_evict_last();
             uint32_t kc = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-                const TileRef t = tile_at(tile);
+            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+                int split, sb0, sb1;
+                const TileRef t = tile_at(unit_at(u, split, sb0, sb1));
                 int xb = 0;  // smallest box covering the tile's rows
                 while (xb < kXMaps - 1 && xbox_rows(xb, BN) < t.rows) ++xb;
                 const CUtensorMap* xm = &tm_x.m[xb];
                 const uint32_t bytes = (uint32_t)xbox_rows(xb, BN) * BK * 2;
-                for (int ks = 0; ks < nsb * 4; ++ks) {
+                for (int ks = sb0 * 4; ks < sb1 * 4; ++ks) {
                     const int s = kc % C::NB;
                     if (!mbar_wait(&b_empty[s], ((kc / C::NB) & 1) ^ 1)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&b_full[s], bytes);
@@ -415,10 +417,11 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             prefetch_tensormap(&tm_w2);
             const uint64_t pol_w = policy_evict_last();  // weights are re-read per token tile
             uint32_t rc = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-                const TileRef t = tile_at(tile);
+            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+                int split, sb0, sb1;
+                const TileRef t = tile_at(unit_at(u, split, sb0, sb1));
                 const CUtensorMap* wm = t.set ? &tm_w2 : &tm_w;
-                for (int sb = 0; sb < nsb; ++sb) {
+                for (int sb = sb0; sb < sb1; ++sb) {
                     const RingPos<C> rp(rc, 0);
                     if (!mbar_wait(&raw_empty[rp.raw_slot], rp.raw_phase ^ 1)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&raw_full[rp.raw_slot], kRawBytes);
@@ -440,14 +443,17 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             constexpr uint32_t fmt = std::is_same<OP, __half>::value ? 0u : 1u;
             uint32_t kc = 0;
             int i = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++i) {
+            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++i) {
                 const int b = i & 1;
+                int split, sb0, sb1;
+                const int tile = unit_at(u, split, sb0, sb1);
                 // MMA N = the tile's tokens rounded up to 16
                 const uint32_t idesc = idesc_f16(fmt, BM, (uint32_t)min(BN, (tile_at(tile).rows + 15) & ~15));
                 if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
-                for (int ks = 0; ks < nsb * 4; ++ks) {
+                for (int ks = sb0 * 4; ks < sb1 * 4; ++ks) {
+                    const bool acc = ks != sb0 * 4;  // the unit's first k-step overwrites
                     const RingPos<C> rp(kc >> 2, (int)(kc & 3));
                     const int sa = rp.a_stage, s = kc % C::NB;
                     if (!mbar_wait(&a_full[sa], rp.a_phase) ||
@@ -461,12 +467,12 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                         const uint32_t a_tmem = tmem_base + (uint32_t)(C::A_COL0 + sa * C::A_COLS);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk)  // 8 columns (16 k) per MMA
-                            umma_f16_ts(d_tmem, a_tmem + 8 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
+                            umma_f16_ts(d_tmem, a_tmem + 8 * kk, db + 2 * kk, idesc, acc || kk != 0);
                     } else {
                         const uint64_t da = smem_desc_k_sw128(sA + sa * C::A_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk)  // +32 bytes along k per MMA
-                            umma_f16_ss(d_tmem, da + 2 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
+                            umma_f16_ss(d_tmem, da + 2 * kk, db + 2 * kk, idesc, acc || kk != 0);
                     }
                     umma_commit(&a_empty[sa]);
                     umma_commit(&b_empty[s]);
@@ -480,36 +486,126 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         }
     } else if (warp < 2 + kEpiWarps) {
         // ---------------------------------------------------------- epilogue
+        // Split-K: every unit stores its fp32 partial (this warp's 32 columns
+        // of the tile); the warp whose arrival completes the tile's count
+        // re-reads its own accumulator and sums all partials in split order,
+        // so the result does not depend on which unit finished last.  Each
+        // warp counts on its own (no barrier between the epilogue warps).
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const int nl = 32 * q + lane;  // column of the tile this lane holds
         int i = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
             const int b = i & 1;
+            int split, sb0, sb1;
+            const int tile = unit_at(u, split, sb0, sb1);
             const TileRef t = tile_at(tile);
             if (!mbar_wait_warp(&acc_full[b], (i >> 1) & 1)) { *abort_flag = 1; break; }
             tc_fence_after();
-            const int n = t.nt * BM + 32 * q + lane;
+            const int n = t.nt * BM + nl;
             const int64_t col = (int64_t)t.set * N + n;
             const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN);
+            bool last = true;
+            if (S > 1) {
+                // partial slot (tile, split): [quadrant][row][32 columns] fp32
+                float* mine = grp.part + (size_t)(tile * S + split) * (BM * BN) + q * (BN * 32) + lane;
 #pragma unroll 1
-            for (int c0 = 0; c0 < t.rows; c0 += 32) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(taddr + c0, r);
-                tmem_ld_wait();
-                const int64_t y0 = (int64_t)(t.row0 + c0) * grp.ldy + col;
-                const int jn = min(32, t.rows - c0);
-                if (grp.row_exp) {  // exact power-of-two row scales (warp-uniform branch)
-                    float f = 0.f;
-                    if (lane < jn) f = __uint_as_float((uint32_t)(grp.row_exp[t.row0 + c0 + lane] + 127) << 23);
+                for (int c0 = 0; c0 < t.rows; c0 += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c0, r);
+                    tmem_ld_wait();
+                    const int jn = min(32, t.rows - c0);
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, f, j));
+                        if (j < jn) __stcg(mine + (c0 + j) * 32, __uint_as_float(r[j]));
                 }
-                if (n < N) {
+                __threadfence();
+                __syncwarp();
+                uint32_t old = 0;
+                uint32_t* cnt = grp.counters + tile * kEpiWarps + q;
+                if (lane == 0) old = atomicAdd(cnt, 1u);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                last = old == (uint32_t)(S - 1);
+                if (last) {
+                    if (lane == 0) atomicExch(cnt, 0u);  // ready for the next launch
+                    __threadfence();
+                    // Sum the S partials of this quadrant in split order.  A
+                    // lane takes 4 columns (c4..c4+3) of rows 4g + rr; loads
+                    // go out 16 at a time (4 splits x 4 row groups) so the
+                    // fix-up costs one L2 round trip per 16 rows and 4 splits.
+                    const int rr = lane >> 3, c4 = 4 * (lane & 7);
+                    const float* qb = grp.part + (size_t)tile * S * (BM * BN) + q * (BN * 32) + c4;
+                    const int nq = t.nt * BM + 32 * q + c4;  // first of the lane's 4 columns
+                    const int64_t cq = (int64_t)t.set * N + nq;
+#pragma unroll 1
+                    for (int rb = 0; rb < t.rows; rb += 16) {
+                        float4 acc[4];
+#pragma unroll 1
+                        for (int s0 = 0; s0 < S; s0 += 4) {
+                            float4 v[4][4];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < jn) store_out(y, ytype, y0 + (int64_t)j * grp.ldy, __uint_as_float(r[j]));
+                            for (int u2 = 0; u2 < 4; ++u2)
+#pragma unroll
+                                for (int g = 0; g < 4; ++g) {
+                                    const int row = rb + 4 * g + rr;
+                                    v[u2][g] = (s0 + u2 < S && row < t.rows)
+                                                   ? __ldcg(reinterpret_cast<const float4*>(
+                                                         qb + (size_t)(s0 + u2) * (BM * BN) + row * 32))
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                                }
+#pragma unroll
+                            for (int u2 = 0; u2 < 4; ++u2) {
+                                if (s0 + u2 >= S) break;
+#pragma unroll
+                                for (int g = 0; g < 4; ++g) {
+                                    if (s0 + u2 == 0) {
+                                        acc[g] = v[u2][g];
+                                    } else {
+                                        acc[g].x += v[u2][g].x;
+                                        acc[g].y += v[u2][g].y;
+                                        acc[g].z += v[u2][g].z;
+                                        acc[g].w += v[u2][g].w;
+                                    }
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int g = 0; g < 4; ++g) {
+                            const int row = rb + 4 * g + rr;
+                            if (row >= t.rows) continue;
+                            float f = 1.f;
+                            if (grp.row_exp)
+                                f = __uint_as_float((uint32_t)(grp.row_exp[t.row0 + row] + 127) << 23);
+                            const int64_t yi = (int64_t)(t.row0 + row) * grp.ldy + cq;
+                            const float o[4] = {acc[g].x * f, acc[g].y * f, acc[g].z * f, acc[g].w * f};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                if (nq + e < N) store_out(y, ytype, yi + e, o[e]);
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c0 = 0; c0 < t.rows; c0 += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c0, r);
+                    tmem_ld_wait();
+                    const int64_t y0 = (int64_t)(t.row0 + c0) * grp.ldy + col;
+                    const int jn = min(32, t.rows - c0);
+                    if (grp.row_exp) {  // exact power-of-two row scales (warp-uniform branch)
+                        float f = 0.f;
+                        if (lane < jn) f = __uint_as_float((uint32_t)(grp.row_exp[t.row0 + c0 + lane] + 127) << 23);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            r[j] = __float_as_uint(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, f, j));
+                    }
+                    if (n < N) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < jn) store_out(y, ytype, y0 + (int64_t)j * grp.ldy, __uint_as_float(r[j]));
+                    }
                 }
             }
+            (void)last;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -533,8 +629,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                              : 16 * wi + 8 * (lane >> 4) + (lane & 7);  // weight row in tile
         const int swz = r & 7;
         uint32_t rc = 0;  // super-blocks in kernel order; this team takes rc % DT == team
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            for (int sb = 0; sb < nsb; ++sb, ++rc) {
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
+            int split, sb0, sb1;
+            unit_at(u, split, sb0, sb1);
+            for (int sb = sb0; sb < sb1; ++sb, ++rc) {
                 if ((int)(rc % C::DT) != team) continue;
                 const RingPos<C> rp0(rc, 0);
                 const int rs = rp0.raw_slot;
@@ -619,7 +717,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 template <class C, typename OP>
 int launch(const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx, int M, int N, int K,
-           void* y, int ytype, const GemmGroups& grp, int64_t max_tiles, cudaStream_t st) {
+           void* y, int ytype, const GemmGroups& grp, int64_t max_units, int sms,
+           cudaStream_t st) {
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc<C, OP>,
@@ -627,9 +726,7 @@ int launch(const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx, int M
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm_q4k_tc)");
         configured = true;
     }
-    static int sms = 0;
-    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_tiles, sms));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_units, sms));
     gemm_q4k_tc<C, OP><<<grid, C::THREADS, C::SMEM, st>>>(tw, tw2, tx, M, N, K, y, ytype, grp);
     return FTC_OK;
 }
@@ -673,10 +770,108 @@ int act_maps(XMaps* mx, const void* x, int x_dtype, int64_t rows, int64_t K, int
     return FTC_OK;
 }
 
+// ------------------------------------------------------------- split-K
+
+// Units (tiles x splits) of one launch are capped at kUnitsPerSm per SM; the
+// per-device scratch holds the partials and arrival counters of that many.
+constexpr int kUnitsPerSm = 4;
+constexpr int kMaxSplits = 16;
+constexpr int kMinSbPerSplit = 2;
+
+struct SplitScratch {
+    int units = 0;  // capacity in units (0: none)
+    uint32_t* counters = nullptr;
+    float* part = nullptr;
+};
+
+std::mutex g_split_mu;
+SplitScratch g_split[64];  // per device
+
+int device_sms() {
+    static int sms[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    return sms[dev] > 0 ? sms[dev] : 148;
+}
+
+// The device's split-K scratch, allocated on first use (never freed, never
+// moved: graphs that captured its address stay valid).  Inside a stream
+// capture nothing can be allocated; *out stays empty and the caller runs
+// without splits.
+int split_scratch(cudaStream_t st, int sms, SplitScratch* out) {
+    int dev = 0;
+    FTC_CUDA(cudaGetDevice(&dev));
+    FTC_REQUIRE(dev >= 0 && dev < 64, FTC_E_CUDA, "gemm split-K: device index out of range");
+    std::lock_guard<std::mutex> lk(g_split_mu);
+    SplitScratch& sc = g_split[dev];
+    if (!sc.units) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        FTC_CUDA(cudaStreamIsCapturing(st, &cs));
+        if (cs != cudaStreamCaptureStatusNone) {
+            *out = SplitScratch{};
+            return FTC_OK;
+        }
+        const int units = kUnitsPerSm * sms;
+        const size_t cnt_bytes = ((size_t)units * kEpiWarps * 4 + 255) & ~size_t(255);
+        const size_t part_bytes = (size_t)units * BM * 256 * 4;
+        void* p = nullptr;
+        FTC_CUDA(cudaMalloc(&p, cnt_bytes + part_bytes));
+        const cudaError_t e = cudaMemset(p, 0, cnt_bytes);
+        if (e != cudaSuccess) {
+            cudaFree(p);
+            return cuda_error(e, "cudaMemset(gemm split-K counters)");
+        }
+        sc.counters = static_cast<uint32_t*>(p);
+        sc.part = reinterpret_cast<float*>(static_cast<uint8_t*>(p) + cnt_bytes);
+        sc.units = units;
+    }
+    *out = sc;
+    return FTC_OK;
+}
+
+// Splits for `tiles` output tiles of nsb super-blocks and up to tile_rows
+// token rows each on `sms` SMs: the one that minimizes, in units of one
+// super-block step (~2 us), waves x (super-blocks per unit + one for the
+// pipeline fill and epilogue) plus the fix-up of the last unit of a tile
+// (one L2 round trip, ~1/4 step, per 16 rows and 4 splits).
+int choose_splits(int64_t tiles, int nsb, int tile_rows, int sms) {
+    auto cost = [&](int S) {
+        const int64_t waves = (tiles * S + sms - 1) / sms;
+        const double fix = S > 1 ? 0.5 + 0.25 * ((S + 3) / 4) * ((tile_rows + 15) / 16) : 0.0;
+        return (double)waves * ((nsb + S - 1) / S + 1) + fix;
+    };
+    int best = 1;
+    double best_cost = cost(1);
+    for (int S = 2; S <= kMaxSplits; ++S) {
+        if (nsb < kMinSbPerSplit * S || tiles * S > (int64_t)kUnitsPerSm * sms) break;
+        const double c = cost(S);
+        if (c < best_cost) best = S, best_cost = c;
+    }
+    return best;
+}
+
 int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx,
-             int M, int N, int K, void* y, int y_dtype, const GemmGroups& grp, int64_t max_tiles,
-             cudaStream_t st) {
+             int M, int N, int K, void* y, int y_dtype, GemmGroups grp, int64_t max_tiles,
+             int tile_rows, cudaStream_t st) {
     const bool bf = x_dtype == FTC_BF16;
+    const int sms = device_sms();
+    const int S = choose_splits(max_tiles, K / 256, std::min(tile_rows, BN), sms);
+    grp.splits = 1;
+    grp.counters = nullptr;
+    grp.part = nullptr;
+    if (S > 1) {
+        SplitScratch sc;
+        const int rc = split_scratch(st, sms, &sc);
+        if (rc != FTC_OK) return rc;
+        if (sc.units >= max_tiles * S) {
+            grp.splits = S;
+            grp.counters = sc.counters;
+            grp.part = sc.part;
+        }
+    }
+    const int64_t units = max_tiles * grp.splits;
     // small token counts: A stages in tensor memory (no shared-memory A
     // stores or A reads by the MMA); large: the 256-token tile, which halves
     // the weight traffic per FLOP and needs all 512 TMEM columns for its two
@@ -685,15 +880,38 @@ int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2,
     using C256 = Cfg<256, 1, 3, 3, 3>;
     int rc;
     if (BN == 128)
-        rc = bf ? launch<C128, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
-                : launch<C128, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
+        rc = bf ? launch<C128, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st)
+                : launch<C128, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st);
     else
-        rc = bf ? launch<C256, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st)
-                : launch<C256, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, max_tiles, st);
+        rc = bf ? launch<C256, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st)
+                : launch<C256, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st);
     if (rc != FTC_OK) return rc;
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;
 }
+
+}  // namespace
+
+// Status reader of this file's kernels.  Clearing a recorded timeout also
+// zeroes the split-K arrival counters, which a launch that gave up part way
+// may have left uneven.
+int devstat_gemm_q4k(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_dev_status, sizeof(int)) != cudaSuccess) return -1;
+    if (clear && v) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(g_dev_status, &z, sizeof(int)) != cudaSuccess) return -1;
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+        std::lock_guard<std::mutex> lk(g_split_mu);
+        const SplitScratch& sc = g_split[dev];
+        if (sc.units && cudaMemset(sc.counters, 0, (size_t)sc.units * kEpiWarps * 4) != cudaSuccess)
+            return -1;
+    }
+    return v;
+}
+
+namespace {
 
 int check_types(int x_dtype, int y_dtype, const char* who) {
     FTC_REQUIRE(x_dtype == FTC_BF16 || x_dtype == FTC_F16, FTC_E_UNSUPPORTED,
@@ -723,9 +941,10 @@ int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void
     if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm"))) return rc;
     if ((rc = act_maps(&tx, x, x_dtype, M, K, BN, "ftc_gemm"))) return rc;
     if (inject_fail("ftc_gemm")) return set_error(FTC_E_INJECTED, "ftc_gemm: injected failure");
-    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, nullptr};
+    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, nullptr, 1, nullptr, nullptr};
     const int64_t tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
-    return dispatch(BN, x_dtype, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles, st);
+    return dispatch(BN, x_dtype, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles,
+                    (int)std::min<int64_t>(M, BN), st);
 }
 
 // Dense GEMM on fp16 rows scaled by 2^-row_exp (ftc_rows_to_f16), output
@@ -748,9 +967,10 @@ int gemm_q4k_rowscaled(const void* w, int64_t N, int64_t K, int64_t row_stride, 
     if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm_rowscaled")))
         return rc;
     if ((rc = act_maps(&tx, x16, FTC_F16, M, K, BN, "ftc_gemm_rowscaled"))) return rc;
-    GemmGroups grp = {nullptr, nullptr, 1, 1, N, row_exp};
+    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, row_exp, 1, nullptr, nullptr};
     const int64_t tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
-    return dispatch(BN, FTC_F16, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles, st);
+    return dispatch(BN, FTC_F16, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles,
+                    (int)std::min<int64_t>(M, BN), st);
 }
 
 // Grouped form: rows of x are grouped by expert (device counts / offsets);
@@ -786,12 +1006,12 @@ int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64
         (rc = weight_map(&tw2, w2, N, K, row_stride, G, plane_stride, "gemm_q4k_grouped")))
         return rc;
     if ((rc = act_maps(&tx, x, x_dtype, rows, K, BN, "gemm_q4k_grouped"))) return rc;
-    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy, row_exp};
+    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy, row_exp, 1, nullptr, nullptr};
     // upper bound on tiles: every non-empty group adds at most one partial token tile
     const int64_t tok_tiles = (rows + BN - 1) / BN + std::min<int64_t>(G, rows);
     const int64_t tiles = tok_tiles * ((N + BM - 1) / BM) * n_sets;
     return dispatch(BN, x_dtype, tw, n_sets == 2 ? tw2 : tw, tx, (int)rows, (int)N, (int)K, y,
-                    y_dtype, grp, tiles, st);
+                    y_dtype, grp, tiles, (int)std::min<int64_t>(max_rows_per_group, BN), st);
 }
 
 }  // namespace ftc
