@@ -86,6 +86,42 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
+// One 256-block of x (lane j holds elements 8j..8j+7): block scale, three
+// byte planes and the sub-block sums.
+__device__ __forceinline__ void plane_block(const float (&v)[8], int sb, int lane, uint32_t* planes,
+                                            float* sums, float* scales) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    // amax in [2^p, 2^(p+1)): s_b = 2^(p-21) keeps |x / s_b| < 2^22
+    const int eb = (int)((__float_as_uint(amax) >> 23) & 0xFF);
+    const int se = max(eb - 21, 1);
+    const float inv = __uint_as_float((uint32_t)(254 - se) << 23);
+    uint32_t h[2] = {0, 0}, m[2] = {0, 0}, l[2] = {0, 0};
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        // round(x * inv) via the 1.5 * 2^23 magic constant (x * inv is exact)
+        const int q = __float_as_int(fmaf(v[i], inv, 12582912.0f)) - 0x4B400000;
+        sum += q;
+        h[i >> 2] |= ((uint32_t)(q >> 16) & 0xFFu) << (8 * (i & 3));
+        m[i >> 2] |= ((uint32_t)(q >> 8) & 0xFFu) << (8 * (i & 3));
+        l[i >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (i & 3));
+    }
+    const int t = lane >> 3, u = 2 * (lane & 7);
+    uint32_t* dst = planes + (sb * 4 + t) * kPlaneWords;
+    *reinterpret_cast<uint2*>(dst + u) = make_uint2(h[0], h[1]);
+    *reinterpret_cast<uint2*>(dst + 16 + u) = make_uint2(m[0], m[1]);
+    *reinterpret_cast<uint2*>(dst + 32 + u) = make_uint2(l[0], l[1]);
+    // sub-block sums: lanes 8t..8t+3 hold sub-block 2t, 8t+4..8t+7 sub-block 2t+1
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if ((lane & 3) == 0) sums[(sb * 4 + t) * 2 + ((lane >> 2) & 1)] = (float)sum;
+    if (lane == 0) scales[sb] = __uint_as_float((uint32_t)se << 23);
+}
+
 // Per-CTA activation prologue: consumer warp w converts super-blocks w,
 // w + NCW, ... (lane j: elements 8j..8j+7 of the block) into plane words,
 // sub-block sums and the block scale, laid out for the consumers:
@@ -94,40 +130,27 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 __device__ __forceinline__ void build_planes(const float* __restrict__ x, int nsb, int cw, int ncw,
                                              int lane, uint32_t* planes, float* sums,
                                              float* scales) {
-    for (int sb = cw; sb < nsb; sb += ncw) {
-        const float4* xp = reinterpret_cast<const float4*>(x + (int64_t)sb * 256 + 8 * lane);
-        const float4 a = __ldg(xp), b = __ldg(xp + 1);
-        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        float amax = 0.f;
+    // the warp's blocks go four at a time: all loads of a batch are in
+    // flight together, so a long x costs one L2 round trip per batch
+    constexpr int kBatch = 4;
+    for (int sb0 = cw; sb0 < nsb; sb0 += kBatch * ncw) {
+        float4 a[kBatch], b[kBatch];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        // amax in [2^p, 2^(p+1)): s_b = 2^(p-21) keeps |x / s_b| < 2^22
-        const int eb = (int)((__float_as_uint(amax) >> 23) & 0xFF);
-        const int se = max(eb - 21, 1);
-        const float inv = __uint_as_float((uint32_t)(254 - se) << 23);
-        uint32_t h[2] = {0, 0}, m[2] = {0, 0}, l[2] = {0, 0};
-        int sum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            // round(x * inv) via the 1.5 * 2^23 magic constant (x * inv is exact)
-            const int q = __float_as_int(fmaf(v[i], inv, 12582912.0f)) - 0x4B400000;
-            sum += q;
-            h[i >> 2] |= ((uint32_t)(q >> 16) & 0xFFu) << (8 * (i & 3));
-            m[i >> 2] |= ((uint32_t)(q >> 8) & 0xFFu) << (8 * (i & 3));
-            l[i >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (i & 3));
+        for (int i = 0; i < kBatch; ++i) {
+            const int sb = sb0 + i * ncw;
+            if (sb < nsb) {
+                const float4* xp = reinterpret_cast<const float4*>(x + (int64_t)sb * 256 + 8 * lane);
+                a[i] = __ldg(xp);
+                b[i] = __ldg(xp + 1);
+            }
         }
-        const int t = lane >> 3, u = 2 * (lane & 7);
-        uint32_t* dst = planes + (sb * 4 + t) * kPlaneWords;
-        *reinterpret_cast<uint2*>(dst + u) = make_uint2(h[0], h[1]);
-        *reinterpret_cast<uint2*>(dst + 16 + u) = make_uint2(m[0], m[1]);
-        *reinterpret_cast<uint2*>(dst + 32 + u) = make_uint2(l[0], l[1]);
-        // sub-block sums: lanes 8t..8t+3 hold sub-block 2t, 8t+4..8t+7 sub-block 2t+1
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        if ((lane & 3) == 0) sums[(sb * 4 + t) * 2 + ((lane >> 2) & 1)] = (float)sum;
-        if (lane == 0) scales[sb] = __uint_as_float((uint32_t)se << 23);
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const int sb = sb0 + i * ncw;
+            if (sb >= nsb) break;
+            const float v[8] = {a[i].x, a[i].y, a[i].z, a[i].w, b[i].x, b[i].y, b[i].z, b[i].w};
+            plane_block(v, sb, lane, planes, sums, scales);
+        }
     }
 }
 
