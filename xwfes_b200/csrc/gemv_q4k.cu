@@ -43,7 +43,12 @@ FTC_DEVSTAT_READER(devstat_gemv_q4k)
 namespace {
 
 constexpr int kStages = 4;
-constexpr int kPlaneWords = 48;  // per (super-block, quartet lane): 3 planes x 16 words
+// Activation words per (super-block, quartet lane): 3 planes x 16 words,
+// padded to 52 so that the 128-bit loads of 8 consecutive lanes (stride 52
+// words = 20 banks mod 32) fall on 8 different bank quads; at 48 words they
+// would collide 4-way and the 18 consumer warps' start-up loads would take
+// ~2 us of shared-memory time per launch.
+constexpr int kPlaneWords = 52;
 constexpr int kMaxThreads = 608; // 18 consumer warps + 1 producer at <= 107 registers
 
 }  // namespace
@@ -125,7 +130,7 @@ __device__ __forceinline__ void plane_block(const float (&v)[8], int sb, int lan
 // Per-CTA activation prologue: consumer warp w converts super-blocks w,
 // w + NCW, ... (lane j: elements 8j..8j+7 of the block) into plane words,
 // sub-block sums and the block scale, laid out for the consumers:
-//   planes[(sb*4 + t)*48 + plane*16 + u]   u = word within the lane's 64
+//   planes[(sb*4 + t)*kPlaneWords + plane*16 + u]   u = word within the lane's 64
 //   sums[(sb*4 + t)*2 + {0: low sub-block, 1: high}],  scales[sb]
 __device__ __forceinline__ void build_planes(const float* __restrict__ x, int nsb, int cw, int ncw,
                                              int lane, uint32_t* planes, float* sums,
