@@ -50,6 +50,7 @@ constexpr int kStages = 4;
 // ~2 us of shared-memory time per launch.
 constexpr int kPlaneWords = 52;
 constexpr int kMaxThreads = 608; // 18 consumer warps + 1 producer at <= 107 registers
+constexpr size_t kMaxSmem = 227 * 1024;  // dynamic shared memory per CTA (the sm_100 limit)
 
 }  // namespace
 
@@ -477,12 +478,12 @@ bool plan_q4k(int64_t Ntot, int64_t K, int64_t stride, Q4kPlan& p) {
              + (size_t)nsb * 9 * 4                         // sums + scales
              + (size_t)2 * kStages * p.WK * RC * 4         // partials, two rounds
              + 16 + 2 * kStages * 8;                        // barriers
-    while (p.smem > 220 * 1024 && p.RPW > 1) {             // shrink chunks to fit
+    while (p.smem > kMaxSmem && p.RPW > 1) {               // shrink chunks to fit
         p.smem -= (size_t)kStages * (p.RPW / 2) * p.WR * stride;
         p.smem -= (size_t)2 * kStages * p.WK * (p.RPW / 2) * p.WR * 4;
         p.RPW /= 2;
     }
-    if (p.smem > 220 * 1024 || p.threads > kMaxThreads) return false;
+    if (p.smem > kMaxSmem || p.threads > kMaxThreads) return false;
     p.RC = p.RPW * p.WR;
     return true;
 }
@@ -586,7 +587,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     auto launch = [&](auto kern, int idx) -> int {
         if (!configured[idx]) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 220 * 1024);
+                                                 (int)kMaxSmem);
             if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemv_q4k_dp4a)");
             configured[idx] = true;
         }
