@@ -383,6 +383,9 @@ TP_M = [1, 16, 1024]
 L2_BYTES = 126 * 2**20
 
 
+TP_PEER_M = 16
+
+
 def time_tp(dev, world, rank, seed=0):
     """Config 4: the Llama-3-70B-shaped Q4_K block (q, k, v, o, gate, up,
     down), tensor-parallel over the `world` GPUs (strong scaling: the block's
@@ -393,11 +396,15 @@ def time_tp(dev, world, rank, seed=0):
     import torch
     import torch.distributed as dist
     from xwfes_b200 import tp
+    from xwfes_b200 import ftc
     d = tp.DIMS_70B
     ops = tp.CudaOps(dev)
     shard_b = tp.weight_bytes(d) // world
     copies = min(4, max(1, -(-2 * L2_BYTES // shard_b)))
-    blocks = [tp.TPBlock.build(d, world, rank, ops, tp.rank_shards(d, world, rank, seed=seed + c))
+    # partials of up to TP_PEER_M tokens go through the NVLink peer allreduce
+    peer = ftc.PeerAllreduce(TP_PEER_M * d["n_embd"]) if world > 1 else None
+    blocks = [tp.TPBlock.build(d, world, rank, ops, tp.rank_shards(d, world, rank, seed=seed + c),
+                               peer=peer)
               for c in range(copies)]
     out = {}
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -440,10 +447,14 @@ def time_tp(dev, world, rank, seed=0):
                        "weight_GBps": round(tp.weight_bytes(d) / (us * 1e-6) / 1e9, 1),
                        "tflops": round(tp.flops(d, M) / (us * 1e-6) / 1e12, 2)}
     del blocks
+    if peer is not None:
+        dist.barrier(device_ids=[dev.index])  # no rank still writes into a peer's buffer
+        peer.close()
     return {"workload": "config 4: Llama-3-70B-shaped Q4_K block (q 8192x8192, k/v 1024x8192, "
                         "o 8192x8192, gate/up 28672x8192, down 8192x28672), fp32 activations",
             "parallelism": f"tp{world} (column-parallel q/k/v/gate/up, row-parallel o/down, "
-                           "NCCL allreduce of fp32 partials after o and down)",
+                           f"allreduce of fp32 partials after o and down: one-shot over NVLink "
+                           f"peer memory (ftc_peer_ar) for M <= {TP_PEER_M}, NCCL above)",
             "scaling": "strong (the whole block's work is split over the GPUs)",
             "weight_bytes": tp.weight_bytes(d), "weight_copies_rotated": copies,
             "kernels": "M<=8: decode GEMV (fp32); M>8: tcgen05 GEMM on row-scaled fp16",

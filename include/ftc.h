@@ -293,6 +293,33 @@ int ftc_expert_chunk_static(int dtype, const float* x, float* out, const void* g
                             const void* up, const void* down, int64_t M, int64_t K, int64_t IC,
                             int64_t gate_up_row_stride, int64_t down_row_stride, void* stream);
 
+/* ---- tensor-parallel exchange: allreduce over NVLink peer memory ----
+ *
+ * One-shot allreduce (sum) of fp32 vectors between the ranks of a
+ * tensor-parallel group, one process per GPU.  The row-parallel matmuls of
+ * the tensor-parallel block (config 4) produce [M, n_embd] fp32 partials
+ * that every rank needs summed; the reference has no such step (one process
+ * runs every matmul, ft/src/engine.cpp:485-600).  Each rank's CTAs store
+ * their slice into every rank's buffer, raise per-block flags and sum the
+ * slots in rank order, so every rank gets the same bits.  Meant for small
+ * vectors (up to a few MB); use NCCL for large ones.
+ *
+ * Setup: every rank calls ftc_peer_ar_create (same world and max_elems),
+ * the FTC_IPC_HANDLE_BYTES handles are exchanged out of band (e.g. an
+ * all-gather over the process group) and every rank calls ftc_peer_ar_open
+ * with all handles in rank order.  Calls must then be made by every rank in
+ * the same order (stream-ordered on each rank; CUDA-graph capture is fine).
+ * A rank that does not join a call makes the others' kernels give up after
+ * the library's wait bound and record status 1 (ftc_device_status). */
+#define FTC_IPC_HANDLE_BYTES 64
+typedef struct ftc_peer_ar ftc_peer_ar;
+int ftc_peer_ar_create(int rank, int world, int64_t max_elems, ftc_peer_ar** out, void* handle);
+int ftc_peer_ar_open(ftc_peer_ar* ar, const void* handles);
+int64_t ftc_peer_ar_max_elems(const ftc_peer_ar* ar);
+/* out[i] = sum over ranks of in[i], i < n <= max_elems; out may equal in. */
+int ftc_peer_ar_sum_f32(ftc_peer_ar* ar, const float* in, float* out, int64_t n, void* stream);
+int ftc_peer_ar_destroy(ftc_peer_ar* ar);
+
 #ifdef __cplusplus
 }
 #endif

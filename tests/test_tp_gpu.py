@@ -90,16 +90,20 @@ torch.cuda.set_device(rank)
 import datetime
 dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                         device_id=torch.device("cuda", rank))
+from xwfes_b200 import ftc
 d = {dims!r}
 w = tp.full_weights(d, seed=2)
+peer = ftc.PeerAllreduce(16 * d["n_embd"]) if {peer!r} else None
 blk = tp.TPBlock.build(d, world, rank, tp.CudaOps(torch.device("cuda", rank)),
-                       tp.shard(w, d, world, rank))
-for M in (1, 16):
+                       tp.shard(w, d, world, rank), peer=peer)
+for M in (1, 16, 40):
     x = np.random.default_rng(M).standard_normal((M, d["n_embd"])).astype(np.float32)
     out, _ = blk.forward(torch.from_numpy(x).cuda())
     torch.cuda.synchronize()
     np.save(os.path.join({out!r}, f"out{{M}}_{{rank}}.npy"), out.cpu().numpy())
 dist.barrier()
+if peer is not None:
+    peer.close()
 dist.destroy_process_group()
 """
 
@@ -114,8 +118,11 @@ def _free_port():
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_two_gpus_nccl(oracle, weights, tmp_path):
-    code = _CHILD.format(root=ROOT, dims=MID, out=str(tmp_path))
+@pytest.mark.parametrize("peer", [False, True], ids=["nccl", "peer_allreduce"])
+def test_two_gpus(oracle, weights, tmp_path, peer):
+    """Two ranks on two GPUs; the row-parallel partials summed by NCCL, or
+    (peer) by ftc_peer_ar for M <= 16 and NCCL for M = 40."""
+    code = _CHILD.format(root=ROOT, dims=MID, out=str(tmp_path), peer=peer)
     port = _free_port()
     procs = []
     for r in range(2):
@@ -124,7 +131,7 @@ def test_two_gpus_nccl(oracle, weights, tmp_path):
         procs.append(subprocess.Popen([sys.executable, "-c", code], env=env, cwd=ROOT))
     for p in procs:
         assert p.wait(timeout=300) == 0
-    for M in (1, 16):
+    for M in (1, 16, 40):
         o0, o1 = (np.load(tmp_path / f"out{M}_{r}.npy") for r in range(2))
         assert np.array_equal(o0, o1)
         ref = oracle_block(oracle, weights, MID, np.random.default_rng(M).standard_normal(

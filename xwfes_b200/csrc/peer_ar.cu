@@ -1,0 +1,254 @@
+// peer_ar.cu -- one-shot allreduce of fp32 partials over NVLink peer memory,
+// for the small row-parallel outputs of the tensor-parallel block (config 4:
+// the [M, n_embd] partials of o and down, 32 KB per rank at M = 1).
+//
+// The reference has no tensor parallelism (one process runs every matmul of
+// ft/src/engine.cpp:485-600); the allreduce is the exchange step the
+// row-parallel split adds.  At these sizes an allreduce is all latency, so
+// the exchange carries its own completion flags: every fp32 value travels
+// with the call's epoch in the same 8-byte word (value bits low, epoch
+// high), written with one store, so a reader that sees the epoch also sees
+// the value -- no memory fence and no separate flag round trip.
+//
+// Layout.  Every rank owns one device region, mapped by every other rank
+// through a CUDA IPC handle:
+//   data  [2 parities][world source ranks][max_elems] u64 (value | epoch << 32)
+//   ctr   [kArBlocks] uint32   (this rank's call counter per block)
+// A call runs kArBlocks CTAs; CTA b owns slice b of the vector.  It
+//   1. stores its slice of `in` into slot [parity][rank] of every rank's data
+//      (its own included) -- 8-byte stores to peer addresses over NVLink;
+//   2. reads its slice of every source slot of its own region, waiting per
+//      word until the word carries this call's epoch (bounded in time);
+//   3. sums the sources in rank order 0, 1, ... world-1 into `out`.
+// Every rank adds the same values in the same order, so all ranks hold the
+// same bits.  The epoch is the per-block call counter kept in device memory
+// (graph replays advance it), and the two parities keep a rank that has
+// moved on to the next call from overwriting a slot a slower peer is still
+// reading: a rank can only be one call ahead, because finishing a call needs
+// every peer's words of that call.
+//
+// A peer that never arrives makes the wait give up after the same bound as
+// every other wait of this library (FTC_DEVSTAT_WAIT_TIMEOUT) and the CTA
+// returns without writing its slice.
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace ftc {
+
+FTC_DEVSTAT_READER(devstat_peer_ar)
+
+namespace {
+
+constexpr int kArBlocks = 148;  // one CTA per SM, every call (the call counters are per CTA)
+constexpr int kArThreads = 256;
+constexpr int kArBatch = 4;     // elements a thread gathers at once
+constexpr int kArMaxRanks = 8;
+
+struct ArPeers {
+    uint64_t* data[kArMaxRanks];  // each rank's data region (this rank's own included)
+};
+
+__device__ __forceinline__ void st_word(uint64_t* p, uint64_t v) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kArThreads)
+peer_ar_f32(const __grid_constant__ ArPeers P, int rank, int world, int64_t max_elems,
+            const float* __restrict__ in, float* __restrict__ out, int64_t n,
+            uint32_t* __restrict__ ctr) {
+    const int b = blockIdx.x;
+    __shared__ uint32_t s_epoch;
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        s_epoch = ctr[b] + 1u;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
+    const int par = (int)(epoch & 1u);
+    const int64_t i0 = n * b / kArBlocks, i1 = n * (b + 1) / kArBlocks;
+    const int64_t slot = ((int64_t)par * world + rank) * max_elems;
+    const uint64_t tag = (uint64_t)epoch << 32;
+
+    // 1. push this rank's slice to every rank
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += kArThreads) {
+        const uint64_t w = tag | __float_as_uint(in[i]);
+        for (int q = 0; q < world; ++q) st_word(P.data[q] + slot + i, w);
+    }
+    // 2. + 3. gather every source's word of each element (a thread keeps the
+    // loads of kArBatch elements x all sources in flight together), then sum
+    // in rank order
+    const uint64_t* d = P.data[rank] + (int64_t)par * world * max_elems;
+    volatile int* ok = &s_ok;
+    uint64_t t0 = 0;
+    for (int64_t base = i0 + threadIdx.x; base < i1 && *ok; base += kArThreads * kArBatch) {
+        uint64_t w[kArBatch][kArMaxRanks];
+        uint32_t pending = 0;  // bit e * kArMaxRanks + s: word (element e, source s) not seen yet
+#pragma unroll
+        for (int e = 0; e < kArBatch; ++e)
+            if (base + e * kArThreads < i1) pending |= ((1u << world) - 1u) << (e * kArMaxRanks);
+        while (pending) {
+#pragma unroll
+            for (int e = 0; e < kArBatch; ++e)
+#pragma unroll
+                for (int s = 0; s < kArMaxRanks; ++s)
+                    if ((pending >> (e * kArMaxRanks + s)) & 1u)
+                        w[e][s] = ld_word(d + s * max_elems + base + e * kArThreads);
+#pragma unroll
+            for (int e = 0; e < kArBatch; ++e)
+#pragma unroll
+                for (int s = 0; s < kArMaxRanks; ++s)
+                    if (((pending >> (e * kArMaxRanks + s)) & 1u) && (w[e][s] >> 32) == epoch)
+                        pending &= ~(1u << (e * kArMaxRanks + s));
+            if (pending) {
+                const uint64_t now = global_ns();
+                if (t0 == 0) {
+                    t0 = now;
+                } else if (now - t0 > kWaitLimitNs) {
+                    record_timeout();
+                    *ok = 0;
+                }
+                if (!*ok) break;
+            }
+        }
+        if (pending) break;
+#pragma unroll
+        for (int e = 0; e < kArBatch; ++e) {
+            const int64_t i = base + e * kArThreads;
+            if (i >= i1) break;
+            float a = __uint_as_float((uint32_t)w[e][0]);
+#pragma unroll
+            for (int s = 1; s < kArMaxRanks; ++s)
+                if (s < world) a += __uint_as_float((uint32_t)w[e][s]);
+            out[i] = a;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ctr[b] = epoch;
+}
+
+}  // namespace
+
+}  // namespace ftc
+
+struct ftc_peer_ar {
+    int rank = 0, world = 0, device = 0;
+    int64_t max_elems = 0;
+    void* base = nullptr;  // this rank's region
+    uint32_t* ctr = nullptr;
+    void* peer_base[ftc::kArMaxRanks] = {};  // opened IPC mappings (nullptr for self)
+    ftc::ArPeers peers = {};
+    bool open = false;
+};
+
+namespace {
+
+size_t region_bytes(int world, int64_t max_elems) {
+    const size_t data = (size_t)2 * world * max_elems * sizeof(uint64_t);
+    return ((data + 255) & ~size_t(255)) + ftc::kArBlocks * sizeof(uint32_t);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ftc_peer_ar_create(int rank, int world, int64_t max_elems, ftc_peer_ar** out, void* handle) {
+    using namespace ftc;
+    FTC_REQUIRE(out && handle, FTC_E_INVALID, "ftc_peer_ar_create: null pointer");
+    FTC_REQUIRE(world >= 1 && world <= kArMaxRanks && rank >= 0 && rank < world, FTC_E_INVALID,
+                "ftc_peer_ar_create: 1..8 ranks, 0 <= rank < world");
+    FTC_REQUIRE(max_elems > 0 && max_elems <= ((int64_t)1 << 28), FTC_E_INVALID,
+                "ftc_peer_ar_create: max_elems must be in 1..2^28");
+    if (inject_fail("ftc_peer_ar_create"))
+        return set_error(FTC_E_INJECTED, "ftc_peer_ar_create: injected failure");
+    auto* ar = new ftc_peer_ar();
+    ar->rank = rank;
+    ar->world = world;
+    ar->max_elems = max_elems;
+    cudaError_t e = cudaGetDevice(&ar->device);
+    const size_t bytes = region_bytes(world, max_elems);
+    if (e == cudaSuccess) e = cudaMalloc(&ar->base, bytes);
+    if (e == cudaSuccess) e = cudaMemset(ar->base, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, ar->base);
+    if (e != cudaSuccess) {
+        if (ar->base) cudaFree(ar->base);
+        delete ar;
+        return cuda_error(e, "ftc_peer_ar_create");
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    ar->ctr = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ar->base) + bytes -
+                                          kArBlocks * sizeof(uint32_t));
+    *out = ar;
+    return ok();
+}
+
+int ftc_peer_ar_open(ftc_peer_ar* ar, const void* handles) {
+    using namespace ftc;
+    FTC_REQUIRE(ar && handles, FTC_E_INVALID, "ftc_peer_ar_open: null pointer");
+    FTC_REQUIRE(!ar->open, FTC_E_INVALID, "ftc_peer_ar_open: already open");
+    for (int q = 0; q < ar->world; ++q) {
+        void* p = ar->base;
+        if (q != ar->rank) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const uint8_t*>(handles) + q * FTC_IPC_HANDLE_BYTES,
+                        sizeof(h));
+            const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                for (int j = 0; j < q; ++j)
+                    if (ar->peer_base[j]) cudaIpcCloseMemHandle(ar->peer_base[j]);
+                return cuda_error(e, "ftc_peer_ar_open: cudaIpcOpenMemHandle");
+            }
+            ar->peer_base[q] = p;
+        }
+        ar->peers.data[q] = static_cast<uint64_t*>(p);
+    }
+    ar->open = true;
+    return ok();
+}
+
+int64_t ftc_peer_ar_max_elems(const ftc_peer_ar* ar) { return ar ? ar->max_elems : 0; }
+
+int ftc_peer_ar_sum_f32(ftc_peer_ar* ar, const float* in, float* out, int64_t n, void* stream) {
+    using namespace ftc;
+    FTC_REQUIRE(ar && in && out, FTC_E_INVALID, "ftc_peer_ar_sum_f32: null pointer");
+    FTC_REQUIRE(ar->open, FTC_E_INVALID, "ftc_peer_ar_sum_f32: ftc_peer_ar_open not called");
+    FTC_REQUIRE(n >= 0 && n <= ar->max_elems, FTC_E_INVALID,
+                "ftc_peer_ar_sum_f32: n exceeds the buffer's max_elems");
+    if (n == 0) return ok();
+    if (inject_fail("ftc_peer_ar_sum_f32"))
+        return set_error(FTC_E_INJECTED, "ftc_peer_ar_sum_f32: injected failure");
+    peer_ar_f32<<<kArBlocks, kArThreads, 0, (cudaStream_t)stream>>>(
+        ar->peers, ar->rank, ar->world, ar->max_elems, in, out, n, ar->ctr);
+    FTC_CUDA(cudaGetLastError());
+    return ok();
+}
+
+int ftc_peer_ar_destroy(ftc_peer_ar* ar) {
+    using namespace ftc;
+    if (!ar) return ok();
+    cudaError_t first = cudaSuccess;
+    for (int q = 0; q < ar->world; ++q)
+        if (ar->peer_base[q]) {
+            const cudaError_t e = cudaIpcCloseMemHandle(ar->peer_base[q]);
+            if (first == cudaSuccess) first = e;
+        }
+    if (ar->base) {
+        const cudaError_t e = cudaFree(ar->base);
+        if (first == cudaSuccess) first = e;
+    }
+    delete ar;
+    if (first != cudaSuccess) return cuda_error(first, "ftc_peer_ar_destroy");
+    return ok();
+}
+
+}  // extern "C"

@@ -54,6 +54,11 @@ SIGNATURES = {
     "ftc_moe_experts": (C.c_int, [_p, _p, C.c_int, _i64, _p, _p, _i64, _p, _p, C.c_size_t, _p]),
     "ftc_moe_workspace_bytes": (C.c_size_t, [_p, _i64]),
     "ftc_moe_ffn": (C.c_int, [_p, _p, _p, C.c_int, _i64, _p, _p, C.c_size_t, _p]),
+    "ftc_peer_ar_create": (C.c_int, [C.c_int, C.c_int, _i64, C.POINTER(_p), _p]),
+    "ftc_peer_ar_open": (C.c_int, [_p, _p]),
+    "ftc_peer_ar_max_elems": (_i64, [_p]),
+    "ftc_peer_ar_sum_f32": (C.c_int, [_p, _p, _p, _i64, _p]),
+    "ftc_peer_ar_destroy": (C.c_int, [_p]),
 }
 
 
@@ -467,3 +472,47 @@ class CudaBackend:
 
     def sync(self):
         check(lib().ftc_backend_sync(self._h), "ftc_backend_sync")
+
+
+IPC_HANDLE_BYTES = 64  # FTC_IPC_HANDLE_BYTES in include/ftc.h
+
+
+class PeerAllreduce:
+    """Sum of fp32 vectors over the ranks of a process group through NVLink
+    peer memory (ftc_peer_ar_*): one process per GPU, small vectors.  The
+    CUDA IPC handles are exchanged with an all-gather over ``group``."""
+
+    def __init__(self, max_elems, group=None):
+        import torch
+        import torch.distributed as dist
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.max_elems = int(max_elems)
+        h = (C.c_uint8 * IPC_HANDLE_BYTES)()
+        ptr = _p()
+        check(lib().ftc_peer_ar_create(self.rank, self.world, self.max_elems, C.byref(ptr), h),
+              "ftc_peer_ar_create")
+        self._ar = ptr
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        allh = (C.c_uint8 * (IPC_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
+        check(lib().ftc_peer_ar_open(self._ar, allh), "ftc_peer_ar_open")
+        # every rank has mapped every other rank's buffer before the first call
+        dist.barrier(group=group)
+        self.torch = torch
+
+    def fits(self, t):
+        return t.dtype == self.torch.float32 and t.is_contiguous() and t.numel() <= self.max_elems
+
+    def sum_(self, t, stream=None):
+        """In-place sum of the fp32 CUDA tensor ``t`` over the ranks."""
+        if not self.fits(t):
+            raise ValueError("PeerAllreduce: contiguous fp32 tensor of at most max_elems")
+        check(lib().ftc_peer_ar_sum_f32(self._ar, t.data_ptr(), t.data_ptr(), t.numel(),
+                                        _stream(stream)), "ftc_peer_ar_sum_f32")
+        return t
+
+    def close(self):
+        if self._ar:
+            check(lib().ftc_peer_ar_destroy(self._ar), "ftc_peer_ar_destroy")
+            self._ar = None

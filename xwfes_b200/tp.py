@@ -23,7 +23,10 @@ Every rank uploads only its own shard (contiguous GGUF blocks; a K slice of a
 row is a run of whole super-blocks).  Matmuls: M <= 8 tokens use the decode
 GEMV (fp32 activations), larger M the tcgen05 GEMM on fp16 rows with
 power-of-two row scales (ftc_rows_to_f16 / ftc_gemm_rowscaled), fp32 outputs.
-The allreduce sums fp32 partials (NCCL on GPUs; any torch.distributed group).
+The allreduce sums fp32 partials: small ones (decode-sized M) through
+ftc_peer_ar (one-shot over NVLink peer memory, a few microseconds) when the
+block is given a :class:`~xwfes_b200.ftc.PeerAllreduce`, the rest through
+torch.distributed (NCCL on GPUs, any group on the CPU).
 
 The compute is injected (``ops``): :class:`CudaOps` runs the library's
 kernels; tests run the same orchestration with the CPU oracle under gloo.
@@ -150,14 +153,17 @@ class TPBlock:
     ops: object
     shards: dict
     group: object = None
+    peer: object = None  # optional PeerAllreduce for partials that fit its buffer
 
     @classmethod
-    def build(cls, dims, G, rank, ops, host_shards, group=None):
+    def build(cls, dims, G, rank, ops, host_shards, group=None, peer=None):
         dev = {nm: (ops.upload(a), n, k) for nm, (a, n, k) in host_shards.items()}
-        return cls(dims, G, rank, ops, dev, group)
+        return cls(dims, G, rank, ops, dev, group, peer)
 
     def _allreduce(self, t):
         if self.G > 1:
+            if self.peer is not None and self.peer.fits(t):
+                return self.peer.sum_(t)
             import torch.distributed as dist
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
