@@ -203,6 +203,15 @@ int ftc_rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t
  * activation (ft/src/cpu_backend.cpp:127). */
 int ftc_silu_mul(const float* g, const float* u, int64_t n, float* h, void* stream);
 
+/* The same on rows that hold [gate (n values) | up (n values)] side by side
+ * (pitch ld >= 2n: the output of one matmul over stacked gate and up
+ * weights): row m of the result is silu(gate) * up, written either to h
+ * (fp32 rows, pitch n) or, when h is NULL, to out16 as fp16 rows with
+ * power-of-two scales exactly as ftc_rows_to_f16 would give for that fp32
+ * row (out16 pitch n, n even, row_exp[rows]). */
+int ftc_silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h, void* out16,
+                      int32_t* row_exp, void* stream);
+
 /* Routed-expert MoE FFN layer on the device: the reference's
  * Engine::Impl::moe_ffn (ft/src/engine.cpp:179-241) after the router matmul,
  * with each expert's FFN (ft/src/cpu_backend.cpp:106-149) in the standard

@@ -64,14 +64,14 @@ class OracleOps:
         return arr
 
     def matmuls(self, x, ws):
-        xn = x.numpy()
+        xn = np.ascontiguousarray(x.numpy())
         return [torch.from_numpy(self.O.matmul(xn, w, F.Q4_K, k, threads=2)) for w, n, k in ws]
 
-    def silu_mul(self, g, u):
-        gn = g.numpy()
+    def silu_matmul(self, gu, n, w):
+        gn, un = gu.numpy()[:, :n], gu.numpy()[:, n:2 * n]
         with np.errstate(over="ignore"):  # exp(-g) = inf gives silu = -0, as in C
-            h = gn / (np.float32(1) + np.exp(-gn)) * u.numpy()
-        return torch.from_numpy(h.astype(np.float32))
+            h = (gn / (np.float32(1) + np.exp(-gn)) * un).astype(np.float32)
+        return self.matmuls(torch.from_numpy(np.ascontiguousarray(h)), [w])[0]
 
 
 def _rank_main(rank, world, port, out_dir):

@@ -66,16 +66,18 @@ def test_block_single_gpu_vs_oracle(oracle, weights, M):
 @pytest.mark.parametrize("M", [1, 16])
 def test_sharded_ranks_on_one_gpu(oracle, weights, G, M):
     """Every rank's shards through the kernels (K slices of whole
-    super-blocks for o and down), partials summed by hand."""
+    super-blocks for o and down; stacked q/k/v and gate/up rows), partials
+    summed by hand."""
     ops = tp.CudaOps(torch.device("cuda", 0))
     ranks = [tp.TPBlock.build(MID, G, r, ops, tp.shard(weights, MID, G, r)) for r in range(G)]
     x = torch.from_numpy(x_rows(M, MID, seed=7)).cuda()
-    qs = [ops.matmuls(x, [b.shards["q"]])[0] for b in ranks]
+    nq, nf = MID["n_q"] // G, MID["n_ff"] // G
+    qs = [ops.matmuls(x, [b.shards["qkv"]])[0][:, :nq] for b in ranks]
     h = sum(ops.matmuls(q, [b.shards["o"]])[0] for q, b in zip(qs, ranks))
     out = 0
     for b in ranks:
-        g, u = ops.matmuls(h, [b.shards["gate"], b.shards["up"]])
-        out = out + ops.matmuls(ops.silu_mul(g, u), [b.shards["down"]])[0]
+        gu = ops.matmuls(h, [b.shards["gate_up"]])[0]
+        out = out + ops.silu_matmul(gu, nf, b.shards["down"])
     torch.cuda.synchronize()
     ref = oracle_block(oracle, weights, MID, x.cpu().numpy())
     assert norm_err(out.cpu().numpy(), ref) <= (1e-5 if M <= 8 else TOL)
@@ -137,3 +139,18 @@ def test_two_gpus(oracle, weights, tmp_path, peer):
         ref = oracle_block(oracle, weights, MID, np.random.default_rng(M).standard_normal(
             (M, MID["n_embd"])).astype(np.float32))
         assert norm_err(o0, ref) <= (1e-5 if M <= 8 else TOL)
+
+
+@pytest.mark.parametrize("M", [1, 5, 33])
+def test_silu_mul_rows(M):
+    """ftc_silu_mul_rows equals ftc_silu_mul on the split halves (fp32 rows)
+    and ftc_rows_to_f16 of that result (fp16 rows), bit for bit."""
+    from xwfes_b200 import ftc
+    n = 3584
+    gu = torch.randn(M, 2 * n + 8, device="cuda") * 3
+    g, u = gu[:, :n].contiguous(), gu[:, n:2 * n].contiguous()
+    ref = ftc.silu_mul(g, u)
+    assert torch.equal(ftc.silu_mul_rows(gu, n), ref)
+    h16, e = ftc.silu_mul_rows(gu, n, to_f16=True)
+    r16, re = ftc.rows_to_f16(ref)
+    assert torch.equal(h16, r16) and torch.equal(e, re)

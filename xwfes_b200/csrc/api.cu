@@ -66,6 +66,8 @@ int gemm_q4k_rowscaled(const void* w, int64_t N, int64_t K, int64_t row_stride, 
                        int64_t M, void* y, int y_dtype, const int32_t* row_exp, cudaStream_t st);
 int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
                 int32_t* row_exp, cudaStream_t st);
+int silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h, void* out16,
+                  int32_t* row_exp, cudaStream_t st);
 int silu_mul(const float* g, const float* u, int64_t n, float* h, cudaStream_t st);
 size_t moe_workspace_bytes(const ftc_moe_desc* d, int64_t T);
 size_t moe_experts_workspace_bytes(const ftc_moe_desc* d, int64_t rows);
@@ -462,6 +464,12 @@ int ftc_rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t
 
 int ftc_silu_mul(const float* g, const float* u, int64_t n, float* h, void* stream) {
     int rc = silu_mul(g, u, n, h, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h, void* out16,
+                      int32_t* row_exp, void* stream) {
+    int rc = silu_mul_rows(gu, rows, n, ld, h, out16, row_exp, (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

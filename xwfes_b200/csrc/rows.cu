@@ -7,6 +7,11 @@
 //                 epilogue multiplies its output rows by 2^e[m] (exact).
 //   silu_mul      h = silu(g) * u in fp32, g / (1 + exp(-g)) as the
 //                 reference's expert FFN (ft/src/cpu_backend.cpp:127).
+//   silu_mul_rows the same on rows holding [gate | up] side by side (the
+//                 output of one matmul over stacked gate and up weights),
+//                 into fp32 rows, or straight into fp16 rows with their
+//                 power-of-two scales (bit for bit rows_to_f16 of the fp32
+//                 result).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -52,7 +57,91 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
     }
 }
 
+__device__ __forceinline__ float silu_gate(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+// fp32 rows: h[m][k] = silu(gu[m][k]) * gu[m][n + k], grid-stride over all
+// elements (decode-sized M has too few rows for one CTA per row).
+__global__ void silu_mul_rows_f32(const float* __restrict__ gu, int64_t ld, int64_t rows, int n,
+                                  float* __restrict__ h) {
+    const int64_t total = rows * n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / n, k = i - m * n;
+        const float* g = gu + m * ld;
+        h[i] = silu_gate(g[k], g[n + k]);
+    }
+}
+
+// fp16 rows scaled as rows_to_f16: one CTA per row; the row's silu values
+// are kept in shared memory between the max and the scaling pass when they
+// fit (cache = true), else recomputed (same arithmetic, same bits).
+template <bool kCache>
+__global__ void __launch_bounds__(1024)
+silu_mul_rows_f16(const float* __restrict__ gu, int64_t ld, int n, __half* __restrict__ out16,
+                  int32_t* __restrict__ row_exp) {
+    extern __shared__ float hs[];
+    __shared__ float red[32];
+    const float* g = gu + (int64_t)blockIdx.x * ld;
+    const float* u = g + n;
+    float amax = 0.f;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        const float v = silu_gate(g[k], u[k]);
+        if (kCache) hs[k] = v;
+        amax = fmaxf(amax, fabsf(v));
+    }
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    float m = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+    int e = 0;
+    if (m > 0.f && isfinite(m))
+        e = max(-126, min(126, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14));
+    const float sc = __uint_as_float((uint32_t)(127 - e) << 23);
+    __half2* dst = reinterpret_cast<__half2*>(out16 + (int64_t)blockIdx.x * n);
+    for (int k = 2 * threadIdx.x; k < n; k += 2 * blockDim.x) {
+        const float a = kCache ? hs[k] : silu_gate(g[k], u[k]);
+        const float b = kCache ? hs[k + 1] : silu_gate(g[k + 1], u[k + 1]);
+        dst[k >> 1] = __floats2half2_rn(a * sc, b * sc);
+    }
+    if (threadIdx.x == 0) row_exp[blockIdx.x] = e;
+}
+
+constexpr int kSiluCacheMax = 48 * 1024;  // row values kept in shared memory (192 KB)
+
 }  // namespace
+
+int silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h, void* out16,
+                  int32_t* row_exp, cudaStream_t st) {
+    FTC_REQUIRE(gu && (h || (out16 && row_exp)), FTC_E_INVALID, "ftc_silu_mul_rows: null pointer");
+    FTC_REQUIRE(rows >= 0 && rows <= INT32_MAX && n > 0 && n <= INT32_MAX && ld >= 2 * n,
+                FTC_E_INVALID, "ftc_silu_mul_rows: bad shape (ld >= 2n)");
+    FTC_REQUIRE(h || (n % 2 == 0 && (uintptr_t)out16 % 4 == 0), FTC_E_INVALID,
+                "ftc_silu_mul_rows: fp16 rows need an even n and 4-byte alignment");
+    if (rows == 0) return FTC_OK;
+    if (h) {
+        static int sms = 0;
+        if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+        const int64_t total = rows * n;
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8));
+        silu_mul_rows_f32<<<grid, 256, 0, st>>>(gu, ld, rows, (int)n, h);
+    } else if (n <= kSiluCacheMax) {
+        static bool configured = false;
+        if (!configured) {
+            FTC_CUDA(cudaFuncSetAttribute(silu_mul_rows_f16<true>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kSiluCacheMax * (int)sizeof(float)));
+            configured = true;
+        }
+        silu_mul_rows_f16<true><<<(int)rows, 1024, (size_t)n * sizeof(float), st>>>(
+            gu, ld, (int)n, static_cast<__half*>(out16), row_exp);
+    } else {
+        silu_mul_rows_f16<false><<<(int)rows, 1024, 0, st>>>(gu, ld, (int)n,
+                                                             static_cast<__half*>(out16), row_exp);
+    }
+    FTC_CUDA(cudaGetLastError());
+    return FTC_OK;
+}
 
 int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
                 int32_t* row_exp, cudaStream_t st) {

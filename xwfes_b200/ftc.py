@@ -54,6 +54,7 @@ SIGNATURES = {
     "ftc_moe_experts": (C.c_int, [_p, _p, C.c_int, _i64, _p, _p, _i64, _p, _p, C.c_size_t, _p]),
     "ftc_moe_workspace_bytes": (C.c_size_t, [_p, _i64]),
     "ftc_moe_ffn": (C.c_int, [_p, _p, _p, C.c_int, _i64, _p, _p, C.c_size_t, _p]),
+    "ftc_silu_mul_rows": (C.c_int, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
     "ftc_peer_ar_create": (C.c_int, [C.c_int, C.c_int, _i64, C.POINTER(_p), _p]),
     "ftc_peer_ar_open": (C.c_int, [_p, _p]),
     "ftc_peer_ar_max_elems": (_i64, [_p]),
@@ -228,6 +229,26 @@ def silu_mul(g, u, out=None, stream=None):
     check(lib().ftc_silu_mul(g.data_ptr(), u.data_ptr(), g.numel(), out.data_ptr(),
                              _stream(stream)), "ftc_silu_mul")
     return out
+
+
+def silu_mul_rows(gu, n, to_f16=False, stream=None):
+    """Rows of ``gu`` (fp32 CUDA [M, >= 2n], row pitch gu.stride(0)) hold
+    [gate | up]; returns silu(gate) * up as fp32 [M, n], or with ``to_f16``
+    the fp16 rows and row exponents of :func:`rows_to_f16` of that result."""
+    import torch
+    m = gu.shape[0]
+    if gu.dtype != torch.float32 or gu.stride(1) != 1:
+        raise ValueError("silu_mul_rows: fp32 rows with unit column stride")
+    if to_f16:
+        out = torch.empty((m, n), dtype=torch.float16, device=gu.device)
+        e = torch.empty((m,), dtype=torch.int32, device=gu.device)
+        check(lib().ftc_silu_mul_rows(gu.data_ptr(), m, n, gu.stride(0), None, out.data_ptr(),
+                                      e.data_ptr(), _stream(stream)), "ftc_silu_mul_rows")
+        return out, e
+    h = torch.empty((m, n), dtype=torch.float32, device=gu.device)
+    check(lib().ftc_silu_mul_rows(gu.data_ptr(), m, n, gu.stride(0), h.data_ptr(), None, None,
+                                  _stream(stream)), "ftc_silu_mul_rows")
+    return h
 
 
 def _align(n, a=256):

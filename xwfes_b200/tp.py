@@ -20,7 +20,12 @@ the same chain of Q4_K matmuls split across G GPUs:
   out = allreduce_r( a_r . down_r )
 
 Every rank uploads only its own shard (contiguous GGUF blocks; a K slice of a
-row is a run of whole super-blocks).  Matmuls: M <= 8 tokens use the decode
+row is a run of whole super-blocks).  A rank's q, k and v rows are stacked
+into one weight, and so are its gate and up rows, so each group is one
+matmul launch (rows are independent: the stacked product is the row-wise
+concatenation of the separate ones, bit for bit); silu(gate) * up is taken
+on the [gate | up] output rows by one kernel that also produces the fp16
+operand of the down GEMM.  Matmuls: M <= 8 tokens use the decode
 GEMV (fp32 activations), larger M the tcgen05 GEMM on fp16 rows with
 power-of-two row scales (ftc_rows_to_f16 / ftc_gemm_rowscaled), fp32 outputs.
 The allreduce sums fp32 partials: small ones (decode-sized M) through
@@ -128,11 +133,21 @@ class CudaOps:
     def upload(self, arr):
         return self.torch.from_numpy(arr).to(self.device)
 
+    def silu_matmul(self, gu, n, w):
+        """(silu(gate) * up) . W^T for rows gu = [gate (n) | up (n)]."""
+        ftc, M = self.ftc, gu.shape[0]
+        wt, wn, wk = w
+        if M <= 8:
+            return ftc.mul_mat_vec(wt, F.Q4_K, wn, wk, ftc.silu_mul_rows(gu, n))
+        x16, e = ftc.silu_mul_rows(gu, n, to_f16=True)
+        return ftc.gemm_rowscaled(wt, F.Q4_K, wn, wk, x16, e)
+
     def matmuls(self, x, ws):
         """[x . W^T for (W, n, k) in ws], x fp32 [M, k] shared by all."""
         ftc, M = self.ftc, x.shape[0]
         k = ws[0][2]
         if M <= 8:
+            x = x.contiguous()
             if len(ws) == 1:
                 w, n, _ = ws[0]
                 return [ftc.mul_mat_vec(w, F.Q4_K, n, k, x)]
@@ -157,7 +172,12 @@ class TPBlock:
 
     @classmethod
     def build(cls, dims, G, rank, ops, host_shards, group=None, peer=None):
-        dev = {nm: (ops.upload(a), n, k) for nm, (a, n, k) in host_shards.items()}
+        h = dict(host_shards)
+        for grp, names in (("qkv", ("q", "k", "v")), ("gate_up", ("gate", "up"))):
+            parts = [h.pop(nm) for nm in names]
+            h[grp] = (np.concatenate([a for a, _, _ in parts], axis=0),
+                      sum(n for _, n, _ in parts), parts[0][2])
+        dev = {nm: (ops.upload(a), n, k) for nm, (a, n, k) in h.items()}
         return cls(dims, G, rank, ops, dev, group, peer)
 
     def _allreduce(self, t):
@@ -172,10 +192,11 @@ class TPBlock:
         """x: fp32 [M, n_embd] on this rank's device (replicated); returns the
         block output (fp32 [M, n_embd], identical on every rank) and this
         rank's q/k/v slices."""
-        W = self.shards
-        q, k, v = self.ops.matmuls(x, [W["q"], W["k"], W["v"]])
+        W, d, G = self.shards, self.dims, self.G
+        nq, nkv, nf = d["n_q"] // G, d["n_kv"] // G, d["n_ff"] // G
+        qkv = self.ops.matmuls(x, [W["qkv"]])[0]
+        q, k, v = qkv[:, :nq], qkv[:, nq:nq + nkv], qkv[:, nq + nkv:]
         h = self._allreduce(self.ops.matmuls(q, [W["o"]])[0])
-        g, u = self.ops.matmuls(h, [W["gate"], W["up"]])
-        a = self.ops.silu_mul(g, u)
-        out = self._allreduce(self.ops.matmuls(a, [W["down"]])[0])
+        gu = self.ops.matmuls(h, [W["gate_up"]])[0]
+        out = self._allreduce(self.ops.silu_matmul(gu, nf, W["down"]))
         return out, (q, k, v)
