@@ -278,7 +278,8 @@ int ftc_moe_combine(const float* y, const int32_t* pos, const int32_t* idx, cons
  * down; same operand rules as ftc_moe_ffn) into y (device fp32
  * [rows][n_embd]).  counts / offsets: device int32 [n_experts]; max_rows:
  * an upper bound on every count.  workspace: 256-byte aligned device memory
- * of at least ftc_moe_experts_workspace_bytes(desc, rows). */
+ * of at least ftc_moe_experts_workspace_bytes(desc, rows).  desc->top_k is
+ * not used here (a rank may hold fewer experts than the layer's top_k). */
 size_t ftc_moe_experts_workspace_bytes(const ftc_moe_desc* desc, int64_t rows);
 int ftc_moe_experts(const ftc_moe_desc* desc, const void* x, int x_dtype, int64_t rows,
                     const int32_t* counts, const int32_t* offsets, int64_t max_rows, float* y,

@@ -90,6 +90,11 @@ def test_moe_entry_validates_before_launch(lib):
     assert rc == -1 and "alignment" in ftc.last_error()
     rc = lib.ftc_moe_ffn(C.byref(d), 256, 256, F.Q8_0, 64, 256, 256, need, None)
     assert rc == -2
+    # the expert FFN entry on pre-grouped rows ignores top_k: an
+    # expert-parallel rank may hold one expert of a top-2 layer
+    one = _moe_desc(n_experts=1, top_k=2)
+    assert lib.ftc_moe_experts_workspace_bytes(C.byref(one), 64) > 0
+    assert lib.ftc_moe_workspace_bytes(C.byref(one), 64) == 0
 
 
 def _run_child(code, env_extra):

@@ -325,12 +325,16 @@ MoeLayout moe_layout(const ftc_moe_desc& d, int64_t T) {
     return L;
 }
 
-int check_desc(const ftc_moe_desc* d, const char* who) {
+// routing: the entry routes tokens (top_k must fit n_experts); the expert
+// FFN entries on pre-grouped rows ignore top_k (an expert-parallel rank may
+// hold fewer experts than the layer's top_k)
+int check_desc(const ftc_moe_desc* d, const char* who, bool routing = true) {
     FTC_REQUIRE(d, FTC_E_INVALID, std::string(who) + ": null descriptor");
     FTC_REQUIRE(d->dtype == FTC_Q4_K, FTC_E_UNSUPPORTED,
                 std::string(who) + ": expert weights must be Q4_K");
-    FTC_REQUIRE(d->n_experts >= 1 && d->n_experts <= kMaxExperts && d->top_k >= 1 &&
-                    d->top_k <= kMaxTopK && d->top_k <= d->n_experts,
+    FTC_REQUIRE(d->n_experts >= 1 && d->n_experts <= kMaxExperts, FTC_E_INVALID,
+                std::string(who) + ": need 1 <= n_experts <= 256");
+    FTC_REQUIRE(!routing || (d->top_k >= 1 && d->top_k <= kMaxTopK && d->top_k <= d->n_experts),
                 FTC_E_INVALID, std::string(who) + ": need 1 <= top_k <= min(8, n_experts) <= 256");
     FTC_REQUIRE(d->n_embd > 0 && d->n_ff > 0 && d->n_embd % 256 == 0 && d->n_ff % 256 == 0 &&
                     d->n_embd <= INT32_MAX && d->n_ff <= kMaxFf,
@@ -504,7 +508,7 @@ int moe_combine_only(const float* y, const int32_t* pos, const int32_t* idx, con
 // counts / offsets: device int32 [E]; rows: total rows; max_rows: bound on
 // any count.  Workspace: moe_experts_workspace_bytes.
 size_t moe_experts_workspace_bytes(const ftc_moe_desc* d, int64_t rows) {
-    if (check_desc(d, "ftc_moe_experts_workspace_bytes") != FTC_OK || rows < 0) return 0;
+    if (check_desc(d, "ftc_moe_experts_workspace_bytes", false) != FTC_OK || rows < 0) return 0;
     size_t o = 0;
     o += align256((size_t)rows * 4);                    // xs
     o += align256((size_t)rows * 4);                    // hs
@@ -517,7 +521,7 @@ size_t moe_experts_workspace_bytes(const ftc_moe_desc* d, int64_t rows) {
 int moe_experts(const ftc_moe_desc* d, const void* x, int x_dtype, int64_t rows,
                 const int32_t* counts, const int32_t* offsets, int64_t max_rows, float* y,
                 void* ws, size_t ws_bytes, cudaStream_t st) {
-    int rc = check_desc(d, "ftc_moe_experts");
+    int rc = check_desc(d, "ftc_moe_experts", false);
     if (rc) return rc;
     FTC_REQUIRE(rows >= 0 && rows <= INT32_MAX / 2 && max_rows >= 0, FTC_E_INVALID,
                 "ftc_moe_experts: bad row count");
