@@ -519,9 +519,11 @@ EP_T = [64, 1024]
 def time_ep(dev, world, rank):
     """Config 5 expert-parallel: each rank holds 8/world experts (full
     Mixtral-8x7B expert shapes) and T/world of the tokens; one forward =
-    routing, count and row all-to-alls, local grouped expert GEMMs, reverse
-    all-to-all, combine (NCCL).  Eager (the split sizes go to the host once
-    per forward); time = max over ranks, CUDA events, barrier before."""
+    routing, packing into fixed-capacity send buffers, count and row
+    all-to-alls with equal splits, device regrouping, local grouped expert
+    GEMMs, reverse all-to-all, combine.  No host synchronisation inside a
+    forward, so it is captured and replayed as a CUDA graph (NCCL included);
+    time = max over ranks, CUDA events, barrier before."""
     import torch
     import torch.distributed as dist
     from xwfes_b200 import ep
@@ -532,26 +534,37 @@ def time_ep(dev, world, rank):
         [S.weight(F.Q4_K, n, k, seed=0, name=f"moe.{nm}.{e}") for e in range(e0, e1)])).to(dev)
     ops = ep.CudaEPOps(dev, mk("gate", FF, K), mk("up", FF, K), mk("down", K, FF), e1 - e0, U, K,
                        FF)
-    layer = ep.EPMoE(E, U, K, world, rank, ops)
     per_expert = 3 * FF * F.row_bytes(F.Q4_K, K)
     out = {}
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cs = torch.cuda.Stream(device=dev)
     for T in EP_T:
         t0, t1 = ep.token_range(T, world, rank)
+        layer = ep.EPMoE(E, U, K, world, rank, ops, max_tokens=-(-T // world))
         logits = torch.from_numpy(S.router_logits(T, E, seed=0)[t0:t1]).to(dev)
         x = torch.from_numpy(S.activations_bf16(T, K, seed=0, name="moe.x")[t0:t1].view(
             np.int16)).to(dev).view(torch.bfloat16)
-        for _ in range(3):
+        with torch.cuda.stream(cs):
+            for _ in range(3):  # eager warm-up (NCCL, workspaces, split-K scratch)
+                layer.forward(logits, x)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cs):
             layer.forward(logits, x)
+        with torch.cuda.stream(cs):
+            for _ in range(3):
+                g.replay()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier(device_ids=[dev.index])
         reps = 10
-        ev0.record()
-        for _ in range(reps):
-            layer.forward(logits, x)
-        ev1.record()
+        ev0.record(cs)
+        with torch.cuda.stream(cs):
+            for _ in range(reps):
+                g.replay()
+        ev1.record(cs)
         torch.cuda.synchronize()
+        del g
         t = torch.tensor([ev0.elapsed_time(ev1) / reps], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -561,8 +574,9 @@ def time_ep(dev, world, rank):
                        "tflops": round(2.0 * T * U * 3 * FF * K / (us * 1e-6) / 1e12, 2)}
     return {"workload": "config 5: Mixtral-8x7B-shaped MoE layer, expert-parallel, T tokens "
                         "split over the ranks",
-            "parallelism": f"ep{world} ({E // world} experts per GPU; NCCL all-to-all of counts, "
-                           "token rows (bf16) and expert outputs (fp32))",
+            "parallelism": f"ep{world} ({E // world} experts per GPU; equal-split NCCL "
+                           "all-to-alls of counts, token rows (bf16) and expert outputs (fp32) "
+                           "with a fixed capacity per rank; CUDA graph per forward)",
             "scaling": "strong (T and the 8 experts are split over the GPUs)",
             "per_T": out}
 

@@ -303,6 +303,34 @@ int ftc_expert_chunk_static(int dtype, const float* x, float* out, const void* g
                             const void* up, const void* down, int64_t M, int64_t K, int64_t IC,
                             int64_t gate_up_row_stride, int64_t down_row_stride, void* stream);
 
+/* ---- expert-parallel exchange with fixed capacity ----
+ *
+ * The expert-parallel MoE layer (experts split evenly over `world` GPUs,
+ * rank d holding experts [d*E/world, (d+1)*E/world)) exchanges rows with
+ * all-to-alls of equal splits: every rank sends every rank `cap` rows
+ * (cap >= this rank's T * top_k, the same on all ranks), so no split size
+ * goes to the host and the layer can be captured in a CUDA graph.
+ *
+ * ftc_ep_pack, after ftc_moe_route on this rank's T tokens: send[d][i] (rows
+ * of n_embd x_dtype values) = x[row_token[off_d + i]] for the cnt_d rows
+ * routed to rank d (off_d, cnt_d: prefix sums of counts over rank d's
+ * experts; slots past cnt_d are left as they are); pos_padded[t][u] =
+ * d * cap + i, the slot of token t's u-th row, i.e. where its expert output
+ * comes back in the reverse exchange (pass it to ftc_moe_combine as pos).
+ * The per-expert counts themselves are the [world][E/world] counts to send.
+ *
+ * ftc_ep_regroup, on the receiving rank with recv_counts[src][e] (rows of
+ * local expert e from rank src): counts[e] / offsets[e] of the local
+ * experts and a permutation of the world * cap received slots: perm[j] is
+ * the slot that goes to position j (valid rows in expert-major,
+ * source-major order first, then the padding), inv its inverse. */
+int ftc_ep_pack(const void* x, int x_dtype, int64_t T, int64_t n_embd, const int32_t* idx,
+                const int32_t* counts, const int32_t* pos, const int32_t* row_token,
+                int64_t n_experts, int64_t top_k, int64_t world, int64_t cap, void* send,
+                int32_t* pos_padded, void* stream);
+int ftc_ep_regroup(const int32_t* recv_counts, int64_t world, int64_t n_local, int64_t cap,
+                   int32_t* perm, int32_t* inv, int32_t* counts, int32_t* offsets, void* stream);
+
 /* ---- tensor-parallel exchange: allreduce over NVLink peer memory ----
  *
  * One-shot allreduce (sum) of fp32 vectors between the ranks of a

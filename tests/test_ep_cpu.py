@@ -27,13 +27,28 @@ def test_ranges():
 
 
 def test_regroup_orders_rows_by_expert():
-    rc = np.array([[2, 0, 1], [1, 3, 0]])  # [source][local expert]
-    perm, counts, offsets = ep.regroup(rc)
-    # received rows: s0: e0 e0 e2, s1: e0 e1 e1 e1 -> indices 0..6
-    assert perm.tolist() == [0, 1, 3, 4, 5, 6, 2]
+    rc = np.array([[2, 0, 1], [1, 3, 0]])  # [source][local expert], cap 4
+    perm, inv, counts, offsets = ep.regroup(rc, 4)
+    # slots: s0 -> 0 1 (e0) 2 (e2) 3 (pad); s1 -> 4 (e0) 5 6 7 (e1)
+    assert perm.tolist() == [0, 1, 4, 5, 6, 7, 2, 3]
+    assert (perm[inv] == np.arange(8)).all() and (inv[perm] == np.arange(8)).all()
     assert counts.tolist() == [3, 3, 1] and offsets.tolist() == [0, 3, 6]
-    perm, counts, _ = ep.regroup(np.zeros((2, 2), np.int64))
-    assert perm.size == 0 and counts.tolist() == [0, 0]
+    perm, _, counts, _ = ep.regroup(np.zeros((2, 2), np.int64), 3)
+    assert perm.tolist() == list(range(6)) and counts.tolist() == [0, 0]
+
+
+def test_pack_slots():
+    # 4 experts on 2 ranks; 3 tokens, top-2
+    idx = np.array([[0, 3], [2, 0], [1, 2]])
+    counts = np.bincount(idx.ravel(), minlength=4)          # [2, 1, 2, 1]
+    order = sorted(range(6), key=lambda r: (idx.ravel()[r], r))
+    row_token = np.array([r // 2 for r in order])
+    pos = np.empty(6, np.int64)
+    pos[order] = np.arange(6)
+    src, pp = ep.pack_slots(counts, row_token, idx, pos.reshape(3, 2), 2, 6)
+    assert src[0].tolist() == [0, 1, 2, -1, -1, -1]          # experts 0, 1
+    assert src[1].tolist() == [1, 2, 0, -1, -1, -1]          # experts 2, 3
+    assert pp.tolist() == [[0, 8], [6, 1], [2, 7]]
 
 
 def np_route(oracle, logits, u):
@@ -69,10 +84,19 @@ class OracleEPOps:
     def route(self, logits, u):
         return np_route(self.O, logits.numpy(), u)
 
-    def gather(self, x, route, rows):
-        return x[torch.from_numpy(route["row_token"][:rows].astype(np.int64))]
+    def pack(self, x, route, world, cap):
+        src, pp = ep.pack_slots(route["counts"].numpy(), route["row_token"], route["idx"],
+                                route["pos"], world, cap)
+        send = torch.zeros((world, cap, x.shape[1]), dtype=x.dtype)
+        valid = torch.from_numpy(src >= 0)
+        send[valid] = x[torch.from_numpy(src[src >= 0])]
+        return send, pp
 
-    def experts(self, x, counts, offsets):
+    def regroup(self, recv_counts, world, n_local, cap):
+        perm, inv, counts, offsets = ep.regroup(recv_counts.numpy().reshape(world, n_local), cap)
+        return torch.from_numpy(perm), torch.from_numpy(inv), counts, offsets
+
+    def experts(self, x, counts, offsets, max_rows):
         xn = x.numpy().astype(np.float32)
         y = np.zeros_like(xn)
         for e, (c, o) in enumerate(zip(counts, offsets)):
@@ -83,20 +107,14 @@ class OracleEPOps:
                 y[o:o + c] = out
         return torch.from_numpy(y)
 
-    def combine(self, y, route):
-        yn = y.numpy()
-        idx, w, pos, rank = route["idx"], route["w"], route["pos"], route["rank"]
+    def combine(self, y, route, pos):
+        yn = y.numpy().reshape(-1, K)
+        idx, w, rank = route["idx"], route["w"], route["rank"]
         out = np.zeros((idx.shape[0], K), np.float32)
         for t in range(idx.shape[0]):
             for s in sorted(range(idx.shape[1]), key=lambda s: rank[idx[t, s]]):
                 out[t] = out[t] + np.float32(w[t, s]) * yn[pos[t, s]]
         return torch.from_numpy(out)
-
-    def to_host(self, *ts):
-        return [t.numpy() for t in ts]
-
-    def index(self, n):
-        return torch.from_numpy(n)
 
 
 def _weights():
@@ -119,7 +137,8 @@ def _rank_main(rank, world, port, out_dir):
     try:
         g, u, d = _weights()
         e0, e1 = ep.expert_range(E, world, rank)
-        layer = ep.EPMoE(E, U, K, world, rank, OracleEPOps(O, g[e0:e1], u[e0:e1], d[e0:e1]))
+        layer = ep.EPMoE(E, U, K, world, rank, OracleEPOps(O, g[e0:e1], u[e0:e1], d[e0:e1]),
+                         max_tokens=-(-T // world))
         logits, x = _inputs()
         t0, t1 = ep.token_range(T, world, rank)
         out = layer.forward(torch.from_numpy(logits[t0:t1]), torch.from_numpy(x[t0:t1]))

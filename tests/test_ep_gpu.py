@@ -60,7 +60,7 @@ def single_gpu(T):
 def test_one_rank_equals_moe_layer(T):
     g, u, d = (torch.from_numpy(a).cuda() for a in weights())
     ops = ep.CudaEPOps(torch.device("cuda", 0), g, u, d, E, U, K, FF)
-    layer = ep.EPMoE(E, U, K, 1, 0, ops)
+    layer = ep.EPMoE(E, U, K, 1, 0, ops, max_tokens=T)
     lg, x = to_dev(*inputs(T))
     out = layer.forward(lg, x)
     torch.cuda.synchronize()
@@ -82,7 +82,7 @@ e0, e1 = ep.expert_range(T.E, world, rank)
 dev = torch.device("cuda", rank)
 ops = ep.CudaEPOps(dev, *(torch.from_numpy(a[e0:e1]).to(dev) for a in (g, u, d)),
                    e1 - e0, T.U, T.K, T.FF)
-layer = ep.EPMoE(T.E, T.U, T.K, world, rank, ops)
+layer = ep.EPMoE(T.E, T.U, T.K, world, rank, ops, max_tokens=150)
 for n in (64, 300):
     logits, x = T.inputs(n)
     t0, t1 = ep.token_range(n, world, rank)
@@ -119,3 +119,31 @@ def test_two_gpus_nccl(tmp_path):
     for n in (64, 300):
         got = np.concatenate([np.load(tmp_path / f"out{n}_{r}.npy") for r in range(2)])
         assert close(got, single_gpu(n))
+
+
+@pytest.mark.parametrize("T,world", [(1, 1), (37, 2), (64, 4), (300, 8)])
+def test_pack_and_regroup_match_host_reference(T, world):
+    """ftc_ep_pack / ftc_ep_regroup against the host restatement in ep.py,
+    element for element, on the device routing of random logits."""
+    from xwfes_b200 import ftc
+    cap = T * U + 3
+    lg, xb = to_dev(*inputs(T))
+    route = ftc.moe_route(lg, U)
+    send, pp = ftc.ep_pack(xb, route, world, cap)
+    torch.cuda.synchronize()
+    h = {k: v.cpu().numpy() for k, v in route.items()}
+    src, pp_ref = ep.pack_slots(h["counts"], h["row_token"], h["idx"], h["pos"], world, cap)
+    assert np.array_equal(pp.cpu().numpy(), pp_ref)
+    sv, xv = send.cpu().view(torch.int16).numpy(), xb.cpu().view(torch.int16).numpy()
+    for d in range(world):
+        valid = src[d] >= 0
+        assert np.array_equal(sv[d][valid], xv[src[d][valid]])
+    # receive side: counts of `world` sources for the n_local experts of one rank
+    El = E // world
+    rng = np.random.default_rng(T)
+    rc = rng.integers(0, 4, size=(world, El)).astype(np.int32)
+    rc = np.minimum(rc, cap // max(1, El))
+    got = ftc.ep_regroup(torch.from_numpy(rc.ravel()).cuda(), world, El, cap)
+    ref = ep.regroup(rc, cap)
+    for g, r in zip(got, ref):
+        assert np.array_equal(g.cpu().numpy(), r)

@@ -68,6 +68,12 @@ int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld,
                 int32_t* row_exp, cudaStream_t st);
 int silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h, void* out16,
                   int32_t* row_exp, cudaStream_t st);
+int ep_pack(const void* x, int x_dtype, int64_t T, int64_t n_embd, const int32_t* idx,
+            const int32_t* counts, const int32_t* pos, const int32_t* row_token, int64_t n_experts,
+            int64_t top_k, int64_t world, int64_t cap, void* send, int32_t* pos_padded,
+            cudaStream_t st);
+int ep_regroup(const int32_t* recv_counts, int64_t world, int64_t n_local, int64_t cap,
+               int32_t* perm, int32_t* inv, int32_t* counts, int32_t* offsets, cudaStream_t st);
 int silu_mul(const float* g, const float* u, int64_t n, float* h, cudaStream_t st);
 size_t moe_workspace_bytes(const ftc_moe_desc* d, int64_t T);
 size_t moe_experts_workspace_bytes(const ftc_moe_desc* d, int64_t rows);
@@ -470,6 +476,22 @@ int ftc_silu_mul(const float* g, const float* u, int64_t n, float* h, void* stre
 int ftc_silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h, void* out16,
                       int32_t* row_exp, void* stream) {
     int rc = silu_mul_rows(gu, rows, n, ld, h, out16, row_exp, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_ep_pack(const void* x, int x_dtype, int64_t T, int64_t n_embd, const int32_t* idx,
+                const int32_t* counts, const int32_t* pos, const int32_t* row_token,
+                int64_t n_experts, int64_t top_k, int64_t world, int64_t cap, void* send,
+                int32_t* pos_padded, void* stream) {
+    int rc = ep_pack(x, x_dtype, T, n_embd, idx, counts, pos, row_token, n_experts, top_k, world,
+                     cap, send, pos_padded, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_ep_regroup(const int32_t* recv_counts, int64_t world, int64_t n_local, int64_t cap,
+                   int32_t* perm, int32_t* inv, int32_t* counts, int32_t* offsets, void* stream) {
+    int rc = ep_regroup(recv_counts, world, n_local, cap, perm, inv, counts, offsets,
+                        (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

@@ -9,17 +9,23 @@ expert planes, uploaded only there) and a shard of the tokens:
   1. route its tokens on the device (ftc_moe_route): top-k experts, weights,
      rows grouped by expert -- which is grouped by destination rank, since
      each rank's experts are contiguous;
-  2. all-to-all of the per-expert row counts (int32 [E]); the split sizes go
-     to the host once (NCCL's all-to-all takes them there);
-  3. all-to-all of the token rows (their own dtype, bf16 for config 5);
-  4. the received rows, regrouped by local expert, through the local expert
-     FFNs (ftc_moe_experts: grouped tcgen05 dequant-GEMMs);
-  5. the reverse all-to-all of the fp32 expert outputs;
+  2. pack the rows for each destination into a send buffer of fixed capacity
+     (ftc_ep_pack: cap rows per destination, cap = the layer's token
+     capacity per rank x top_k) and note where each row's output comes back;
+  3. all-to-all of the per-expert row counts and of the row buffers, both
+     with equal splits -- no split size goes to the host, so the whole
+     forward runs without a host synchronisation and can be captured in a
+     CUDA graph;
+  4. regroup the received rows by local expert (ftc_ep_regroup: a
+     permutation computed on the device) and run the local expert FFNs
+     (ftc_moe_experts: grouped tcgen05 dequant-GEMMs on device counts);
+  5. the reverse all-to-all of the fp32 expert outputs (equal splits);
   6. the weighted sum in expert first-use order (ftc_moe_combine).
 
-Every token's result is the same arithmetic as the single-GPU layer
-(ftc_moe_ffn's grouped path): each output row depends only on its own token
-and expert, not on which other rows share a tile or a GPU.
+Every token's result is the arithmetic of the single-GPU layer
+(ftc_moe_ffn's grouped path) on the same rows; only the GEMMs' split-K
+choice, which follows the launch's tile count, may order the fp32 partial
+sums differently.
 
 The compute is injected (``ops``): :class:`CudaEPOps` runs the library's
 kernels, the CPU tests run the same orchestration with the oracle under gloo.
@@ -44,19 +50,41 @@ def token_range(T, G, r):
     return t0, t0 + base + (1 if r < extra else 0)
 
 
-def regroup(recv_counts):
-    """recv_counts[s][e]: rows of local expert e received from rank s, stored
-    source-major ([s][e][rows]).  Returns (perm, counts, offsets): perm[i] is
-    the received row that goes to position i of the expert-major order."""
+def rank_spans(counts, G):
+    """(off_d, cnt_d) of every rank d: its experts' rows in the expert order."""
+    c = np.asarray(counts, dtype=np.int64).reshape(G, -1).sum(axis=1)
+    return np.concatenate([[0], np.cumsum(c)[:-1]]), c
+
+
+def pack_slots(counts, row_token, idx, pos, G, cap):
+    """What ftc_ep_pack computes, on the host: src[d][i] = the token whose
+    row goes to slot i of rank d (-1: padding) and pos_padded [T, U]."""
+    off, cnt = rank_spans(counts, G)
+    src = np.full((G, cap), -1, np.int64)
+    for d in range(G):
+        src[d, :cnt[d]] = row_token[off[d]:off[d] + cnt[d]]
+    El = len(counts) // G
+    d_of = np.asarray(idx) // El
+    return src, (d_of * cap + (np.asarray(pos) - off[d_of])).astype(np.int32)
+
+
+def regroup(recv_counts, cap):
+    """What ftc_ep_regroup computes, on the host.  recv_counts[s][e]: rows of
+    local expert e received from rank s, stored at slots s*cap + (rows of
+    s's earlier experts) + i.  Returns (perm, inv, counts, offsets): perm[j]
+    is the slot at position j of the expert-major order (valid rows first,
+    source-major within an expert, then the padding), inv its inverse."""
     rc = np.asarray(recv_counts, dtype=np.int64)
     G, El = rc.shape
-    start = np.zeros_like(rc)
-    start.reshape(-1)[1:] = np.cumsum(rc.reshape(-1))[:-1]
-    perm = np.concatenate([np.arange(start[s, e], start[s, e] + rc[s, e])
-                           for e in range(El) for s in range(G)] or [np.zeros(0, np.int64)])
     counts = rc.sum(axis=0)
     offsets = np.concatenate([[0], np.cumsum(counts)[:-1]])
-    return perm.astype(np.int64), counts.astype(np.int32), offsets.astype(np.int32)
+    base = np.concatenate([np.zeros((G, 1), np.int64), np.cumsum(rc, axis=1)[:, :-1]], axis=1)
+    order = [s * cap + base[s, e] + i for e in range(El) for s in range(G) for i in range(rc[s, e])]
+    order += [s * cap + i for s in range(G) for i in range(rc[s].sum(), cap)]
+    perm = np.asarray(order, dtype=np.int64)
+    inv = np.empty_like(perm)
+    inv[perm] = np.arange(perm.size)
+    return perm, inv, counts.astype(np.int32), offsets.astype(np.int32)
 
 
 class CudaEPOps:
@@ -73,81 +101,54 @@ class CudaEPOps:
     def route(self, logits, top_k):
         return self.ftc.moe_route(logits, top_k)
 
-    def gather(self, x, route, rows):
-        return x.index_select(0, route["row_token"][:rows].long())
+    def pack(self, x, route, world, cap):
+        return self.ftc.ep_pack(x, route, world, cap)
 
-    def experts(self, x, counts, offsets):
-        t = self.torch
-        if x.shape[0] == 0:
-            return t.empty((0, x.shape[1]), dtype=t.float32, device=x.device)
-        return self.layer.experts(x, self.index(counts), self.index(offsets), int(counts.max()))
+    def regroup(self, recv_counts, world, n_local, cap):
+        return self.ftc.ep_regroup(recv_counts, world, n_local, cap)
 
-    def combine(self, y, route):
-        return self.ftc.moe_combine(y, route)
+    def experts(self, x, counts, offsets, max_rows):
+        return self.layer.experts(x, counts, offsets, max_rows)
 
-    def to_host(self, *ts):
-        """One device-to-host read of several int32 vectors (one sync)."""
-        t = self.torch
-        flat = t.cat([v.reshape(-1) for v in ts]).cpu().numpy()
-        out, o = [], 0
-        for v in ts:
-            out.append(flat[o:o + v.numel()])
-            o += v.numel()
-        return out
-
-    def index(self, n):
-        """Host index array to the device through pinned memory, without
-        waiting for the GPU (stream-ordered)."""
-        t = self.torch
-        h = t.from_numpy(np.ascontiguousarray(n)).pin_memory()
-        return h.to(self.device, non_blocking=True)
+    def combine(self, y, route, pos):
+        return self.ftc.moe_combine(y, route, pos=pos)
 
 
 class EPMoE:
-    """Rank r of G of an expert-parallel MoE layer."""
+    """Rank r of G of an expert-parallel MoE layer for up to ``max_tokens``
+    tokens per rank (the exchange capacity)."""
 
-    def __init__(self, n_experts, top_k, n_embd, G, rank, ops, group=None):
+    def __init__(self, n_experts, top_k, n_embd, G, rank, ops, max_tokens, group=None):
         self.E, self.U, self.K, self.G, self.rank = n_experts, top_k, n_embd, G, rank
         self.El = n_experts // G
         expert_range(n_experts, G, rank)
         self.ops, self.group = ops, group
+        self.max_tokens = int(max_tokens)
+        self.cap = self.max_tokens * top_k
 
-    def _a2a(self, out, inp, out_splits=None, in_splits=None):
+    def _a2a(self, out, inp):
         import torch.distributed as dist
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        dist.all_to_all_single(out, inp, group=self.group)
         return out
 
     def forward(self, logits, x):
-        """logits: fp32 [T_r, E] and x: [T_r, n_embd] of this rank's tokens;
-        returns their MoE outputs (fp32 [T_r, n_embd])."""
-        import torch
-        ops, G, El, U = self.ops, self.G, self.El, self.U
+        """logits: fp32 [T_r, E] and x: [T_r, n_embd] of this rank's tokens
+        (T_r <= max_tokens); returns their MoE outputs (fp32 [T_r, n_embd])."""
+        ops, G, El, U, K, cap = self.ops, self.G, self.El, self.U, self.K, self.cap
         T = logits.shape[0]
-        R = T * U
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the layer's capacity of {self.max_tokens} per rank")
         route = ops.route(logits, U)
+        send, pos = ops.pack(x, route, G, cap)
         counts = route["counts"]
         if G > 1:
-            recv_counts = self._a2a(torch.empty_like(counts), counts)
+            recv_counts = self._a2a(counts.new_empty(counts.shape), counts)
+            recv = self._a2a(send.new_empty(send.shape), send)
         else:
-            recv_counts = counts
-        # the split sizes on the host: the layer's one synchronisation
-        c, rc = ops.to_host(counts, recv_counts)
-        c, rc = c.reshape(G, El), rc.reshape(G, El)
-        send_splits = [int(v) for v in c.sum(axis=1)]
-        recv_splits = [int(v) for v in rc.sum(axis=1)]
-        xg = ops.gather(x, route, R)  # rows in expert order = destination order
-        if G > 1:
-            xr = self._a2a(x.new_empty((sum(recv_splits), x.shape[1])), xg, recv_splits,
-                           send_splits)
-        else:
-            xr = xg
-        perm, lcounts, loffsets = regroup(rc)
-        pi = ops.index(perm)
-        yl = ops.experts(xr.index_select(0, pi), lcounts, loffsets)
-        yr = torch.empty_like(yl)
-        yr[pi] = yl
-        if G > 1:
-            yb = self._a2a(yl.new_empty((R, yl.shape[1])), yr, send_splits, recv_splits)
-        else:
-            yb = yr
-        return ops.combine(yb, route)
+            recv_counts, recv = counts, send
+        perm, inv, lcounts, loffsets = ops.regroup(recv_counts, G, El, cap)
+        xl = recv.reshape(G * cap, K).index_select(0, perm)
+        yl = ops.experts(xl, lcounts, loffsets, G * cap)
+        yr = yl.index_select(0, inv)
+        yb = self._a2a(yr.new_empty(yr.shape), yr) if G > 1 else yr
+        return ops.combine(yb, route, pos)

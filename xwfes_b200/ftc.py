@@ -55,6 +55,9 @@ SIGNATURES = {
     "ftc_moe_workspace_bytes": (C.c_size_t, [_p, _i64]),
     "ftc_moe_ffn": (C.c_int, [_p, _p, _p, C.c_int, _i64, _p, _p, C.c_size_t, _p]),
     "ftc_silu_mul_rows": (C.c_int, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "ftc_ep_pack": (C.c_int, [_p, C.c_int, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+                              _p, _p, _p]),
+    "ftc_ep_regroup": (C.c_int, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
     "ftc_peer_ar_create": (C.c_int, [C.c_int, C.c_int, _i64, C.POINTER(_p), _p]),
     "ftc_peer_ar_open": (C.c_int, [_p, _p]),
     "ftc_peer_ar_max_elems": (_i64, [_p]),
@@ -274,17 +277,50 @@ def moe_route(logits, top_k, stream=None):
     return r
 
 
-def moe_combine(y, route, out=None, stream=None):
-    """out[t] = sum_u w[t][u] * y[pos[t][u]] in expert first-use order."""
+def moe_combine(y, route, out=None, stream=None, pos=None):
+    """out[t] = sum_u w[t][u] * y[pos[t][u]] in expert first-use order
+    (``pos`` defaults to the routing's row positions)."""
     import torch
     T, U = route["idx"].shape
-    K = y.shape[1]
+    K = y.shape[-1]
     if out is None:
         out = torch.empty((T, K), dtype=torch.float32, device=y.device)
-    check(lib().ftc_moe_combine(y.data_ptr(), route["pos"].data_ptr(), route["idx"].data_ptr(),
+    pos = route["pos"] if pos is None else pos
+    check(lib().ftc_moe_combine(y.data_ptr(), pos.data_ptr(), route["idx"].data_ptr(),
                                 route["w"].data_ptr(), route["rank"].data_ptr(), T, U, K,
                                 out.data_ptr(), _stream(stream)), "ftc_moe_combine")
     return out
+
+
+def ep_pack(x, route, world, cap, send=None, stream=None):
+    """Rows of this rank's tokens into the equal-split send buffer
+    [world, cap, n_embd] (ftc_ep_pack); returns (send, pos_padded)."""
+    import torch
+    T, K = x.shape
+    U = route["idx"].shape[1]
+    E = route["counts"].shape[0]
+    xt = {torch.float32: F.F32, torch.bfloat16: F.BF16, torch.float16: F.F16}[x.dtype]
+    if send is None:
+        send = torch.empty((world, cap, K), dtype=x.dtype, device=x.device)
+    pp = torch.empty((T, U), dtype=torch.int32, device=x.device)
+    check(lib().ftc_ep_pack(x.data_ptr(), xt, T, K, route["idx"].data_ptr(),
+                            route["counts"].data_ptr(), route["pos"].data_ptr(),
+                            route["row_token"].data_ptr(), E, U, world, cap, send.data_ptr(),
+                            pp.data_ptr(), _stream(stream)), "ftc_ep_pack")
+    return send, pp
+
+
+def ep_regroup(recv_counts, world, n_local, cap, stream=None):
+    """(perm, inv, counts, offsets) int32 CUDA tensors of ftc_ep_regroup."""
+    import torch
+    dev = recv_counts.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    perm, inv = torch.empty(world * cap, **i32), torch.empty(world * cap, **i32)
+    counts, offsets = torch.empty(n_local, **i32), torch.empty(n_local, **i32)
+    check(lib().ftc_ep_regroup(recv_counts.data_ptr(), world, n_local, cap, perm.data_ptr(),
+                               inv.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
+                               _stream(stream)), "ftc_ep_regroup")
+    return perm, inv, counts, offsets
 
 
 class MoeLayer:
