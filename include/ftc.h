@@ -358,6 +358,18 @@ int64_t ftc_peer_ar_max_elems(const ftc_peer_ar* ar);
 int ftc_peer_ar_sum_f32(ftc_peer_ar* ar, const float* in, float* out, int64_t n, void* stream);
 int ftc_peer_ar_destroy(ftc_peer_ar* ar);
 
+/* A row-parallel decode GEMV and its allreduce in one kernel: every rank
+ * passes its shard w (N rows of Q4_K, its K columns) and its x (fp32, K);
+ * y = sum over the ranks of x . w^T (fp32, N <= max_elems), the same bits on
+ * every rank.  The kernel's producer pushes each finished row of the rank's
+ * partial into every rank's buffer and each CTA then sums its own rows over
+ * the ranks in rank order (bounded waits, as ftc_peer_ar_sum_f32).  Shares
+ * ar's call counters with ftc_peer_ar_sum_f32; every rank makes the same
+ * calls in the same order.  FTC_E_UNSUPPORTED if the shape or alignment does
+ * not fit the fused kernel. */
+int ftc_mul_mat_vec_allreduce(ftc_peer_ar* ar, int dtype, const void* w, int64_t N, int64_t K,
+                               int64_t row_stride, const float* x, float* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

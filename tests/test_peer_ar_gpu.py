@@ -6,6 +6,12 @@ ranks -- for vector lengths that take the float4 path and the scalar path,
 for repeated calls (the two buffer parities alternate) and for calls
 replayed from a CUDA graph (the call counters live on the device).
 
+Fused GEMV + allreduce (ftc_mul_mat_vec_allreduce): every rank's GEMV
+partial pushed by the GEMV kernel itself and summed there must equal the
+separate GEMV followed by ftc_peer_ar_sum_f32, bit for bit, on every rank --
+also interleaved with plain sums (the two share the call counters) and
+replayed from a CUDA graph.
+
 Failure path: when one rank does not join a call, the other's kernel gives
 up after the library's wait bound, records status 1 (ftc_device_status) and
 the process stays usable.  Nothing faults: the waiting rank only polls its
@@ -67,6 +73,40 @@ if mode == "sum":
     del g
     torch.cuda.synchronize()
     assert ftc.device_status() == 0
+elif mode == "fused":
+    from xwfes_b200 import formats as F, synth as S
+    shapes = [(8192, 1024), (1000, 3584), (4096, 4096)]
+    for i, (n, k) in enumerate(shapes):
+        w = torch.from_numpy(S.weight(F.Q4_K, n, k, seed=rank, name=f"par.{{i}}")).cuda()
+        for call in range(2):
+            x = torch.from_numpy(T.inputs(rank, k, 100 + call)).cuda().reshape(1, k)
+            yf = ar.mul_mat_vec_sum(w, F.Q4_K, n, k, x)
+            yr = ftc.mul_mat_vec(w, F.Q4_K, n, k, x)
+            ar.sum_(yr)
+            out[f"f{{i}}_{{call}}"] = yf.cpu().numpy()
+            out[f"r{{i}}_{{call}}"] = yr.cpu().numpy()
+    n, k = shapes[0]
+    w = torch.from_numpy(S.weight(F.Q4_K, n, k, seed=rank, name="par.0")).cuda()
+    x = torch.from_numpy(T.inputs(rank, k, 200)).cuda().reshape(1, k)
+    y = torch.empty(1, n, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        ar.mul_mat_vec_sum(w, F.Q4_K, n, k, x, y=y, stream=s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        ar.mul_mat_vec_sum(w, F.Q4_K, n, k, x, y=y, stream=s)
+    for call in range(3):
+        y.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        out[f"g_{{call}}"] = y.cpu().numpy()
+    del g
+    yr = ftc.mul_mat_vec(w, F.Q4_K, n, k, x)
+    ar.sum_(yr)
+    out["g_ref"] = yr.cpu().numpy()
+    torch.cuda.synchronize()
+    assert ftc.device_status() == 0
 else:  # rank 1 stays out of the call; rank 0 must time out cleanly
     if rank == 0:
         t = torch.ones(8192, device="cuda")
@@ -119,3 +159,15 @@ def test_absent_rank_times_out(tmp_path):
     status, secs = r0["status"]
     assert status == 1 and secs >= 1.0
     assert r0["after"].tolist() == [0, 2, 4, 6]
+
+
+def test_fused_gemv_allreduce_matches_separate(tmp_path):
+    r0, r1 = _run(tmp_path, "fused")
+    for i in range(3):
+        for call in range(2):
+            f, r = f"f{i}_{call}", f"r{i}_{call}"
+            assert np.array_equal(r0[f], r0[r]) and np.array_equal(r1[f], r1[r]), (i, call)
+            assert np.array_equal(r0[f], r1[f]), (i, call)
+    for call in range(3):
+        assert np.array_equal(r0[f"g_{call}"], r0["g_ref"])
+        assert np.array_equal(r1[f"g_{call}"], r0["g_ref"])

@@ -14,6 +14,27 @@ constexpr int kGemvMaxMats = 8;
 // x_p = x[0] for every p unless per_matrix_x.  With sel set, matrix p with
 // sel_slot[p] >= 0 starts at W[p] + sel[sel_slot[p]] * sel_stride (expert
 // ids read on the device after the preceding kernel, clamped to [0, sel_max]).
+// A peer allreduce buffer as the kernels see it (see peer_ar.cu): every
+// rank's data region ([2 parities][world][max_elems] words of fp32 value |
+// epoch << 32), this rank's call epoch and finished-CTA count.
+constexpr int kPeerMaxRanks = 8;
+constexpr int kPeerBlocks = 148;
+struct PeerView {
+    uint64_t* data[kPeerMaxRanks];
+    int world, rank;
+    int64_t max_elems;
+    uint32_t* ctr;  // [0] epoch of the last completed call, [1] CTAs done in this call
+};
+
+// Called once per CTA at the end of a call: the last CTA to finish makes
+// `epoch` the last completed call and resets the count for the next call.
+__device__ __forceinline__ void peer_call_done(uint32_t* ctr, uint32_t epoch) {
+    if (atomicAdd(&ctr[1], 1u) == gridDim.x - 1) {
+        ctr[1] = 0;
+        ctr[0] = epoch;
+    }
+}
+
 struct GemvSpec {
     int P;
     int64_t K, stride;
@@ -34,6 +55,9 @@ struct GemvSpec {
     int pf_n;
     const uint8_t* pf_ptr[kGemvMaxMats];
     int64_t pf_len[kGemvMaxMats];
+    // Allreduce over a tensor-parallel group (one matrix, y the sum over the
+    // ranks of their partial products): nullptr for a plain GEMV.
+    const PeerView* peer;
 };
 
 constexpr int64_t kGemvPrefetchWindow = 24ll << 20;

@@ -81,6 +81,10 @@ struct GemvBatch {
     const uint8_t* pf_ptr[kGemvMaxMats];
     int64_t pf_len[kGemvMaxMats];
     int64_t pf_total;
+    // fused allreduce (one matrix): y = sum over the group's ranks of their
+    // partial products, exchanged through peer memory (see peer_ar.cu)
+    int fused;
+    PeerView peer;
 };
 
 namespace {
@@ -287,6 +291,67 @@ __device__ __forceinline__ const uint8_t* matrix_base(const GemvBatch& B, int p)
     return w;
 }
 
+__device__ __forceinline__ void st_word(uint64_t* p, uint64_t v) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Fused allreduce, after the producer has pushed this CTA's rows to every
+// rank: every thread takes rows of this CTA's chunks, waits (bounded) until
+// each rank's word for the row carries this launch's epoch, and writes the
+// sum in rank order.  Every rank's CTA b owns the same rows (the ranks run
+// the same plan), so a CTA only waits for its counterparts.
+__device__ __noinline__ void fused_allreduce_tail(const GemvBatch& B, const ChunkWalk& cw, int RC) {
+    named_barrier(2, blockDim.x);  // this CTA's pushes are done
+    const PeerView& P = B.peer;
+    grid_dependency_wait();        // (returns at once: the pushes came after it)
+    const uint32_t epoch = P.ctr[0] + 1u;
+    const int world = P.world;
+    const uint64_t* d = P.data[P.rank] + (int64_t)(epoch & 1u) * world * P.max_elems;
+    const int64_t N = B.N[0];
+    const int nck = (cw.cend - cw.c0 + cw.step - 1) / cw.step;
+    uint64_t t0 = 0;
+    bool ok = true;
+    for (int idx = threadIdx.x; idx < nck * RC && ok; idx += blockDim.x) {
+        const int ci = idx / RC;
+        const int64_t row = (int64_t)(cw.c0 + ci * cw.step) * RC + (idx - ci * RC);
+        if (row >= N) continue;
+        uint64_t w[kPeerMaxRanks];
+        uint32_t pending = (1u << world) - 1u;
+        while (pending) {
+#pragma unroll
+            for (int s = 0; s < kPeerMaxRanks; ++s)
+                if ((pending >> s) & 1u) w[s] = ld_word(d + s * P.max_elems + row);
+#pragma unroll
+            for (int s = 0; s < kPeerMaxRanks; ++s)
+                if (((pending >> s) & 1u) && (uint32_t)(w[s] >> 32) == epoch) pending &= ~(1u << s);
+            if (pending) {
+                const uint64_t now = global_ns();
+                if (t0 == 0) {
+                    t0 = now;
+                } else if (now - t0 > kWaitLimitNs) {
+                    record_timeout();
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) break;
+        float a = __uint_as_float((uint32_t)w[0]);
+#pragma unroll
+        for (int s = 1; s < kPeerMaxRanks; ++s)
+            if (s < world) a += __uint_as_float((uint32_t)w[s]);
+        B.y[0][row] = a;
+    }
+    named_barrier(2, blockDim.x);
+    if (threadIdx.x == 0) peer_call_done(P.ctr, epoch);
+}
+
 template <int RPW>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int WK, int WR,
@@ -325,6 +390,11 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
         const uint64_t pol = policy_evict_first();
         bool ok = true;
         int it = 0;
+        // fused allreduce: this call's epoch, read before the first push,
+        // once the previous grid on the stream has completed (the weight
+        // copies above the wait still start early)
+        uint32_t epoch = 0;
+        bool have_epoch = false;
         auto reduce = [&](int j) {  // partials of iteration j -> y
             const int s = j % kStages, rd = (j / kStages) & 1;
             const int c = cw.c0 + j * cw.step;
@@ -335,7 +405,20 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
                 const float* r = red + ((rd * kStages + s) * WK) * RM + row;
                 float v = 0.f;
                 for (int wk = 0; wk < WK; ++wk) v += r[wk * RM];
-                B.y[p][(int64_t)lc * RC + row] = v;
+                if (B.fused) {  // this rank's partial row, tagged, into every rank's slot
+                    const PeerView& P = B.peer;
+                    if (!have_epoch) {
+                        grid_dependency_wait();
+                        epoch = P.ctr[0] + 1u;
+                        have_epoch = true;
+                    }
+                    const int64_t slot = ((int64_t)(epoch & 1u) * P.world + P.rank) * P.max_elems +
+                                         (int64_t)lc * RC + row;
+                    const uint64_t wv = ((uint64_t)epoch << 32) | __float_as_uint(v);
+                    for (int q = 0; q < P.world; ++q) st_word(P.data[q] + slot, wv);
+                } else {
+                    B.y[p][(int64_t)lc * RC + row] = v;
+                }
             }
         };
         auto issue = [&](int c, int s) {
@@ -389,6 +472,7 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
             for (int j = max(0, it - kStages); j < it; ++j)
                 mbar_wait_warp(&full[j % kStages], (j / kStages) & 1);
         }
+        if (B.fused) fused_allreduce_tail(B, cw, RC);
         return;
     }
 
@@ -450,6 +534,7 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (B.fused) fused_allreduce_tail(B, cw, RC);
 }
 
 struct Q4kPlan {
@@ -525,6 +610,8 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
         ntot += g.N[i];
     }
     if (g.sel && (g.sel_stride % 16 || g.sel_max < 0)) return FTC_E_UNSUPPORTED;
+    if (g.peer && (P != 1 || g.per_matrix_x || g.sel || g.N[0] > g.peer->max_elems))
+        return FTC_E_UNSUPPORTED;
     Q4kPlan p;
     if (!plan_q4k(ntot, g.K, g.stride, p)) return FTC_E_UNSUPPORTED;
     static int sms = 0;
@@ -559,6 +646,10 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     }
     const int nchunks = B.first_chunk[P];
     p.grid = std::min(nchunks, sms);
+    B.fused = g.peer ? 1 : 0;
+    if (g.peer) {
+        B.peer = *g.peer;
+    }
     if (g.per_matrix_x) {
         // one CTA per matrix, then each further CTA to the matrix with the
         // most chunks per CTA (no CTA without a chunk)

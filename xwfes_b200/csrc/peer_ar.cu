@@ -13,7 +13,8 @@
 // Layout.  Every rank owns one device region, mapped by every other rank
 // through a CUDA IPC handle:
 //   data  [2 parities][world source ranks][max_elems] u64 (value | epoch << 32)
-//   ctr   [kArBlocks] uint32   (this rank's call counter per block)
+//   ctr   [2] uint32: this rank's call epoch, and the CTAs of the current
+//         call that have finished (the last one advances the epoch)
 // A call runs kArBlocks CTAs; CTA b owns slice b of the vector.  It
 //   1. stores its slice of `in` into slot [parity][rank] of every rank's data
 //      (its own included) -- 8-byte stores to peer addresses over NVLink;
@@ -21,11 +22,15 @@
 //      word until the word carries this call's epoch (bounded in time);
 //   3. sums the sources in rank order 0, 1, ... world-1 into `out`.
 // Every rank adds the same values in the same order, so all ranks hold the
-// same bits.  The epoch is the per-block call counter kept in device memory
-// (graph replays advance it), and the two parities keep a rank that has
-// moved on to the next call from overwriting a slot a slower peer is still
-// reading: a rank can only be one call ahead, because finishing a call needs
-// every peer's words of that call.
+// same bits.  The epoch counts this rank's calls in device memory (graph
+// replays advance it): every CTA of a call reads it once the previous call
+// on the stream has completed, and the CTA that finishes last advances it.
+// One epoch per call, not per CTA, because a given element is written by
+// different CTAs in different kinds of calls (slices here, row chunks in the
+// fused GEMV).  The two parities keep a rank that has moved on to the next
+// call from overwriting a slot a slower peer is still reading: a rank can
+// only be one call ahead, because finishing a call needs every peer's words
+// of that call.
 //
 // A peer that never arrives makes the wait give up after the same bound as
 // every other wait of this library (FTC_DEVSTAT_WAIT_TIMEOUT) and the CTA
@@ -34,6 +39,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "gemv_batch.cuh"
 #include "sm100.cuh"
 
 namespace ftc {
@@ -42,10 +48,10 @@ FTC_DEVSTAT_READER(devstat_peer_ar)
 
 namespace {
 
-constexpr int kArBlocks = 148;  // one CTA per SM, every call (the call counters are per CTA)
+constexpr int kArBlocks = kPeerBlocks;  // one CTA per SM, every call (the call counters are per CTA)
 constexpr int kArThreads = 256;
 constexpr int kArBatch = 4;     // elements a thread gathers at once
-constexpr int kArMaxRanks = 8;
+constexpr int kArMaxRanks = kPeerMaxRanks;
 
 struct ArPeers {
     uint64_t* data[kArMaxRanks];  // each rank's data region (this rank's own included)
@@ -69,7 +75,7 @@ peer_ar_f32(const __grid_constant__ ArPeers P, int rank, int world, int64_t max_
     __shared__ uint32_t s_epoch;
     __shared__ int s_ok;
     if (threadIdx.x == 0) {
-        s_epoch = ctr[b] + 1u;
+        s_epoch = ctr[0] + 1u;  // the previous call on the stream has completed
         s_ok = 1;
     }
     __syncthreads();
@@ -133,7 +139,7 @@ peer_ar_f32(const __grid_constant__ ArPeers P, int rank, int world, int64_t max_
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) ctr[b] = epoch;
+    if (threadIdx.x == 0) peer_call_done(ctr, epoch);
 }
 
 }  // namespace
@@ -149,6 +155,22 @@ struct ftc_peer_ar {
     ftc::ArPeers peers = {};
     bool open = false;
 };
+
+namespace ftc {
+
+// The buffer of an opened ftc_peer_ar, for kernels that push their partial
+// results into it themselves (the fused GEMV + allreduce).
+int peer_ar_view(const ftc_peer_ar* ar, PeerView* v) {
+    FTC_REQUIRE(ar && ar->open, FTC_E_INVALID, "peer allreduce: ftc_peer_ar_open not called");
+    for (int q = 0; q < kPeerMaxRanks; ++q) v->data[q] = q < ar->world ? ar->peers.data[q] : nullptr;
+    v->world = ar->world;
+    v->rank = ar->rank;
+    v->max_elems = ar->max_elems;
+    v->ctr = ar->ctr;
+    return FTC_OK;
+}
+
+}  // namespace ftc
 
 namespace {
 
@@ -231,6 +253,38 @@ int ftc_peer_ar_sum_f32(ftc_peer_ar* ar, const float* in, float* out, int64_t n,
         ar->peers, ar->rank, ar->world, ar->max_elems, in, out, n, ar->ctr);
     FTC_CUDA(cudaGetLastError());
     return ok();
+}
+
+int ftc_mul_mat_vec_allreduce(ftc_peer_ar* ar, int dtype, const void* w, int64_t N, int64_t K,
+                               int64_t row_stride, const float* x, float* y, void* stream) {
+    using namespace ftc;
+    FTC_REQUIRE(ar && w && x && y, FTC_E_INVALID, "ftc_mul_mat_vec_allreduce: null pointer");
+    FTC_REQUIRE(dtype == FTC_Q4_K, FTC_E_UNSUPPORTED,
+                "ftc_mul_mat_vec_allreduce: Q4_K weights only");
+    FTC_REQUIRE(N > 0 && K > 0 && K % 256 == 0 && row_stride >= (K / 256) * 144, FTC_E_INVALID,
+                "ftc_mul_mat_vec_allreduce: bad shape");
+    FTC_REQUIRE(N <= ar->max_elems, FTC_E_INVALID,
+                "ftc_mul_mat_vec_allreduce: N exceeds the buffer's max_elems");
+    if (inject_fail("ftc_mul_mat_vec_allreduce"))
+        return set_error(FTC_E_INJECTED, "ftc_mul_mat_vec_allreduce: injected failure");
+    PeerView v;
+    int rc = peer_ar_view(ar, &v);
+    if (rc) return rc;
+    GemvSpec g = {};
+    g.P = 1;
+    g.K = K;
+    g.stride = row_stride;
+    g.W[0] = static_cast<const uint8_t*>(w);
+    g.N[0] = N;
+    g.y[0] = y;
+    g.x[0] = x;
+    g.peer = &v;
+    rc = gemv_q4k_batch(g, (cudaStream_t)stream);
+    if (rc == FTC_E_UNSUPPORTED)
+        return set_error(rc, "ftc_mul_mat_vec_allreduce: shape or alignment not supported by the "
+                             "fused kernel (16-byte aligned rows and x; use ftc_mul_mat_vec + "
+                             "ftc_peer_ar_sum_f32)");
+    return rc ? rc : ok();
 }
 
 int ftc_peer_ar_destroy(ftc_peer_ar* ar) {

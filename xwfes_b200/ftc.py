@@ -63,6 +63,7 @@ SIGNATURES = {
     "ftc_peer_ar_max_elems": (_i64, [_p]),
     "ftc_peer_ar_sum_f32": (C.c_int, [_p, _p, _p, _i64, _p]),
     "ftc_peer_ar_destroy": (C.c_int, [_p]),
+    "ftc_mul_mat_vec_allreduce": (C.c_int, [_p, C.c_int, _p, _i64, _i64, _i64, _p, _p, _p]),
 }
 
 
@@ -568,6 +569,19 @@ class PeerAllreduce:
         check(lib().ftc_peer_ar_sum_f32(self._ar, t.data_ptr(), t.data_ptr(), t.numel(),
                                         _stream(stream)), "ftc_peer_ar_sum_f32")
         return t
+
+    def mul_mat_vec_sum(self, w, dtype, n, k, x, y=None, row_stride=None, stream=None):
+        """y = sum over the ranks of x . W^T for this rank's shard W (one token,
+        fp32), GEMV and allreduce in one kernel (ftc_mul_mat_vec_allreduce)."""
+        import torch
+        t = F.dtype_id(dtype)
+        if y is None:
+            y = torch.empty((1, n), dtype=torch.float32, device=x.device)
+        rs = row_stride if row_stride is not None else row_bytes(t, k)
+        check(lib().ftc_mul_mat_vec_allreduce(self._ar, t, w.data_ptr(), n, k, rs, x.data_ptr(),
+                                              y.data_ptr(), _stream(stream)),
+              "ftc_mul_mat_vec_allreduce")
+        return y
 
     def close(self):
         if self._ar:

@@ -133,14 +133,23 @@ class CudaOps:
     def upload(self, arr):
         return self.torch.from_numpy(arr).to(self.device)
 
-    def silu_matmul(self, gu, n, w):
-        """(silu(gate) * up) . W^T for rows gu = [gate (n) | up (n)]."""
+    def silu_matmul(self, gu, n, w, peer=None):
+        """(silu(gate) * up) . W^T for rows gu = [gate (n) | up (n)]; with
+        ``peer`` (one token) the product is also summed over the ranks."""
         ftc, M = self.ftc, gu.shape[0]
         wt, wn, wk = w
         if M <= 8:
-            return ftc.mul_mat_vec(wt, F.Q4_K, wn, wk, ftc.silu_mul_rows(gu, n))
+            h = ftc.silu_mul_rows(gu, n)
+            if peer is not None:
+                return peer.mul_mat_vec_sum(wt, F.Q4_K, wn, wk, h)
+            return ftc.mul_mat_vec(wt, F.Q4_K, wn, wk, h)
         x16, e = ftc.silu_mul_rows(gu, n, to_f16=True)
         return ftc.gemm_rowscaled(wt, F.Q4_K, wn, wk, x16, e)
+
+    def matmul_sum(self, x, w, peer):
+        """x . W^T summed over the ranks, GEMV and allreduce fused (one token)."""
+        wt, wn, wk = w
+        return peer.mul_mat_vec_sum(wt, F.Q4_K, wn, wk, x.contiguous())
 
     def matmuls(self, x, ws):
         """[x . W^T for (W, n, k) in ws], x fp32 [M, k] shared by all."""
@@ -196,7 +205,15 @@ class TPBlock:
         nq, nkv, nf = d["n_q"] // G, d["n_kv"] // G, d["n_ff"] // G
         qkv = self.ops.matmuls(x, [W["qkv"]])[0]
         q, k, v = qkv[:, :nq], qkv[:, nq:nq + nkv], qkv[:, nq + nkv:]
+        if self._fused(x):  # one token: the row-parallel GEMVs carry their allreduce
+            h = self.ops.matmul_sum(q, W["o"], self.peer)
+            gu = self.ops.matmuls(h, [W["gate_up"]])[0]
+            return self.ops.silu_matmul(gu, nf, W["down"], peer=self.peer), (q, k, v)
         h = self._allreduce(self.ops.matmuls(q, [W["o"]])[0])
         gu = self.ops.matmuls(h, [W["gate_up"]])[0]
         out = self._allreduce(self.ops.silu_matmul(gu, nf, W["down"]))
         return out, (q, k, v)
+
+    def _fused(self, x):
+        return (self.G > 1 and self.peer is not None and x.shape[0] == 1 and
+                hasattr(self.ops, "matmul_sum"))
