@@ -348,7 +348,11 @@ int ftc_ep_regroup(const int32_t* recv_counts, int64_t world, int64_t n_local, i
  * with all handles in rank order.  Calls must then be made by every rank in
  * the same order (stream-ordered on each rank; CUDA-graph capture is fine).
  * A rank that does not join a call makes the others' kernels give up after
- * the library's wait bound and record status 1 (ftc_device_status). */
+ * the library's wait bound and record status 1 (ftc_device_status).
+ * Vectors of 16384+ elements on 4+ ranks use a two-shot exchange (each
+ * element to an owner rank, the owner's rank-ordered sum to every rank);
+ * the environment variable FTC_PEER_AR_TWO_SHOT=<elements> sets that
+ * threshold for any group size. */
 #define FTC_IPC_HANDLE_BYTES 64
 typedef struct ftc_peer_ar ftc_peer_ar;
 int ftc_peer_ar_create(int rank, int world, int64_t max_elems, ftc_peer_ar** out, void* handle);

@@ -136,8 +136,11 @@ def _run(tmp_path, mode):
     port = _free_port()
     procs = []
     for r in range(2):
+        # vectors of 65536+ elements take the two-shot exchange (by default only
+        # used on 4+ ranks), so both exchanges are covered on two GPUs
         env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r),
-                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                   FTC_PEER_AR_TWO_SHOT="65536")
         procs.append(subprocess.Popen([sys.executable, "-c", code], env=env, cwd=ROOT))
     for p in procs:
         assert p.wait(timeout=300) == 0

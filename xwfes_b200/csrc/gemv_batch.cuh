@@ -15,8 +15,8 @@ constexpr int kGemvMaxMats = 8;
 // sel_slot[p] >= 0 starts at W[p] + sel[sel_slot[p]] * sel_stride (expert
 // ids read on the device after the preceding kernel, clamped to [0, sel_max]).
 // A peer allreduce buffer as the kernels see it (see peer_ar.cu): every
-// rank's data region ([2 parities][world][max_elems] words of fp32 value |
-// epoch << 32), this rank's call epoch and finished-CTA count.
+// rank's data region ([2 parities][world + 1][max_elems] words of fp32 value
+// | epoch << 32), this rank's call epoch and finished-CTA count.
 constexpr int kPeerMaxRanks = 8;
 constexpr int kPeerBlocks = 148;
 struct PeerView {

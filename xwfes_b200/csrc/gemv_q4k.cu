@@ -312,7 +312,7 @@ __device__ __noinline__ void fused_allreduce_tail(const GemvBatch& B, const Chun
     grid_dependency_wait();        // (returns at once: the pushes came after it)
     const uint32_t epoch = P.ctr[0] + 1u;
     const int world = P.world;
-    const uint64_t* d = P.data[P.rank] + (int64_t)(epoch & 1u) * world * P.max_elems;
+    const uint64_t* d = P.data[P.rank] + (int64_t)(epoch & 1u) * (world + 1) * P.max_elems;
     const int64_t N = B.N[0];
     const int nck = (cw.cend - cw.c0 + cw.step - 1) / cw.step;
     uint64_t t0 = 0;
@@ -412,8 +412,8 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
                         epoch = P.ctr[0] + 1u;
                         have_epoch = true;
                     }
-                    const int64_t slot = ((int64_t)(epoch & 1u) * P.world + P.rank) * P.max_elems +
-                                         (int64_t)lc * RC + row;
+                    const int64_t slot = ((int64_t)(epoch & 1u) * (P.world + 1) + P.rank) *
+                                             P.max_elems + (int64_t)lc * RC + row;
                     const uint64_t wv = ((uint64_t)epoch << 32) | __float_as_uint(v);
                     for (int q = 0; q < P.world; ++q) st_word(P.data[q] + slot, wv);
                 } else {

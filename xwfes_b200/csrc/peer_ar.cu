@@ -12,7 +12,8 @@
 //
 // Layout.  Every rank owns one device region, mapped by every other rank
 // through a CUDA IPC handle:
-//   data  [2 parities][world source ranks][max_elems] u64 (value | epoch << 32)
+//   data  [2 parities][world source ranks + 1][max_elems] u64 (value | epoch << 32);
+//         the extra slot holds the owners' sums of a two-shot call
 //   ctr   [2] uint32: this rank's call epoch, and the CTAs of the current
 //         call that have finished (the last one advances the epoch)
 // A call runs kArBlocks CTAs; CTA b owns slice b of the vector.  It
@@ -35,6 +36,7 @@
 // A peer that never arrives makes the wait give up after the same bound as
 // every other wait of this library (FTC_DEVSTAT_WAIT_TIMEOUT) and the CTA
 // returns without writing its slice.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -67,48 +69,28 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(kArThreads)
-peer_ar_f32(const __grid_constant__ ArPeers P, int rank, int world, int64_t max_elems,
-            const float* __restrict__ in, float* __restrict__ out, int64_t n,
-            uint32_t* __restrict__ ctr) {
-    const int b = blockIdx.x;
-    __shared__ uint32_t s_epoch;
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-        s_epoch = ctr[0] + 1u;  // the previous call on the stream has completed
-        s_ok = 1;
-    }
-    __syncthreads();
-    const uint32_t epoch = s_epoch;
-    const int par = (int)(epoch & 1u);
-    const int64_t i0 = n * b / kArBlocks, i1 = n * (b + 1) / kArBlocks;
-    const int64_t slot = ((int64_t)par * world + rank) * max_elems;
-    const uint64_t tag = (uint64_t)epoch << 32;
-
-    // 1. push this rank's slice to every rank
-    for (int64_t i = i0 + threadIdx.x; i < i1; i += kArThreads) {
-        const uint64_t w = tag | __float_as_uint(in[i]);
-        for (int q = 0; q < world; ++q) st_word(P.data[q] + slot + i, w);
-    }
-    // 2. + 3. gather every source's word of each element (a thread keeps the
-    // loads of kArBatch elements x all sources in flight together), then sum
-    // in rank order
-    const uint64_t* d = P.data[rank] + (int64_t)par * world * max_elems;
-    volatile int* ok = &s_ok;
+// Waits (bounded) until the words of elements [lo, hi) from `nsrc` sources
+// (source s at d + s * stride) carry `epoch`, then calls emit(i, sum) with the
+// sources summed in order.  A thread keeps the loads of kArBatch elements x
+// all sources in flight together.  Returns false when the wait gave up.
+template <class Emit>
+__device__ __forceinline__ bool gather_sum(const uint64_t* d, int nsrc, int64_t stride, int64_t lo,
+                                           int64_t hi, uint32_t epoch, volatile int* ok,
+                                           Emit emit) {
     uint64_t t0 = 0;
-    for (int64_t base = i0 + threadIdx.x; base < i1 && *ok; base += kArThreads * kArBatch) {
+    for (int64_t base = lo + threadIdx.x; base < hi && *ok; base += kArThreads * kArBatch) {
         uint64_t w[kArBatch][kArMaxRanks];
         uint32_t pending = 0;  // bit e * kArMaxRanks + s: word (element e, source s) not seen yet
 #pragma unroll
         for (int e = 0; e < kArBatch; ++e)
-            if (base + e * kArThreads < i1) pending |= ((1u << world) - 1u) << (e * kArMaxRanks);
+            if (base + e * kArThreads < hi) pending |= ((1u << nsrc) - 1u) << (e * kArMaxRanks);
         while (pending) {
 #pragma unroll
             for (int e = 0; e < kArBatch; ++e)
 #pragma unroll
                 for (int s = 0; s < kArMaxRanks; ++s)
                     if ((pending >> (e * kArMaxRanks + s)) & 1u)
-                        w[e][s] = ld_word(d + s * max_elems + base + e * kArThreads);
+                        w[e][s] = ld_word(d + s * stride + base + e * kArThreads);
 #pragma unroll
             for (int e = 0; e < kArBatch; ++e)
 #pragma unroll
@@ -123,20 +105,75 @@ peer_ar_f32(const __grid_constant__ ArPeers P, int rank, int world, int64_t max_
                     record_timeout();
                     *ok = 0;
                 }
-                if (!*ok) break;
+                if (!*ok) return false;
             }
         }
-        if (pending) break;
 #pragma unroll
         for (int e = 0; e < kArBatch; ++e) {
             const int64_t i = base + e * kArThreads;
-            if (i >= i1) break;
+            if (i >= hi) break;
             float a = __uint_as_float((uint32_t)w[e][0]);
 #pragma unroll
             for (int s = 1; s < kArMaxRanks; ++s)
-                if (s < world) a += __uint_as_float((uint32_t)w[e][s]);
-            out[i] = a;
+                if (s < nsrc) a += __uint_as_float((uint32_t)w[e][s]);
+            emit(i, a);
         }
+    }
+    return *ok != 0;
+}
+
+// One-shot (two_shot == 0): every rank pushes its slice of every element to
+// every rank and sums all sources itself.  Two-shot: within each CTA's slice
+// [i0, i1), rank o owns the o-th of `world` sub-slices; every rank pushes
+// each element only to its owner (slot [par][rank]), the owner sums the
+// sources in rank order and pushes the sum to every rank (slot [par][world]),
+// and every rank waits for those -- 2 words per element leave a rank instead
+// of `world`, for one more NVLink hop.
+__global__ void __launch_bounds__(kArThreads)
+peer_ar_f32(const __grid_constant__ ArPeers P, int rank, int world, int64_t max_elems,
+            const float* __restrict__ in, float* __restrict__ out, int64_t n, int two_shot,
+            uint32_t* __restrict__ ctr) {
+    const int b = blockIdx.x;
+    __shared__ uint32_t s_epoch;
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        s_epoch = ctr[0] + 1u;  // the previous call on the stream has completed
+        s_ok = 1;
+    }
+    __syncthreads();
+    const uint32_t epoch = s_epoch;
+    const int par = (int)(epoch & 1u);
+    const int64_t i0 = n * b / kArBlocks, i1 = n * (b + 1) / kArBlocks;
+    const int64_t pstride = (int64_t)(world + 1) * max_elems;  // slots of one parity
+    const int64_t slot = par * pstride + (int64_t)rank * max_elems;
+    const uint64_t tag = (uint64_t)epoch << 32;
+    const uint64_t* mine = P.data[rank] + par * pstride;
+    volatile int* ok = &s_ok;
+
+    if (!two_shot) {
+        for (int64_t i = i0 + threadIdx.x; i < i1; i += kArThreads) {
+            const uint64_t w = tag | __float_as_uint(in[i]);
+            for (int q = 0; q < world; ++q) st_word(P.data[q] + slot + i, w);
+        }
+        gather_sum(mine, world, max_elems, i0, i1, epoch, ok,
+                   [&](int64_t i, float a) { out[i] = a; });
+    } else {
+        const int64_t len = i1 - i0;
+        auto owner_lo = [&](int o) { return i0 + len * o / world; };
+        for (int64_t i = i0 + threadIdx.x; i < i1; i += kArThreads) {
+            int o = 0;  // owner: the sub-slice holding i
+            while (o + 1 < world && owner_lo(o + 1) <= i) ++o;
+            st_word(P.data[o] + slot + i, tag | __float_as_uint(in[i]));
+        }
+        // the owner's sub-slice: sum the sources, push the sum to every rank
+        const uint64_t* sumslot = mine + (int64_t)world * max_elems;
+        if (gather_sum(mine, world, max_elems, owner_lo(rank), owner_lo(rank + 1), epoch, ok,
+                       [&](int64_t i, float a) {
+                           const uint64_t w = tag | __float_as_uint(a);
+                           for (int q = 0; q < world; ++q)
+                               st_word(P.data[q] + par * pstride + (int64_t)world * max_elems + i, w);
+                       }))
+            gather_sum(sumslot, 1, 0, i0, i1, epoch, ok, [&](int64_t i, float a) { out[i] = a; });
     }
     __syncthreads();
     if (threadIdx.x == 0) peer_call_done(ctr, epoch);
@@ -175,7 +212,8 @@ int peer_ar_view(const ftc_peer_ar* ar, PeerView* v) {
 namespace {
 
 size_t region_bytes(int world, int64_t max_elems) {
-    const size_t data = (size_t)2 * world * max_elems * sizeof(uint64_t);
+    // per parity: one slot per source rank + one for the owners' sums (two-shot)
+    const size_t data = (size_t)2 * (world + 1) * max_elems * sizeof(uint64_t);
     return ((data + 255) & ~size_t(255)) + ftc::kArBlocks * sizeof(uint32_t);
 }
 
@@ -249,8 +287,17 @@ int ftc_peer_ar_sum_f32(ftc_peer_ar* ar, const float* in, float* out, int64_t n,
     if (n == 0) return ok();
     if (inject_fail("ftc_peer_ar_sum_f32"))
         return set_error(FTC_E_INJECTED, "ftc_peer_ar_sum_f32: injected failure");
+    // Two-shot once the one-shot's world-fold traffic outweighs the extra hop:
+    // from 16384 elements on 4 or more ranks (with 2 ranks both move the same
+    // bytes).  FTC_PEER_AR_TWO_SHOT=<elements> overrides the threshold.
+    static const int64_t env_min = [] {
+        const char* e = std::getenv("FTC_PEER_AR_TWO_SHOT");
+        return e ? std::atoll(e) : (int64_t)-1;
+    }();
+    const int64_t two_min = env_min >= 0 ? env_min : (ar->world > 2 ? 16384 : INT64_MAX);
+    const int two_shot = ar->world > 1 && n >= two_min;
     peer_ar_f32<<<kArBlocks, kArThreads, 0, (cudaStream_t)stream>>>(
-        ar->peers, ar->rank, ar->world, ar->max_elems, in, out, n, ar->ctr);
+        ar->peers, ar->rank, ar->world, ar->max_elems, in, out, n, two_shot, ar->ctr);
     FTC_CUDA(cudaGetLastError());
     return ok();
 }
