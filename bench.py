@@ -679,6 +679,27 @@ def run_ncu_gemm_probe():
     return 0
 
 
+def run_ncu_gemm_split_probe():
+    """Three split-K dequant-GEMM launches on a tensor-parallel rank's shape
+    (the stacked q/k/v shard of config 4 at 8 GPUs: 1280 x 8192 Q4_K, 16
+    tokens, fp16 row-scaled operands): 10 output tiles, so K is split over
+    the SMs and the partials are summed by the last unit of each tile."""
+    import torch
+    from xwfes_b200 import ftc
+    dev = torch.device("cuda", 0)
+    n, k, m = 1280, 8192, 16
+    w = torch.from_numpy(S.weight(F.Q4_K, n, k, seed=0, name=f"p.{n}x{k}")).to(dev)
+    x = torch.from_numpy(S.activations_f32(m, k, seed=0, name=f"p.s{m}")).to(dev)
+    x16, e = ftc.rows_to_f16(x)
+    y = torch.empty((m, n), dtype=torch.float32, device=dev)
+    for _ in range(3):
+        ftc.gemm_rowscaled(w, F.Q4_K, n, k, x16, e, y=y)
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": "gemm_q4k_tc split-K 1280x8192 M=16 x3",
+                      "status": ftc.device_status()}))
+    return 0
+
+
 # ----------------------------------------------------------- CPU baselines
 
 def cpu_sample(threads, budget_s=10.0):
@@ -785,6 +806,9 @@ def main():
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: a few launches of the dominant kernel "
                          "(grouped gate+up Q4_K GEMV) on one layer copy, no timing")
+    ap.add_argument("--ncu-gemm-split", action="store_true",
+                    help="profiling mode: three split-K dequant-GEMM launches on a TP rank's "
+                         "q/k/v shard (1280x8192, M=16), no timing")
     ap.add_argument("--ncu-gemm", action="store_true",
                     help="profiling mode: three launches of the config-3 dequant-GEMM "
                          "(14336x4096, M=2048, bf16), no timing")
@@ -799,6 +823,8 @@ def main():
         return run_ncu_probe()
     if args.ncu_gemm:
         return run_ncu_gemm_probe()
+    if args.ncu_gemm_split:
+        return run_ncu_gemm_split_probe()
 
     if args.impl == "reference":
         if rank != 0:
