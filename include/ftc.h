@@ -317,6 +317,7 @@ int ftc_expert_chunk_static(int dtype, const float* x, float* out, const void* g
  * experts; slots past cnt_d are left as they are); pos_padded[t][u] =
  * d * cap + i, the slot of token t's u-th row, i.e. where its expert output
  * comes back in the reverse exchange (pass it to ftc_moe_combine as pos).
+ * With T == 0 (a rank without tokens) only counts and send are read.
  * The per-expert counts themselves are the [world][E/world] counts to send.
  *
  * ftc_ep_regroup, on the receiving rank with recv_counts[src][e] (rows of

@@ -82,6 +82,11 @@ class OracleEPOps:
         self.O, self.gate, self.up, self.down = oracle, gate, up, down
 
     def route(self, logits, u):
+        if logits.shape[0] == 0:  # a rank without tokens (T < world)
+            z = np.zeros((0, u), np.int64)
+            return {"idx": z, "w": z.astype(np.float32), "pos": z, "row_token": np.zeros(0, np.int64),
+                    "counts": torch.zeros(logits.shape[1], dtype=torch.int32),
+                    "rank": np.full(logits.shape[1], -1, np.int32)}
         return np_route(self.O, logits.numpy(), u)
 
     def pack(self, x, route, world, cap):
@@ -123,12 +128,12 @@ def _weights():
             S.expert_weights(F.Q4_K, E, K, FF, seed=3, name="ep.down"))
 
 
-def _inputs():
+def _inputs(T=T):
     return (S.router_logits(T, E, seed=7),
             S.activations_f32(T, K, seed=7, name="ep.x"))
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, T=T):
     import torch.distributed as dist
     from oracle import oracle as O
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -139,7 +144,7 @@ def _rank_main(rank, world, port, out_dir):
         e0, e1 = ep.expert_range(E, world, rank)
         layer = ep.EPMoE(E, U, K, world, rank, OracleEPOps(O, g[e0:e1], u[e0:e1], d[e0:e1]),
                          max_tokens=-(-T // world))
-        logits, x = _inputs()
+        logits, x = _inputs(T)
         t0, t1 = ep.token_range(T, world, rank)
         out = layer.forward(torch.from_numpy(logits[t0:t1]), torch.from_numpy(x[t0:t1]))
         np.save(os.path.join(out_dir, f"out{rank}.npy"), out.numpy())
@@ -162,5 +167,19 @@ def test_two_ranks_match_single_process_moe(tmp_path, oracle):
     got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(2)])
     g, u, d = _weights()
     logits, x = _inputs()
+    ref = oracle.moe_ffn(x, logits, g, u, d, F.Q4_K, K, FF, U, threads=2)
+    np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6 * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("T_,world", [(1, 2), (5, 4)])
+def test_ranks_without_tokens_or_with_fewer_experts_than_top_k(tmp_path, oracle, T_, world):
+    """T < world leaves ranks without tokens (they still take part in every
+    exchange); 4 ranks of a 4-expert top-2 layer hold one expert each."""
+    import torch.multiprocessing as mp
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), T_), nprocs=world,
+                       start_method="spawn", join=True)
+    got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(world)])
+    g, u, d = _weights()
+    logits, x = _inputs(T_)
     ref = oracle.moe_ffn(x, logits, g, u, d, F.Q4_K, K, FF, U, threads=2)
     np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6 * np.abs(ref).max())

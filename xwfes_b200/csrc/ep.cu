@@ -125,8 +125,8 @@ int ep_pack(const void* x, int x_dtype, int64_t T, int64_t n_embd, const int32_t
             const int32_t* counts, const int32_t* pos, const int32_t* row_token, int64_t n_experts,
             int64_t top_k, int64_t world, int64_t cap, void* send, int32_t* pos_padded,
             cudaStream_t st) {
-    FTC_REQUIRE(x && idx && counts && pos && row_token && send && pos_padded, FTC_E_INVALID,
-                "ftc_ep_pack: null pointer");
+    FTC_REQUIRE(counts && send && (T == 0 || (x && idx && pos && row_token && pos_padded)),
+                FTC_E_INVALID, "ftc_ep_pack: null pointer");
     FTC_REQUIRE(x_dtype == FTC_F32 || x_dtype == FTC_BF16 || x_dtype == FTC_F16,
                 FTC_E_UNSUPPORTED, "ftc_ep_pack: x must be fp32, bf16 or fp16");
     FTC_REQUIRE(world >= 1 && n_experts >= 1 && n_experts <= kEpMaxExperts && n_experts % world == 0,

@@ -479,7 +479,9 @@ int moe_route_only(const float* logits, int64_t T, int64_t E, int64_t U, int32_t
     FTC_REQUIRE(E >= 1 && E <= kMaxExperts && U >= 1 && U <= kMaxTopK && U <= E, FTC_E_INVALID,
                 "ftc_moe_route: need 1 <= top_k <= min(8, n_experts) <= 256");
     FTC_REQUIRE(T >= 0 && T * U <= INT32_MAX / 2, FTC_E_INVALID, "ftc_moe_route: bad T");
-    FTC_REQUIRE(logits && idx && w && counts && offsets && rank && pos && row_token,
+    // T == 0 (e.g. an expert-parallel rank without tokens): only the per-expert
+    // arrays are written, the per-token ones may be empty (null)
+    FTC_REQUIRE(counts && offsets && rank && (T == 0 || (logits && idx && w && pos && row_token)),
                 FTC_E_INVALID, "ftc_moe_route: null pointer");
     moe_route<<<1, kRouteThreads, 0, st>>>(logits, (int)T, (int)E, (int)U, idx, w, counts, offsets,
                                            rank, pos, row_token);
@@ -491,11 +493,11 @@ int moe_route_only(const float* logits, int64_t T, int64_t E, int64_t U, int32_t
 int moe_combine_only(const float* y, const int32_t* pos, const int32_t* idx, const float* w,
                      const int32_t* rank, int64_t T, int64_t U, int64_t K, float* out,
                      cudaStream_t st) {
-    FTC_REQUIRE(y && pos && idx && w && rank && out, FTC_E_INVALID, "ftc_moe_combine: null pointer");
     FTC_REQUIRE(T >= 0 && U >= 1 && U <= kMaxTopK && K > 0 && K % 4 == 0 && (uintptr_t)y % 16 == 0 &&
                     (uintptr_t)out % 16 == 0,
                 FTC_E_INVALID, "ftc_moe_combine: bad shape or alignment");
-    if (T == 0) return FTC_OK;
+    if (T == 0) return FTC_OK;  // nothing to combine (empty arrays may be null)
+    FTC_REQUIRE(y && pos && idx && w && rank && out, FTC_E_INVALID, "ftc_moe_combine: null pointer");
     moe_combine<<<grid_for(T * K / 4), 256, 0, st>>>(y, nullptr, pos, idx, w, rank, (int)T, (int)U,
                                                    (int)K, out);
     FTC_CUDA(cudaGetLastError());
