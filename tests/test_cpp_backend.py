@@ -19,7 +19,7 @@ def compile_test(out):
     cmd = ["g++", "-std=c++17", "-O2", "-I", os.path.join(HOST, "compat"), "-I", HOST,
            "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "oracle"),
            os.path.join(ROOT, "tests", "cpp", "test_cuda_backend.cpp"),
-           os.path.join(HOST, "cuda_backend.cpp"),
+           os.path.join(HOST, "cuda_backend.cpp"), os.path.join(HOST, "gguf.cpp"),
            "-L", os.path.dirname(ftc.LIB_PATH), "-lftcuda",
            "-L", os.path.join(ROOT, "oracle"), "-loracle",
            "-Wl,-rpath," + os.path.dirname(ftc.LIB_PATH) + ":" + os.path.join(ROOT, "oracle"),

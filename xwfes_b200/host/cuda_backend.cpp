@@ -60,4 +60,13 @@ void CudaBackend::upload(const HostTensor& t) {
     check(ftc_backend_upload(be_, t.data, n), "upload");
 }
 
+size_t CudaBackend::upload_all(const Gguf& model) {
+    size_t total = 0;
+    for (const auto& kv : model.tensors()) {
+        upload(kv.second);
+        total += kv.second.nbytes;
+    }
+    return total;
+}
+
 }  // namespace ft

@@ -10,6 +10,7 @@
 #include <string>
 
 #include "ft/backend.h"
+#include "ft/gguf.h"
 
 struct ftc_backend;
 
@@ -37,6 +38,11 @@ public:
 
     // Load a tensor's blocks into HBM once (call at Engine::load time).
     void upload(const HostTensor& t);
+    // Every tensor of a model file, blocks unchanged (the engine's load step,
+    // ft/src/engine.cpp:282-396): later matmuls and expert chunks on these
+    // tensors find their device copies instead of copying per call.
+    // Returns the bytes uploaded.
+    size_t upload_all(const Gguf& model);
 
 private:
     ftc_backend* be_ = nullptr;
