@@ -128,3 +128,45 @@ def test_library_refuses_to_fall_back(monkeypatch, tmp_path):
     monkeypatch.setattr(ftc, "_lib", None)
     with pytest.raises(FileNotFoundError):
         ftc.lib()
+
+
+def test_exchange_entry_points_validate_before_launch(lib):
+    """The expert-parallel bookkeeping, the row helpers and the peer
+    allreduce refuse bad arguments before any CUDA call."""
+    import ctypes as C
+    # ftc_ep_pack: per-token arrays may be empty only for T == 0
+    rc = lib.ftc_ep_pack(None, F.BF16, 4, 256, None, 256, None, None, 8, 2, 2, 8, 256, None, None)
+    assert rc == -1 and "null pointer" in ftc.last_error()
+    rc = lib.ftc_ep_pack(256, F.BF16, 4, 256, 256, 256, 256, 256, 8, 2, 3, 8, 256, 256, None)
+    assert rc == -1 and "split evenly" in ftc.last_error()
+    rc = lib.ftc_ep_pack(256, F.BF16, 4, 256, 256, 256, 256, 256, 8, 2, 2, 7, 256, 256, None)
+    assert rc == -1 and "capacity" in ftc.last_error()
+    rc = lib.ftc_ep_pack(256, F.Q4_K, 4, 256, 256, 256, 256, 256, 8, 2, 2, 8, 256, 256, None)
+    assert rc == -2
+    rc = lib.ftc_ep_pack(264, F.BF16, 4, 256, 256, 256, 256, 256, 8, 2, 2, 8, 256, 256, None)
+    assert rc == -1 and "aligned" in ftc.last_error()
+    # ftc_ep_regroup
+    rc = lib.ftc_ep_regroup(None, 2, 4, 8, 256, 256, 256, 256, None)
+    assert rc == -1 and "null" in ftc.last_error()
+    rc = lib.ftc_ep_regroup(256, 16, 32, 8, 256, 256, 256, 256, None)
+    assert rc == -1 and "1..256" in ftc.last_error()
+    # ftc_silu_mul_rows: [gate | up] rows need ld >= 2n; fp16 rows an even n
+    rc = lib.ftc_silu_mul_rows(256, 4, 100, 150, 256, None, None, None)
+    assert rc == -1 and "ld >= 2n" in ftc.last_error()
+    rc = lib.ftc_silu_mul_rows(256, 4, 101, 202, None, 256, 256, None)
+    assert rc == -1 and "even n" in ftc.last_error()
+    rc = lib.ftc_silu_mul_rows(256, 4, 100, 200, None, None, None, None)
+    assert rc == -1 and "null" in ftc.last_error()
+    # peer allreduce: bad group / size, missing buffer
+    h = (C.c_uint8 * 64)()
+    out = C.c_void_p()
+    rc = lib.ftc_peer_ar_create(2, 2, 1024, C.byref(out), h)
+    assert rc == -1 and "rank < world" in ftc.last_error()
+    rc = lib.ftc_peer_ar_create(0, 9, 1024, C.byref(out), h)
+    assert rc == -1 and "1..8 ranks" in ftc.last_error()
+    rc = lib.ftc_peer_ar_create(0, 2, 0, C.byref(out), h)
+    assert rc == -1 and "max_elems" in ftc.last_error()
+    assert lib.ftc_peer_ar_sum_f32(None, 256, 256, 16, None) == -1
+    assert lib.ftc_mul_mat_vec_allreduce(None, F.Q4_K, 256, 16, 256, 144, 256, 256, None) == -1
+    assert lib.ftc_peer_ar_max_elems(None) == 0
+    assert lib.ftc_peer_ar_destroy(None) == 0
