@@ -74,15 +74,16 @@ class OracleOps:
         return self.matmuls(torch.from_numpy(np.ascontiguousarray(h)), [w])[0]
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, dims=None):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        w = tp.full_weights(SMALL, seed=1)
-        blk = tp.TPBlock.build(SMALL, world, rank, OracleOps(), tp.shard(w, SMALL, world, rank))
-        x = torch.from_numpy(np.random.default_rng(0).standard_normal((3, SMALL["n_embd"]))
+        d = dims or SMALL
+        w = tp.full_weights(d, seed=1)
+        blk = tp.TPBlock.build(d, world, rank, OracleOps(), tp.shard(w, d, world, rank))
+        x = torch.from_numpy(np.random.default_rng(0).standard_normal((3, d["n_embd"]))
                              .astype(np.float32))
         out, (q, _, _) = blk.forward(x)
         np.save(os.path.join(out_dir, f"out{rank}.npy"), out.numpy())
@@ -114,4 +115,22 @@ def test_tp_two_ranks_match_unsharded(tmp_path, oracle):
     assert np.max(np.abs(o0 - ref)) <= 1e-5 * np.max(np.abs(ref))
     # column-parallel q slices are the unsharded q's halves, bit for bit
     q = np.concatenate([np.load(tmp_path / f"q{r}.npy") for r in range(2)], axis=1)
+    assert np.array_equal(q, qref.numpy())
+
+
+def test_tp_four_ranks_match_unsharded(tmp_path, oracle):
+    """Four gloo ranks on the MID block: row-parallel K slices of one (o) and
+    two (down) super-blocks, column slices of 256 / 64 / 512 rows."""
+    import torch.multiprocessing as mp
+    mp.start_processes(_rank_main, args=(4, _free_port(), str(tmp_path), MID), nprocs=4,
+                       start_method="spawn", join=True)
+    w = tp.full_weights(MID, seed=1)
+    ref_blk = tp.TPBlock.build(MID, 1, 0, OracleOps(), tp.shard(w, MID, 1, 0))
+    x = torch.from_numpy(np.random.default_rng(0).standard_normal((3, MID["n_embd"]))
+                         .astype(np.float32))
+    ref, (qref, _, _) = ref_blk.forward(x)
+    outs = [np.load(tmp_path / f"out{r}.npy") for r in range(4)]
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+    assert np.max(np.abs(outs[0] - ref.numpy())) <= 1e-5 * np.max(np.abs(ref.numpy()))
+    q = np.concatenate([np.load(tmp_path / f"q{r}.npy") for r in range(4)], axis=1)
     assert np.array_equal(q, qref.numpy())
