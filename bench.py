@@ -402,7 +402,12 @@ def time_tp(dev, world, rank, seed=0):
     shard_b = tp.weight_bytes(d) // world
     copies = min(4, max(1, -(-2 * L2_BYTES // shard_b)))
     # partials of up to TP_PEER_M tokens go through the NVLink peer allreduce
-    peer = ftc.PeerAllreduce(TP_PEER_M * d["n_embd"]) if world > 1 else None
+    peer, peer_note = None, None
+    if world > 1:
+        try:
+            peer = ftc.PeerAllreduce(TP_PEER_M * d["n_embd"])
+        except RuntimeError as e:  # raised on every rank alike: all fall back to NCCL
+            peer_note = f"peer allreduce unavailable, NCCL for every M ({e})"
     blocks = [tp.TPBlock.build(d, world, rank, ops, tp.rank_shards(d, world, rank, seed=seed + c),
                                peer=peer)
               for c in range(copies)]
@@ -458,6 +463,7 @@ def time_tp(dev, world, rank, seed=0):
             "scaling": "strong (the whole block's work is split over the GPUs)",
             "weight_bytes": tp.weight_bytes(d), "weight_copies_rotated": copies,
             "kernels": "M<=8: decode GEMV (fp32); M>8: tcgen05 GEMM on row-scaled fp16",
+            **({"note": peer_note} if peer_note else {}),
             "per_M": out}
 
 

@@ -546,18 +546,42 @@ class PeerAllreduce:
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.max_elems = int(max_elems)
+        self.torch = torch
+        self._ar = None
+        # Each step's outcome is shared before the next one, so that a rank
+        # whose allocation or mapping failed makes every rank raise the same
+        # error instead of leaving the others waiting in a later collective.
         h = (C.c_uint8 * IPC_HANDLE_BYTES)()
         ptr = _p()
-        check(lib().ftc_peer_ar_create(self.rank, self.world, self.max_elems, C.byref(ptr), h),
-              "ftc_peer_ar_create")
-        self._ar = ptr
+        err = None
+        try:
+            check(lib().ftc_peer_ar_create(self.rank, self.world, self.max_elems, C.byref(ptr), h),
+                  "ftc_peer_ar_create")
+            self._ar = ptr
+        except Exception as e:  # noqa: BLE001 - reported to every rank below
+            err = f"{type(e).__name__}: {e}"
         handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(h), group=group)
-        allh = (C.c_uint8 * (IPC_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
-        check(lib().ftc_peer_ar_open(self._ar, allh), "ftc_peer_ar_open")
-        # every rank has mapped every other rank's buffer before the first call
-        dist.barrier(group=group)
-        self.torch = torch
+        dist.all_gather_object(handles, (err, bytes(h)), group=group)
+        self._agree([e for e, _ in handles], "ftc_peer_ar_create")
+        allh = (C.c_uint8 * (IPC_HANDLE_BYTES * self.world)).from_buffer_copy(
+            b"".join(b for _, b in handles))
+        err = None
+        try:
+            check(lib().ftc_peer_ar_open(self._ar, allh), "ftc_peer_ar_open")
+        except Exception as e:  # noqa: BLE001
+            err = f"{type(e).__name__}: {e}"
+        errs = [None] * self.world
+        # also the barrier after which every rank has mapped every other
+        # rank's buffer, before the first call
+        dist.all_gather_object(errs, err, group=group)
+        self._agree(errs, "ftc_peer_ar_open")
+
+    def _agree(self, errs, step):
+        bad = [(r, e) for r, e in enumerate(errs) if e is not None]
+        if bad:
+            self.close()
+            raise RuntimeError(f"PeerAllreduce: {step} failed on rank(s) "
+                               + "; ".join(f"{r}: {e}" for r, e in bad))
 
     def fits(self, t):
         return t.dtype == self.torch.float32 and t.is_contiguous() and t.numel() <= self.max_elems
