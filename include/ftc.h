@@ -118,6 +118,18 @@ typedef struct ftc_expert_chunk_job {
  * Windows not inside a cached range are copied to the device per call. */
 int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* job);
 
+/* The engine's down projection, ft::matmul_down_axpy (ft/src/cpu_backend.cpp:
+ * 60-75; a free function the engine calls beside the interface, at
+ * ft/src/engine.cpp:256, 275), with host buffers:
+ *   y[m][j] += sum_i x[m][i] * W_i[j]      i < n_in, j < N
+ * W_i = row i of w_host (N weights, row_bytes(dtype, N) bytes per row; the
+ * reference's transposed "down" layout, n_in rows = neurons); rows with
+ * x[m][i] == 0 add nothing.  x: host fp32 [M][n_in]; y: host fp32 [M][N],
+ * accumulated.  The weight resolves through the HBM cache like
+ * ftc_backend_matmul's.  M == 0 or n_in == 0 changes nothing. */
+int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int64_t n_in,
+                                 const void* w_host, int dtype, int64_t N, float* y);
+
 /* ft::IBackend::sync (ft/include/ft/backend.h:39). */
 int ftc_backend_sync(ftc_backend* be);
 
@@ -198,6 +210,18 @@ int ftc_gemm_rowscaled(int dtype, const void* w, int64_t N, int64_t K, int64_t r
  * x_dtype (FTC_F32, FTC_BF16, FTC_F16); out: [rows][K] fp16; K even. */
 int ftc_rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
                     int32_t* row_exp, void* stream);
+
+/* ftc_backend_matmul_down_axpy on DEVICE buffers: y[m][j] += sum_i x[m][i] *
+ * W_i[j] (W: n_in rows of N weights, row_stride bytes apart; x fp32
+ * [M][n_in]; y fp32 [M][N], accumulated; zero activations skipped).  N must
+ * be a whole number of blocks.  ws: device scratch of at least
+ * ftc_matmul_down_axpy_workspace_bytes(dtype, n_in, N, M) bytes (NULL when
+ * that is 0); the partial sums of row slabs are added in a fixed order, so
+ * the result is the same on every run. */
+size_t ftc_matmul_down_axpy_workspace_bytes(int dtype, int64_t n_in, int64_t N, int64_t M);
+int ftc_matmul_down_axpy(int dtype, const void* w, int64_t n_in, int64_t N, int64_t row_stride,
+                         const float* x, int64_t M, float* y, void* ws, size_t ws_bytes,
+                         void* stream);
 
 /* h[i] = silu(g[i]) * u[i] = g / (1 + exp(-g)) * u in fp32, the expert FFN's
  * activation (ft/src/cpu_backend.cpp:127). */

@@ -423,6 +423,22 @@ int ftor_expert_chunk(const float* x, float* out, const uint8_t* gate, const uin
     return bctx.err ? -3 : 0;
 }
 
+/* ft/src/cpu_backend.cpp:60-75 (ft::matmul_down_axpy, the engine's dense
+ * and shared-expert down projection, ft/src/engine.cpp:256, 275):
+ * y[m][j] += x[m][i] * W_i[j] for i < n_in in ascending order, rows with
+ * x[m][i] == 0 skipped; W_i = row i of N weights.  Every y[m][j] sees the
+ * same sequence of separately rounded products and sums as the reference's
+ * single-threaded loop, so the column split over threads changes no bit. */
+int ftor_matmul_down_axpy(const float* x, int64_t M, int64_t n_in, const uint8_t* W, int dtype,
+                          int64_t N, int64_t row_stride, float* y, int threads) {
+    if (ftor_block_elems(dtype) <= 0) return -1;
+    if (M <= 0 || n_in <= 0 || N <= 0) return 0;
+    if (row_stride <= 0) row_stride = ftor_row_bytes(dtype, N);
+    struct ph_b_ctx c = {x, M, N, n_in, W, row_stride, dtype, y, 0};
+    parallel_for(N, threads, phase_b, &c);
+    return c.err ? -3 : 0;
+}
+
 /* Standard GGUF layout for the down projection (ffn_down rows = outputs):
  * out[m][o] += dot(h_m, down_o) over n_ff.  Phase A is the reference's
  * (cpu_backend.cpp:115-130); phase B is its matmul (cpu_backend.cpp:90-104)

@@ -25,6 +25,8 @@ int ftor_matmul(const float* x, int64_t M, int64_t K, const uint8_t* W, int dtyp
 int ftor_expert_chunk(const float* x, float* out, const uint8_t* gate, const uint8_t* up,
                       const uint8_t* down, int dtype, int64_t M, int64_t K, int64_t IC,
                       int64_t gu_stride, int64_t dn_stride, int threads);
+int ftor_matmul_down_axpy(const float* x, int64_t M, int64_t n_in, const uint8_t* W, int dtype,
+                          int64_t N, int64_t row_stride, float* y, int threads);
 int ftor_expert_ffn(const float* x, float* out, const uint8_t* gate, const uint8_t* up,
                     const uint8_t* down, int dtype, int64_t M, int64_t K, int64_t n_ff,
                     int64_t gu_stride, int64_t dn_stride, int threads);

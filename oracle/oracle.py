@@ -55,6 +55,8 @@ def lib():
                                            _i64, _i64, C.c_int]
         _lib.ftor_expert_ffn.argtypes = [_p, _p, _p, _p, _p, C.c_int, _i64, _i64, _i64,
                                          _i64, _i64, C.c_int]
+        _lib.ftor_matmul_down_axpy.argtypes = [_p, _i64, _i64, _p, C.c_int, _i64, _i64, _p,
+                                               C.c_int]
         _lib.ftor_route_topk.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p]
         _lib.ftor_moe_ffn.argtypes = [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
                                       C.c_int, _p, C.c_int]
@@ -82,6 +84,7 @@ def ref():
         r.ftref_matmul.argtypes = [_p, _i64, _i64, _p, C.c_uint32, _i64, _p, C.c_int]
         r.ftref_run_expert_chunk.argtypes = [_p, _p, _p, _p, _p, C.c_uint32, _i64, _i64, _i64,
                                              C.c_size_t, C.c_size_t, C.c_int]
+        r.ftref_matmul_down_axpy.argtypes = [_p, _i64, _i64, _p, C.c_uint32, _i64, _p]
         _ref = r
     return _ref
 
@@ -138,6 +141,18 @@ def expert_chunk(x, out, gate, up, down, dtype, k, ic, threads=1):
                                    m, k, ic, gate.shape[1], down.shape[1], threads),
            "ftor_expert_chunk")
     return out
+
+
+def matmul_down_axpy(x, w, dtype, n, y, threads=1):
+    """``y[m] += x_m . W`` with W = ``w`` ``[n_in, row_bytes(n)]`` (n_in rows of
+    ``n`` weights, the reference's transposed down convention); x fp32
+    ``[m, n_in]``, ``y`` fp32 ``[m, n]`` accumulated in place."""
+    w = _c(w, np.uint8)
+    x = _c(x, np.float32).reshape(-1, w.shape[0])
+    assert y.dtype == np.float32 and y.flags.c_contiguous and y.shape == (x.shape[0], n)
+    _check(lib().ftor_matmul_down_axpy(_ptr(x), x.shape[0], w.shape[0], _ptr(w), dtype, n,
+                                       w.shape[1], _ptr(y), threads), "ftor_matmul_down_axpy")
+    return y
 
 
 def expert_ffn(x, out, gate, up, down, dtype, k, n_ff, threads=1):
@@ -210,3 +225,13 @@ def ref_expert_chunk(x, out, gate, up, down, dtype, k, ic, threads=1):
                                         dtype, x.shape[0], k, ic, gate.shape[1], down.shape[1],
                                         threads), "ftref_run_expert_chunk")
     return out
+
+
+def ref_matmul_down_axpy(x, w, dtype, n, y):
+    """The reference's own ft::matmul_down_axpy; ``y`` accumulated in place."""
+    w = _c(w, np.uint8)
+    x = _c(x, np.float32).reshape(-1, w.shape[0])
+    assert y.dtype == np.float32 and y.flags.c_contiguous and y.shape == (x.shape[0], n)
+    _check(ref().ftref_matmul_down_axpy(_ptr(x), x.shape[0], w.shape[0], _ptr(w), dtype, n,
+                                        _ptr(y)), "ftref_matmul_down_axpy")
+    return y

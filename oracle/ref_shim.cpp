@@ -70,4 +70,14 @@ int ftref_run_expert_chunk(const float* x, float* out, const void* gate, const v
     } catch (const std::exception&) { return -1; }
 }
 
+// ft::matmul_down_axpy (ft/src/cpu_backend.cpp:60-75): y[m] += x_m . W over
+// n_in rows of N weights each.
+int ftref_matmul_down_axpy(const float* x, int64_t M, int64_t n_in, const void* W, uint32_t dtype,
+                           int64_t N, float* y) {
+    try {
+        matmul_down_axpy(x, M, n_in, view(W, dtype, N, n_in), y);
+        return 0;
+    } catch (const std::exception&) { return -1; }
+}
+
 }  // extern "C"

@@ -120,6 +120,58 @@ static void test_expert_chunk_windows(CudaBackend& be) {
     CHECK(maxerr < 1e-4, "chunked expert equivalence (reference test bound)");
 }
 
+// The engine's FFN down projection (ft/src/engine.cpp:256, 275) in both
+// layouts: neuron-major through matmul_down_axpy (checked against the
+// reference's loop, ftor_matmul_down_axpy), output-major through matmul.
+static void test_down_project(CudaBackend& be, DType t, int64_t n_ff, int64_t n_embd, int64_t M) {
+    std::vector<float> h((size_t)(M * n_ff));
+    for (size_t i = 0; i < h.size(); ++i) h[i] = (i % 5 == 0) ? 0.f : rnd();
+    std::vector<float> y0((size_t)(M * n_embd));
+    for (auto& v : y0) v = rnd();
+    char msg[128];
+    {  // neuron-major: n_ff rows of n_embd weights
+        auto w = random_blocks(t, n_ff, n_embd);
+        HostTensor W = view(w, t, n_embd, n_ff);
+        std::vector<float> y = y0, ref = y0;
+        be.down_project(h.data(), M, n_ff, W, y.data());
+        ftor_matmul_down_axpy(h.data(), M, n_ff, w.data(), (int)t, n_embd,
+                              (int64_t)W.row_stride_bytes(), ref.data(), 8);
+        std::snprintf(msg, sizeof msg, "down_project neuron rows dtype %u n_ff %lld M %lld",
+                      (unsigned)t, (long long)n_ff, (long long)M);
+        CHECK(rel_err(y, ref) <= 2e-3, msg);
+    }
+    if (n_ff != n_embd) {  // output-major: n_embd rows of n_ff weights
+        auto w = random_blocks(t, n_embd, n_ff);
+        HostTensor W = view(w, t, n_ff, n_embd);
+        std::vector<float> y = y0, ref((size_t)(M * n_embd));
+        be.down_project(h.data(), M, n_ff, W, y.data());
+        ftor_matmul(h.data(), M, n_ff, w.data(), (int)t, n_embd, (int64_t)W.row_stride_bytes(),
+                    ref.data(), 8);
+        for (size_t i = 0; i < ref.size(); ++i) ref[i] += y0[i];
+        std::snprintf(msg, sizeof msg, "down_project output rows dtype %u n_ff %lld M %lld",
+                      (unsigned)t, (long long)n_ff, (long long)M);
+        CHECK(rel_err(y, ref) <= 2e-3, msg);
+    }
+}
+
+// Host-only checks (no device): the down-weight layout by shape.
+static void test_down_layout() {
+    std::vector<uint8_t> b(16);
+    HostTensor a = view(b, DType::Q4_K, 4096, 14336);   // n_ff rows
+    HostTensor o = view(b, DType::Q4_K, 14336, 4096);   // n_ff columns
+    HostTensor sq = view(b, DType::Q4_K, 4096, 4096);
+    CHECK(down_layout(a, 14336) == DownLayout::NeuronRows, "n_ff rows -> neuron rows");
+    CHECK(down_layout(o, 14336) == DownLayout::OutputRows, "n_ff columns -> output rows");
+    CHECK(down_layout(sq, 4096) == DownLayout::NeuronRows, "square -> the reference's layout");
+    bool threw = false;
+    try {
+        down_layout(a, 1000);
+    } catch (const std::runtime_error&) {
+        threw = true;
+    }
+    CHECK(threw, "no n_ff dimension throws");
+}
+
 static void test_upload_and_errors(CudaBackend& be) {
     auto w = random_blocks(DType::Q4_K, 256, 4096);
     HostTensor W = view(w, DType::Q4_K, 4096, 256);
@@ -136,7 +188,13 @@ static void test_upload_and_errors(CudaBackend& be) {
     be.sync();
 }
 
-int main() {
+int main(int argc, char** argv) {
+    test_down_layout();
+    if (argc > 1 && std::strcmp(argv[1], "--host-only") == 0) {
+        if (g_fails) return 1;
+        std::printf("all tests passed\n");
+        return 0;
+    }
     try {
         CudaBackend be(0);
         CHECK(be.ready(), "backend ready");
@@ -147,6 +205,10 @@ int main() {
         test_matmul(be, DType::Q8_0, 256, 4096, 1);
         test_matmul(be, DType::Q6_K, 300, 4096, 2);
         test_expert_chunk_windows(be);
+        test_down_project(be, DType::Q4_K, 14336, 4096, 1);
+        test_down_project(be, DType::Q4_K, 1024, 512, 3);
+        test_down_project(be, DType::Q8_0, 96, 4096, 9);
+        test_down_project(be, DType::Q6_K, 512, 512, 2);
         test_upload_and_errors(be);
     } catch (const std::exception& e) {
         std::printf("FAIL exception: %s\n", e.what());

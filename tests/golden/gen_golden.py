@@ -20,6 +20,10 @@ Fixtures (all small, numpy .npz):
   run window by window through CpuBackend::run_expert_chunk.
 * ref_expert_q8_0.npz -- one Q8_0 expert chunk through run_expert_chunk.
 * ref_dequant_formats.npz -- F16/BF16/Q4_0/Q4_1 rows through dequant_row.
+* ref_down_axpy.npz -- the engine's down projection ft::matmul_down_axpy
+  (ft/src/cpu_backend.cpp:60-75) on Q8_0, F16 and Q4_0 rows in the
+  reference's transposed layout, activations with zeros (the skipped rows)
+  and a non-zero starting y.
 * gguf_kquant.npz -- Q4_K/Q6_K blocks (random and edge cases) with the
   dequantized values from the GGUF format's Python package (gguf-py); the
   reference has no K-quant decoder, so this is the only external pin.
@@ -162,6 +166,30 @@ def gen_formats():
     save("ref_dequant_formats.npz", **arrays)
 
 
+def gen_down_axpy():
+    arrays = {}
+    for t, name, n_in, n in ((F.Q8_0, "q8_0", 96, 256), (F.F16, "f16", 40, 64),
+                             (F.Q4_0, "q4_0", 72, 96)):
+        if t == F.F16:
+            vals = S.rng(0, "golden.axpy.f16").standard_normal(size=(n_in, n)).astype(np.float32)
+            w = vals.astype(np.float16).view(np.uint8)
+        elif t == F.Q4_0:
+            g = S.rng(0, "golden.axpy.q4_0")
+            w = g.integers(0, 256, size=(n_in, (n // 32) * 18), dtype=np.uint8)
+            for b in range(n // 32):  # sane fp16 scales
+                w[:, b * 18:b * 18 + 2] = np.array([0x2E66], dtype=np.uint16).view(np.uint8)
+        else:
+            w = S.weight(t, n_in, n, seed=0, name="golden.axpy." + name)
+        x = S.activations_f32(3, n_in, seed=0, name="golden.axpy.x." + name)
+        x[:, ::7] = 0.0       # rows the reference skips
+        x[1, 5] = -0.0
+        y0 = S.activations_f32(3, n, seed=1, name="golden.axpy.y." + name)
+        y = y0.copy()
+        O.ref_matmul_down_axpy(x, w, t, n, y)
+        arrays.update({name + "_w": w, name + "_x": x, name + "_y0": y0, name + "_y": y})
+    save("ref_down_axpy.npz", **arrays)
+
+
 def kquant_edge_blocks(t):
     """Hand-made edge blocks: zero / subnormal / negative / largest scales."""
     bb = F.BLOCK[t][1]
@@ -229,9 +257,9 @@ def gen_kquant():
 if __name__ == "__main__":
     if not O.have_ref():
         sys.exit("oracle/_ref/libftref.so missing: run make -C oracle where the reference exists")
-    gen_q8_0_gemv()
-    gen_test_quant()
-    gen_chunker()
-    gen_expert_q8_0()
-    gen_formats()
-    gen_kquant()
+    gens = {"q8_0_gemv": gen_q8_0_gemv, "test_quant": gen_test_quant, "chunker": gen_chunker,
+            "expert_q8_0": gen_expert_q8_0, "formats": gen_formats, "kquant": gen_kquant,
+            "down_axpy": gen_down_axpy}
+    # `gen_golden.py name ...` regenerates only the named fixtures
+    for key in sys.argv[1:] or list(gens):
+        gens[key]()

@@ -59,6 +59,28 @@ def test_kernel_entry_points_validate_before_launch(lib):
     assert rc == -1
 
 
+def test_down_axpy_validates_before_launch(lib):
+    rb = F.row_bytes(F.Q4_K, 4096)
+    ws = lib.ftc_matmul_down_axpy_workspace_bytes
+    # a Llama-sized down projection at one token splits the rows into slabs
+    assert ws(F.Q4_K, 14336, 4096, 1) > 0
+    assert ws(F.Q4_K, 14336, 4096, 0) == 0 and ws(7, 14336, 4096, 1) == 0
+    assert ws(F.Q4_K, 4, 4096, 1) == 0  # one slab: sums go straight into y
+    call = lib.ftc_matmul_down_axpy
+    assert call(F.Q4_K, 16, 14336, 4096, rb, 16, 1, 16, None, 0, None) == -1
+    assert "workspace" in ftc.last_error()
+    assert call(F.Q4_K, 16, 64, 4000, rb, 16, 1, 16, None, 0, None) == -1
+    assert "whole number of blocks" in ftc.last_error()
+    assert call(F.Q4_K, 16, 64, 4096, rb - 1, 16, 1, 16, None, 0, None) == -1
+    assert "row_stride" in ftc.last_error()
+    assert call(F.Q4_K, None, 64, 4096, rb, 16, 1, 16, None, 0, None) == -1
+    assert "null" in ftc.last_error()
+    assert call(7, 16, 64, 4096, rb, 16, 1, 16, None, 0, None) == -2
+    # nothing to add: no pointer is touched, no launch
+    assert call(F.Q4_K, None, 64, 4096, rb, None, 0, None, None, 0, None) == 0
+    assert call(F.Q4_K, None, 0, 4096, rb, None, 3, None, None, 0, None) == 0
+
+
 def _moe_desc(**kw):
     rs, rd = F.row_bytes(F.Q4_K, 1024), F.row_bytes(F.Q4_K, 2048)
     v = dict(dtype=F.Q4_K, n_experts=8, top_k=2, n_embd=1024, n_ff=2048, gate_exps=256,

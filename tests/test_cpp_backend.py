@@ -33,6 +33,13 @@ def test_adapter_compiles(tmp_path):
     assert os.path.exists(compile_test(str(tmp_path / "test_cuda_backend")))
 
 
+def test_adapter_host_checks(tmp_path):
+    """The parts of the adapter that need no device (the down-weight layout)."""
+    exe = compile_test(str(tmp_path / "test_cuda_backend"))
+    r = subprocess.run([exe, "--host-only"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and "all tests passed" in r.stdout, r.stdout + r.stderr
+
+
 @pytest.mark.gpu
 def test_adapter_passes_on_gpu(tmp_path):
     exe = compile_test(str(tmp_path / "test_cuda_backend"))

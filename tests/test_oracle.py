@@ -97,6 +97,35 @@ def test_expert_chunk_q8_0_matches_reference(golden, oracle):
     assert np.array_equal(bits(out), bits(g["out"]))
 
 
+@pytest.mark.parametrize("name,t", [("q8_0", F.Q8_0), ("f16", F.F16), ("q4_0", F.Q4_0)])
+def test_down_axpy_matches_reference(golden, oracle, name, t):
+    """ft::matmul_down_axpy (transposed down rows, zero activations skipped,
+    y accumulated) bit for bit, split over threads."""
+    g = golden("ref_down_axpy.npz")
+    y = g[name + "_y0"].copy()
+    oracle.matmul_down_axpy(g[name + "_x"], g[name + "_w"], t, y.shape[1], y, threads=3)
+    assert np.array_equal(bits(y), bits(g[name + "_y"]))
+
+
+@pytest.mark.parametrize("t", [F.Q4_K, F.Q6_K])
+def test_down_axpy_kquant_is_the_row_walk(oracle, t):
+    """For the K-quants (no reference decoder) the oracle's down projection is
+    the reference's loop over dequantized rows, restated in numpy."""
+    n_in, n = 24, 512
+    w = S.weight(t, n_in, n, seed=5, name="axpy.kq")
+    x = S.activations_f32(2, n_in, seed=5, name="axpy.kq.x")
+    x[0, 3] = 0.0
+    y0 = S.activations_f32(2, n, seed=6, name="axpy.kq.y")
+    deq = oracle.dequant_rows(w, t, n)
+    ref = y0.copy()
+    for i in range(n_in):
+        for m in range(2):
+            if x[m, i] != 0:
+                ref[m] = ref[m] + x[m, i] * deq[i]
+    got = oracle.matmul_down_axpy(x, w, t, n, y0.copy(), threads=2)
+    assert np.array_equal(bits(got), bits(ref))
+
+
 @pytest.mark.parametrize("name,t", [("f16", F.F16), ("bf16", F.BF16), ("q4_0", F.Q4_0),
                                     ("q4_1", F.Q4_1)])
 def test_other_formats_match_reference(golden, oracle, name, t):

@@ -75,6 +75,9 @@ int ep_pack(const void* x, int x_dtype, int64_t T, int64_t n_embd, const int32_t
 int ep_regroup(const int32_t* recv_counts, int64_t world, int64_t n_local, int64_t cap,
                int32_t* perm, int32_t* inv, int32_t* counts, int32_t* offsets, cudaStream_t st);
 int silu_mul(const float* g, const float* u, int64_t n, float* h, cudaStream_t st);
+size_t down_axpy_workspace_bytes(int dtype, int64_t n_in, int64_t N, int64_t M);
+int down_axpy(int dtype, const void* w, int64_t n_in, int64_t N, int64_t row_stride,
+              const float* x, int64_t M, float* y, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t moe_workspace_bytes(const ftc_moe_desc* d, int64_t T);
 size_t moe_experts_workspace_bytes(const ftc_moe_desc* d, int64_t rows);
 int moe_route_only(const float* logits, int64_t T, int64_t E, int64_t U, int32_t* idx, float* w,
@@ -397,6 +400,42 @@ int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* jo
     return ok();
 }
 
+int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int64_t n_in,
+                                 const void* w_host, int dtype, int64_t N, float* y) {
+    int rc = bind(be);
+    if (rc) return rc;
+    const Fmt f = fmt_of(dtype);
+    FTC_REQUIRE(f.block_elems > 0, FTC_E_UNSUPPORTED, "ftc_backend_matmul_down_axpy: unknown dtype");
+    FTC_REQUIRE(M >= 0 && n_in >= 0 && N > 0 && N % f.block_elems == 0, FTC_E_INVALID,
+                "ftc_backend_matmul_down_axpy: bad shape (N must be whole blocks)");
+    if (M == 0 || n_in == 0) return ok();  // the reference's loops do nothing
+    FTC_REQUIRE(x && w_host && y, FTC_E_INVALID, "ftc_backend_matmul_down_axpy: null pointer");
+    if (inject_fail("ftc_backend_matmul_down_axpy"))
+        return set_error(FTC_E_INJECTED, "ftc_backend_matmul_down_axpy: injected failure");
+    std::lock_guard<std::mutex> lk(be->mu);
+    const int64_t stride = row_bytes(dtype, N);
+    const void* dW = nullptr;
+    if ((rc = be->resolve(w_host, (size_t)(stride * n_in), &dW))) return rc;
+    const size_t xb = (size_t)(M * n_in) * 4, yb = (size_t)(M * N) * 4;
+    const size_t xo = (xb + 255) & ~(size_t)255;
+    const size_t wsb = down_axpy_workspace_bytes(dtype, n_in, N, M);
+    if ((rc = be->pin_in.ensure(xo + yb)) || (rc = be->pin_out.ensure(yb)) ||
+        (rc = be->dx.ensure(xo + yb)) || (rc = be->dtmp.ensure(wsb ? wsb : 1)))
+        return rc;
+    std::memcpy(be->pin_in.p, x, xb);
+    std::memcpy(static_cast<uint8_t*>(be->pin_in.p) + xo, y, yb);
+    FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, xo + yb, cudaMemcpyHostToDevice, be->stream));
+    const float* dx = static_cast<const float*>(be->dx.p);
+    float* dy = reinterpret_cast<float*>(static_cast<uint8_t*>(be->dx.p) + xo);
+    if ((rc = down_axpy(dtype, dW, n_in, N, stride, dx, M, dy, be->dtmp.p, be->dtmp.cap,
+                        be->stream)))
+        return rc;
+    FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, be->stream));
+    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    std::memcpy(y, be->pin_out.p, yb);
+    return ok();
+}
+
 int ftc_backend_sync(ftc_backend* be) {
     int rc = bind(be);
     if (rc) return rc;
@@ -465,6 +504,17 @@ int ftc_gemm_rowscaled(int dtype, const void* w, int64_t N, int64_t K, int64_t r
 int ftc_rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
                     int32_t* row_exp, void* stream) {
     int rc = rows_to_f16(x, x_dtype, rows, K, ld, out, row_exp, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+size_t ftc_matmul_down_axpy_workspace_bytes(int dtype, int64_t n_in, int64_t N, int64_t M) {
+    return down_axpy_workspace_bytes(dtype, n_in, N, M);
+}
+
+int ftc_matmul_down_axpy(int dtype, const void* w, int64_t n_in, int64_t N, int64_t row_stride,
+                         const float* x, int64_t M, float* y, void* ws, size_t ws_bytes,
+                         void* stream) {
+    int rc = down_axpy(dtype, w, n_in, N, row_stride, x, M, y, ws, ws_bytes, (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

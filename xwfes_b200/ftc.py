@@ -30,6 +30,10 @@ SIGNATURES = {
     "ftc_backend_cached_bytes": (C.c_int, [_p, C.POINTER(C.c_uint64)]),
     "ftc_backend_matmul": (C.c_int, [_p, _p, _i64, _i64, _p, C.c_int, _i64, _p]),
     "ftc_backend_run_expert_chunk": (C.c_int, [_p, _p]),
+    "ftc_backend_matmul_down_axpy": (C.c_int, [_p, _p, _i64, _i64, _p, C.c_int, _i64, _p]),
+    "ftc_matmul_down_axpy_workspace_bytes": (C.c_size_t, [C.c_int, _i64, _i64, _i64]),
+    "ftc_matmul_down_axpy": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p,
+                                       C.c_size_t, _p]),
     "ftc_backend_sync": (C.c_int, [_p]),
     "ftc_backend_stream": (_p, [_p]),
     "ftc_backend_device_ptr": (_p, [_p, _p]),
@@ -151,6 +155,26 @@ def mul_mat_vec(w, dtype, n, k, x, y=None, row_stride=None, stream=None):
     rs = row_stride if row_stride is not None else row_bytes(t, k)
     check(lib().ftc_mul_mat_vec(t, w.data_ptr(), n, k, rs, x2.data_ptr(), m, y.data_ptr(),
                                 _stream(stream)), "ftc_mul_mat_vec")
+    return y
+
+
+def matmul_down_axpy(w, dtype, n_in, n, x, y, row_stride=None, ws=None, stream=None):
+    """y[m][j] += sum_i x[m][i] W_i[j] on the GPU (ftc_matmul_down_axpy): ``w``
+    uint8 CUDA tensor of ``n_in`` rows of ``n`` weights (the reference's
+    transposed down layout), ``x`` fp32 [M, n_in], ``y`` fp32 [M, n]
+    accumulated in place.  ``ws``: scratch (allocated when None)."""
+    import torch
+    t = F.dtype_id(dtype)
+    x2 = x.reshape(-1, n_in)
+    m = x2.shape[0]
+    need = lib().ftc_matmul_down_axpy_workspace_bytes(t, n_in, n, m)
+    if ws is None and need:
+        ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+    rs = row_stride if row_stride is not None else row_bytes(t, n)
+    check(lib().ftc_matmul_down_axpy(t, w.data_ptr(), n_in, n, rs, x2.data_ptr(), m, y.data_ptr(),
+                                     ws.data_ptr() if ws is not None else None,
+                                     ws.numel() if ws is not None else 0, _stream(stream)),
+          "ftc_matmul_down_axpy")
     return y
 
 
@@ -518,6 +542,19 @@ class CudaBackend:
         self._keep[W.ptr()] = W
         check(lib().ftc_backend_matmul(self._h, x.ctypes.data, M, K, W.ptr(), W.dtype,
                                        W.rows(), y.ctypes.data), "ftc_backend_matmul")
+
+    def matmul_down_axpy(self, x, M, n_in, W, y):
+        """ft::matmul_down_axpy: y[m] += x_m . W over the first ``n_in`` rows of
+        W (``W.cols()`` weights each); x fp32 [M][n_in], y fp32 [M][W.cols()]
+        host arrays, y accumulated."""
+        assert x.dtype == np.float32 and x.flags.c_contiguous and x.size >= M * n_in
+        assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * W.cols()
+        if n_in > W.rows():
+            raise ValueError("matmul_down_axpy: n_in exceeds W.rows()")
+        self._keep[W.ptr()] = W
+        check(lib().ftc_backend_matmul_down_axpy(self._h, x.ctypes.data, M, n_in, W.ptr(),
+                                                 W.dtype, W.cols(), y.ctypes.data),
+              "ftc_backend_matmul_down_axpy")
 
     def run_expert_chunk(self, x, out, gate, up, down, dtype, M, K, IC, gu_stride, dn_stride):
         """IBackend::run_expert_chunk with host addresses (ints) for the

@@ -3,6 +3,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "ftc.h"
 
@@ -17,6 +18,13 @@ void check(int rc, const char* what) {
 }
 
 }  // namespace
+
+DownLayout down_layout(const HostTensor& W, int64_t n_ff) {
+    if (W.rows() == n_ff) return DownLayout::NeuronRows;
+    if (W.cols() == n_ff) return DownLayout::OutputRows;
+    throw std::runtime_error("cuda backend: down weight " + W.name + " has no dimension of n_ff = " +
+                             std::to_string(n_ff));
+}
 
 CudaBackend::CudaBackend(int device) {
     check(ftc_backend_create(device, &be_), "create");
@@ -53,6 +61,24 @@ void CudaBackend::run_expert_chunk(const ExpertChunkJob& job) {
 }
 
 void CudaBackend::sync() { check(ftc_backend_sync(be_), "sync"); }
+
+void CudaBackend::matmul_down_axpy(const float* x, int64_t M, int64_t n_in, const HostTensor& W,
+                                   float* y) {
+    if (n_in > W.rows()) throw std::runtime_error("cuda backend: matmul_down_axpy n_in > W.rows()");
+    check(ftc_backend_matmul_down_axpy(be_, x, M, n_in, W.data, (int)W.dtype, W.cols(), y),
+          "matmul_down_axpy");
+}
+
+void CudaBackend::down_project(const float* h, int64_t M, int64_t n_ff, const HostTensor& W,
+                               float* y) {
+    if (down_layout(W, n_ff) == DownLayout::NeuronRows) {
+        matmul_down_axpy(h, M, n_ff, W, y);
+        return;
+    }
+    std::vector<float> t((size_t)(M * W.rows()));
+    matmul(h, M, n_ff, W, t.data());
+    for (size_t i = 0; i < t.size(); ++i) y[i] += t[i];
+}
 
 void CudaBackend::upload(const HostTensor& t) {
     const size_t n = t.nbytes ? t.nbytes

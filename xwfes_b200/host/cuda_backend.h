@@ -16,6 +16,19 @@ struct ftc_backend;
 
 namespace ft {
 
+// The two layouts an FFN down-projection weight comes in.  The reference's
+// engine and test files store it neuron-major, n_ff rows of n_embd weights,
+// and multiply with ft::matmul_down_axpy (ft/src/cpu_backend.cpp:60-75;
+// ft/src/tests/test_core.cpp:164 writes ffn_down_exps with ne = (D, FF, E));
+// standard GGUF files store it output-major, n_embd rows of n_ff weights,
+// the layout every other projection has.
+enum class DownLayout { NeuronRows, OutputRows };
+
+// The layout of W by its shape: n_ff rows -> NeuronRows (also when W is
+// square: the reference's convention); n_ff columns -> OutputRows.  Throws
+// std::runtime_error when neither dimension is n_ff.
+DownLayout down_layout(const HostTensor& W, int64_t n_ff);
+
 class CudaBackend : public IBackend {
 public:
     explicit CudaBackend(int device = 0);
@@ -35,6 +48,19 @@ public:
     // the streamer passes mmap pointers straight through.
     void* alloc_staging(size_t) override { return nullptr; }
     void sync() override;
+
+    // ft::matmul_down_axpy on the GPU: y[m] += x_m . W over the first n_in
+    // rows of W (W.cols() weights each; zero activations skipped); x host fp32
+    // [M][n_in], y host fp32 [M][W.cols()] accumulated.  Replaces the free
+    // function the engine calls beside the interface (ft/src/engine.cpp:256,
+    // 275).  Throws when n_in exceeds W.rows().
+    void matmul_down_axpy(const float* x, int64_t M, int64_t n_in, const HostTensor& W, float* y);
+
+    // The engine's FFN down projection in either layout: y[m] += h_m . down,
+    // h host fp32 [M][n_ff], y host fp32 [M][n_embd] accumulated.  NeuronRows
+    // weights go through matmul_down_axpy, OutputRows weights through matmul
+    // (the dequant GEMV / GEMM of every other projection).
+    void down_project(const float* h, int64_t M, int64_t n_ff, const HostTensor& W, float* y);
 
     // Load a tensor's blocks into HBM once (call at Engine::load time).
     void upload(const HostTensor& t);
