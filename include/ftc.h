@@ -92,7 +92,9 @@ int ftc_backend_cached_bytes(ftc_backend* be, uint64_t* bytes);
  * Uploads W on first use if no cached range covers it.  Returns with y
  * written.  Unlike the reference's CpuBackend::matmul
  * (ft/src/cpu_backend.cpp:90-104), which folds all M rows into y[n], every
- * row m gets its own output row. */
+ * row m gets its own output row.  Q4_K with M > 8 runs on the tensor cores
+ * (ftc_rows_to_f16 + ftc_gemm_rowscaled: fp16 operands, fp32 accumulation);
+ * everything else on the fp32 GEMV, 8 rows per pass over the weight. */
 int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K,
                        const void* w_host, int dtype, int64_t N, float* y);
 

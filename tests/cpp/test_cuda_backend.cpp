@@ -204,6 +204,9 @@ int main(int argc, char** argv) {
         test_matmul(be, DType::Q4_K, 1024, 14336, 3);
         test_matmul(be, DType::Q8_0, 256, 4096, 1);
         test_matmul(be, DType::Q6_K, 300, 4096, 2);
+        test_matmul(be, DType::Q4_K, 1024, 4096, 9);     // tensor-core path from 9 rows
+        test_matmul(be, DType::Q4_K, 4096, 14336, 128);  // a prefill chunk
+        test_matmul(be, DType::Q8_0, 512, 4096, 20);     // GEMV, 8 rows per pass
         test_expert_chunk_windows(be);
         test_down_project(be, DType::Q4_K, 14336, 4096, 1);
         test_down_project(be, DType::Q4_K, 1024, 512, 3);

@@ -40,7 +40,7 @@ def test_matmul_q4_k_host_buffers(be, oracle):
     from xwfes_b200 import ftc
     n = k = 4096
     W = ftc.HostTensor(S.weight(F.Q4_K, n, k, seed=0, name="be"), F.Q4_K, (k, n))
-    for m in (1, 3, 8, 11):
+    for m in (1, 3, 8, 11, 64, 257):  # from 9 rows: the tensor-core GEMM
         x = S.activations_f32(m, k, seed=m)
         y = np.full((m, n), np.nan, dtype=np.float32)
         be.matmul(x, m, k, W, y)

@@ -318,14 +318,30 @@ int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K, co
     if ((rc = be->pin_in.ensure(xb)) || (rc = be->pin_out.ensure(yb)) || (rc = be->dx.ensure(xb)) ||
         (rc = be->dy.ensure(yb)))
         return rc;
+    // Q4_K beyond 8 rows (prefill, speculative verify): the tensor-core GEMM
+    // on fp16 rows with power-of-two row scales, one pass over the weight;
+    // otherwise the fp32 GEMV, 8 rows per pass.
+    const bool tc = dtype == FTC_Q4_K && M > 8 && M <= INT32_MAX && N <= INT32_MAX &&
+                    (uintptr_t)dW % 16 == 0 && stride % 16 == 0;
+    const size_t x16b = tc ? ((size_t)(M * K) * 2 + 255) & ~(size_t)255 : 0;
+    if (tc && (rc = be->dtmp.ensure(x16b + (size_t)M * 4))) return rc;
     std::memcpy(be->pin_in.p, x, xb);
     FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, xb, cudaMemcpyHostToDevice, be->stream));
     const float* dx = static_cast<const float*>(be->dx.p);
     float* dy = static_cast<float*>(be->dy.p);
-    for (int64_t m0 = 0; m0 < M; m0 += 8) {
-        const int64_t mc = M - m0 < 8 ? M - m0 : 8;
-        if ((rc = mul_mat_vec(dtype, dW, N, K, stride, dx + m0 * K, mc, dy + m0 * N, be->stream)))
+    if (tc) {
+        void* x16 = be->dtmp.p;
+        int32_t* row_exp = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(be->dtmp.p) + x16b);
+        if ((rc = rows_to_f16(dx, FTC_F32, M, K, K, x16, row_exp, be->stream)) ||
+            (rc = gemm_q4k_rowscaled(dW, N, K, stride, x16, M, dy, FTC_F32, row_exp, be->stream)))
             return rc;
+    } else {
+        for (int64_t m0 = 0; m0 < M; m0 += 8) {
+            const int64_t mc = M - m0 < 8 ? M - m0 : 8;
+            if ((rc = mul_mat_vec(dtype, dW, N, K, stride, dx + m0 * K, mc, dy + m0 * N,
+                                  be->stream)))
+                return rc;
+        }
     }
     FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, be->stream));
     FTC_CUDA(cudaStreamSynchronize(be->stream));
