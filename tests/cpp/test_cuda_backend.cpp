@@ -59,6 +59,16 @@ static HostTensor view(const std::vector<uint8_t>& b, DType t, int64_t cols, int
     return h;
 }
 
+// max |a-b| / max |b|: the tensor-core path's bound (fp16 operands)
+static double norm_err(const std::vector<float>& a, const std::vector<float>& b) {
+    double d = 0, r = 0;
+    for (size_t i = 0; i < b.size(); ++i) {
+        d = std::fmax(d, std::fabs((double)a[i] - b[i]));
+        r = std::fmax(r, std::fabs((double)b[i]));
+    }
+    return d / r;
+}
+
 // max |a-b| / (|b| + 1e-2 * rms(b))
 static double rel_err(const std::vector<float>& a, const std::vector<float>& b) {
     double ss = 0;
@@ -81,7 +91,9 @@ static void test_matmul(CudaBackend& be, DType t, int64_t N, int64_t K, int64_t 
     char msg[96];
     std::snprintf(msg, sizeof msg, "matmul dtype %u N %lld K %lld M %lld", (unsigned)t,
                   (long long)N, (long long)K, (long long)M);
-    CHECK(rel_err(y, ref) <= 2e-3, msg);
+    // Q4_K beyond 8 rows runs on the tensor cores (fp16 operands)
+    const bool tc = t == DType::Q4_K && M > 8;
+    CHECK((tc ? norm_err(y, ref) : rel_err(y, ref)) <= 2e-3, msg);
 }
 
 // The reference chunker test's shapes (ft/src/tests/test_core.cpp:307-346):
@@ -190,13 +202,29 @@ static void test_upload_and_errors(CudaBackend& be) {
 
 int main(int argc, char** argv) {
     test_down_layout();
-    if (argc > 1 && std::strcmp(argv[1], "--host-only") == 0) {
+    const char* mode = argc > 1 ? argv[1] : "";
+    if (std::strcmp(mode, "--host-only") == 0) {
         if (g_fails) return 1;
         std::printf("all tests passed\n");
         return 0;
     }
+    // --down-project: only the down projection (run late in the suite)
+    const bool down_only = std::strcmp(mode, "--down-project") == 0;
     try {
         CudaBackend be(0);
+        if (down_only) {
+            test_down_project(be, DType::Q4_K, 14336, 4096, 1);
+            test_down_project(be, DType::Q4_K, 1024, 512, 3);
+            test_down_project(be, DType::Q8_0, 96, 4096, 9);
+            test_down_project(be, DType::Q6_K, 512, 512, 2);
+            be.sync();
+            if (g_fails) {
+                std::printf("%d checks FAILED\n", g_fails);
+                return 1;
+            }
+            std::printf("all tests passed\n");
+            return 0;
+        }
         CHECK(be.ready(), "backend ready");
         CHECK(be.info().mem_bytes > (100ull << 30), "device memory reported");
         CHECK(be.alloc_staging(1 << 20) == nullptr, "no staging buffers");
@@ -208,10 +236,6 @@ int main(int argc, char** argv) {
         test_matmul(be, DType::Q4_K, 4096, 14336, 128);  // a prefill chunk
         test_matmul(be, DType::Q8_0, 512, 4096, 20);     // GEMV, 8 rows per pass
         test_expert_chunk_windows(be);
-        test_down_project(be, DType::Q4_K, 14336, 4096, 1);
-        test_down_project(be, DType::Q4_K, 1024, 512, 3);
-        test_down_project(be, DType::Q8_0, 96, 4096, 9);
-        test_down_project(be, DType::Q6_K, 512, 512, 2);
         test_upload_and_errors(be);
     } catch (const std::exception& e) {
         std::printf("FAIL exception: %s\n", e.what());

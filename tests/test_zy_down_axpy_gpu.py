@@ -3,7 +3,12 @@ layout, ft::matmul_down_axpy (ft/src/cpu_backend.cpp:60-75): y[m] += x_m . W
 over n_in rows of N weights, zero activations skipped, y accumulated.
 Checked against the CPU oracle and, through the golden fixture, against the
 reference's own outputs.  Tolerance as in the GEMV tests: max |y - ref| /
-(|ref| + 1e-2 rms(ref)) <= 2e-3 (the GPU sums row slabs separately)."""
+(|ref| + 1e-2 rms(ref)) <= 2e-3 (the GPU sums row slabs separately).  Also
+runs the C++ adapter's down_project checks (tests/cpp/test_cuda_backend.cpp
+--down-project).  The file runs late in the suite, after the kernels this
+path shares (dequant, GEMV, GEMM) are checked."""
+import subprocess
+
 import numpy as np
 import pytest
 
@@ -167,3 +172,10 @@ def test_backend_entry(ftc, oracle):
             be.matmul_down_axpy(x, m, n_in + 1, W, y2)
     finally:
         be.close()
+
+
+def test_cpp_adapter_down_project(tmp_path):
+    from tests.test_cpp_backend import compile_test
+    exe = compile_test(str(tmp_path / "test_cuda_backend"))
+    r = subprocess.run([exe, "--down-project"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "all tests passed" in r.stdout, r.stdout + r.stderr
