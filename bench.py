@@ -274,6 +274,8 @@ def run_ours(args, rank, world, local_rank):
                             "GBps": round(gbytes / (us * 1e-6) / 1e9, 0)}
         del gg
 
+    decode_extras = time_decode_extras(dev, dptr, stream)
+
     # e2e through the C ABI: host x in, host y out, per ftc_backend_matmul call
     ext = torch.cuda.ExternalStream(be.stream(), device=dev)
     yh = {name: np.empty((1, n), dtype=np.float32) for name, n, _ in LAYER}
@@ -368,6 +370,8 @@ def run_ours(args, rank, world, local_rank):
             "d2h_bytes_per_step": d2h,
             "api": "ftc_backend_matmul (ft::IBackend::matmul), pinned staging, sync per call",
         },
+        "decode_batched": decode_extras["batched"],
+        "q6_k_head": decode_extras["q6_k_head"],
         "prefill_dequant_gemm": prefill_summary(prefill, gemm_status),
         "tp_block": tp_block,
         "moe": moe,
@@ -377,6 +381,78 @@ def run_ours(args, rank, world, local_rank):
         "setup_s": round(setup_s, 1),
     }
     return line
+
+
+def time_decode_extras(dev, dptr, stream, reps=20):
+    """Config 2's other cases: the same 8 layer copies at batch 4 and 8 (one
+    ftc_mul_mat_vec launch per matrix, graph-replayed), and the Q6_K output
+    head (128256 x 4096, 431 MB, larger than L2) at batch 1."""
+    import torch
+    from xwfes_b200 import ftc
+    L = ftc.lib()
+    hbm, _, _ = peaks()
+    sp = stream.cuda_stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wbytes, _ = layer_bytes()
+    batched = {}
+    for m in (4, 8):
+        xm = {nm: torch.from_numpy(S.activations_f32(m, ln, seed=0, name=nm)).to(dev)
+              for nm, ln in X_LEN.items()}
+        ym = {name: torch.empty((m, n), dtype=torch.float32, device=dev) for name, n, _ in LAYER}
+
+        def bstep():
+            for li in range(N_LAYERS):
+                for name, n, k in LAYER:
+                    rc = L.ftc_mul_mat_vec(F.Q4_K, dptr[(li, name)], n, k, F.row_bytes(F.Q4_K, k),
+                                           xm[X_OF[name]].data_ptr(), m, ym[name].data_ptr(), sp)
+                    if rc:
+                        raise ftc.FtcError("ftc_mul_mat_vec", rc, ftc.last_error())
+
+        with torch.cuda.stream(stream):
+            bstep()  # eager warm-up outside capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            bstep()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+        us = ev0.elapsed_time(ev1) * 1e3 / reps / N_LAYERS  # per layer
+        gbs = wbytes / (us * 1e-6) / 1e9
+        batched[str(m)] = {"us_per_layer": round(us, 2), "weight_GBps": round(gbs, 1),
+                           "frac_of_hbm": round(gbs / hbm, 3),
+                           "tokens_per_s": round(m / (32 * us * 1e-6), 1)}
+        del g
+    n, k = 128256, 4096
+    # 8 repeats of 16032 seeded rows: the bytes differ in address, not content
+    w = torch.from_numpy(np.tile(S.weight(F.Q6_K, n // 8, k, seed=0, name="head"), (8, 1))).to(dev)
+    x = torch.from_numpy(S.activations_f32(1, k, seed=0, name="head")).to(dev)
+    y = torch.empty((1, n), dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            ftc.mul_mat_vec(w, F.Q6_K, n, k, x, y=y, stream=stream)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(reps):
+            ftc.mul_mat_vec(w, F.Q6_K, n, k, x, y=y, stream=stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    us = ev0.elapsed_time(ev1) * 1e3 / reps
+    hb = n * F.row_bytes(F.Q6_K, k)
+    head = {"us": round(us, 1), "weight_GBps": round(hb / (us * 1e-6) / 1e9, 1),
+            "frac_of_hbm": round(hb / (us * 1e-6) / 1e9 / hbm, 3), "bytes": hb,
+            "l2": "weight 431 MB > L2: every launch streams from HBM"}
+    del w
+    return {"batched": {"workload": "config 2 layer x 8 copies, fp32 activations, batch 4 and 8 "
+                                    "(gemv_q4k batched kernel, one launch per matrix)",
+                        "per_batch": batched},
+            "q6_k_head": {"workload": "config 2 Q6_K output head 128256x4096, batch 1", **head}}
 
 
 TP_M = [1, 16, 1024]
