@@ -372,6 +372,7 @@ def run_ours(args, rank, world, local_rank):
         },
         "decode_batched": decode_extras["batched"],
         "q6_k_head": decode_extras["q6_k_head"],
+        "q8_0_config1": decode_extras["q8_0_config1"],
         "prefill_dequant_gemm": prefill_summary(prefill, gemm_status),
         "tp_block": tp_block,
         "moe": moe,
@@ -449,7 +450,35 @@ def time_decode_extras(dev, dptr, stream, reps=20):
             "frac_of_hbm": round(hb / (us * 1e-6) / 1e9 / hbm, 3), "bytes": hb,
             "l2": "weight 431 MB > L2: every launch streams from HBM"}
     del w
-    return {"batched": {"workload": "config 2 layer x 8 copies, fp32 activations, batch 4 and 8 "
+    # config 1 (Q8_0 4096 x 4096, 17.8 MB): 8 copies per graph so the launches stream from HBM
+    n1 = k1 = 4096
+    w1 = [torch.from_numpy(S.weight(F.Q8_0, n1, k1, seed=c, name="c1")).to(dev) for c in range(8)]
+    x1 = torch.from_numpy(S.activations_f32(1, k1, seed=0, name="c1")).to(dev)
+    y1 = torch.empty((1, n1), dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        for wc in w1:
+            ftc.mul_mat_vec(wc, F.Q8_0, n1, k1, x1, y=y1, stream=stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for wc in w1:
+                ftc.mul_mat_vec(wc, F.Q8_0, n1, k1, x1, y=y1, stream=stream)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    us = ev0.elapsed_time(ev1) * 1e3 / reps / len(w1)
+    b1 = n1 * F.row_bytes(F.Q8_0, k1)
+    q8 = {"workload": "config 1: Q8_0 GEMV 4096x4096, batch 1 (8 weight copies per graph)",
+          "us": round(us, 2), "weight_GBps": round(b1 / (us * 1e-6) / 1e9, 1),
+          "frac_of_hbm": round(b1 / (us * 1e-6) / 1e9 / hbm, 3), "bytes": b1}
+    del g, w1
+    return {"q8_0_config1": q8,
+            "batched": {"workload": "config 2 layer x 8 copies, fp32 activations, batch 4 and 8 "
                                     "(gemv_q4k batched kernel, one launch per matrix)",
                         "per_batch": batched},
             "q6_k_head": {"workload": "config 2 Q6_K output head 128256x4096, batch 1", **head}}
