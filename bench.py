@@ -811,6 +811,43 @@ def run_ncu_gemm_split_probe():
     return 0
 
 
+def run_down_axpy(reps=50):
+    """The engine's neuron-major down projection (ftc_matmul_down_axpy) on the
+    Llama-3-8B dense down shape, n_ff = 14336 rows of 4096 Q4_K weights, at 1
+    and 8 tokens: 4 weight copies rotated (132 MB > L2), CUDA events.  Prints
+    one JSON line; also the small case for an ncu capture (-k regex:rows_axpy)."""
+    import torch
+    from xwfes_b200 import ftc
+    dev = torch.device("cuda", 0)
+    n_in, n = 14336, 4096
+    ws = [torch.from_numpy(S.weight(F.Q4_K, n_in, n, seed=c, name="axpy")).to(dev)
+          for c in range(4)]
+    hbm, _, kind = peaks()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = {}
+    for m in (1, 8):
+        x = torch.from_numpy(S.activations_f32(m, n_in, seed=0, name="axpy.x")).to(dev)
+        y = torch.zeros((m, n), dtype=torch.float32, device=dev)
+        need = ftc.lib().ftc_matmul_down_axpy_workspace_bytes(F.Q4_K, n_in, n, m)
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+        for i in range(3):
+            ftc.matmul_down_axpy(ws[i % 4], F.Q4_K, n_in, n, x, y, ws=scratch)
+        torch.cuda.synchronize()
+        ev0.record()
+        for i in range(reps):
+            ftc.matmul_down_axpy(ws[i % 4], F.Q4_K, n_in, n, x, y, ws=scratch)
+        ev1.record()
+        torch.cuda.synchronize()
+        us = ev0.elapsed_time(ev1) * 1e3 / reps
+        b = n_in * F.row_bytes(F.Q4_K, n) + 4 * m * (n_in + 2 * n)
+        out[str(m)] = {"us": round(us, 2), "GBps": round(b / (us * 1e-6) / 1e9, 1),
+                       "frac": round(b / (us * 1e-6) / 1e9 / hbm, 3), "bytes": b,
+                       "workspace_bytes": need}
+    print(json.dumps({"probe": "ftc_matmul_down_axpy 14336 rows x 4096 Q4_K", "peak": hbm,
+                      "peak_kind": kind, "per_M": out, "status": ftc.device_status()}))
+    return 0
+
+
 # ----------------------------------------------------------- CPU baselines
 
 def cpu_sample(threads, budget_s=10.0):
@@ -923,6 +960,9 @@ def main():
     ap.add_argument("--ncu-gemm", action="store_true",
                     help="profiling mode: three launches of the config-3 dequant-GEMM "
                          "(14336x4096, M=2048, bf16), no timing")
+    ap.add_argument("--down-axpy", action="store_true",
+                    help="time the neuron-major down projection (ftc_matmul_down_axpy) alone "
+                         "and print one JSON line; also the case for ncu captures of rows_axpy")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -936,6 +976,8 @@ def main():
         return run_ncu_gemm_probe()
     if args.ncu_gemm_split:
         return run_ncu_gemm_split_probe()
+    if args.down_axpy:
+        return run_down_axpy()
 
     if args.impl == "reference":
         if rank != 0:
