@@ -521,7 +521,9 @@ def time_tp(dev, world, rank, seed=0):
     st = torch.cuda.current_stream()
     cs = torch.cuda.Stream(device=dev)
     for M in TP_M:
-        x = torch.from_numpy(S.activations_f32(M, d["n_embd"], seed=seed, name=f"tp.x{M}")).to(dev)
+        # config 4's bf16 N(0,1) activations, carried as fp32 (every value bf16-exact)
+        x = torch.from_numpy(S.bf16_bits_to_f32(
+            S.activations_bf16(M, d["n_embd"], seed=seed, name=f"tp.x{M}"))).to(dev)
         reps = 60 if M <= 16 else 12
         with torch.cuda.stream(cs):
             for i in range(3 * copies):  # eager warm-up (NCCL, kernel attributes) before capture
@@ -561,7 +563,8 @@ def time_tp(dev, world, rank, seed=0):
         dist.barrier(device_ids=[dev.index])  # no rank still writes into a peer's buffer
         peer.close()
     return {"workload": "config 4: Llama-3-70B-shaped Q4_K block (q 8192x8192, k/v 1024x8192, "
-                        "o 8192x8192, gate/up 28672x8192, down 8192x28672), fp32 activations",
+                        "o 8192x8192, gate/up 28672x8192, down 8192x28672), bf16 N(0,1) activations "
+                        "carried as fp32",
             "parallelism": f"tp{world} (column-parallel q/k/v/gate/up, row-parallel o/down, "
                            f"allreduce of fp32 partials after o and down: one-shot over NVLink "
                            f"peer memory (ftc_peer_ar) for M <= {TP_PEER_M}, NCCL above)",
