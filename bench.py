@@ -877,20 +877,58 @@ def cpu_sample(threads, budget_s=10.0):
 
 
 def reference_q8_0_config1(threads):
-    """The reference's own CpuBackend::matmul (oracle/_ref) on config 1."""
+    """The reference's own CpuBackend::matmul (oracle/_ref) on config 1, with
+    all host threads and with one."""
     from oracle import oracle as O
     if not O.have_ref():
         return None
     w = S.weight(F.Q8_0, 4096, 4096, seed=0, name="c1")
     x = S.activations_f32(1, 4096, seed=0, name="c1")
-    O.ref_matmul(x, w, F.Q8_0, 4096, threads=threads)
-    reps = 20
-    t = time.perf_counter()
-    for _ in range(reps):
-        O.ref_matmul(x, w, F.Q8_0, 4096, threads=threads)
-    dt = (time.perf_counter() - t) / reps
-    return {"value": round(w.nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
-            "kind": "reference", "sample": "config 1: Q8_0 4096x4096 GEMV, 20 calls"}
+    out = {}
+    for th in sorted({threads, 1}, reverse=True):
+        O.ref_matmul(x, w, F.Q8_0, 4096, threads=th)
+        reps = 20
+        t = time.perf_counter()
+        for _ in range(reps):
+            O.ref_matmul(x, w, F.Q8_0, 4096, threads=th)
+        dt = (time.perf_counter() - t) / reps
+        out[th] = w.nbytes / dt / 1e9
+    return {"value": round(out[threads], 3), "unit": "GB/s", "cores": threads,
+            "value_1_thread": round(out[1], 3), "kind": "reference",
+            "sample": "config 1: Q8_0 4096x4096 GEMV, 20 calls per thread count"}
+
+
+def reference_expert_chunk_q8_0(threads):
+    """The reference's own CpuBackend::run_expert_chunk (oracle/_ref) on the
+    Q8_0 variant of config 5 (the reference has no Q4_K decoder): one window
+    of 1280 neurons -- the window ExpertStreamer::auto_chunk picks for the
+    16 MiB staging budget, ft/include/ft/chunker.h:81-89 -- of one expert
+    (4096 x 14336 shapes) with 16 tokens (T = 64, top-2, 8 experts: 16 rows
+    per expert on average); all host threads and one."""
+    from oracle import oracle as O
+    if not O.have_ref():
+        return None
+    K, IC, M = 4096, 1280, 16
+    g, u, d = (S.weight(F.Q8_0, IC, K, seed=0, name=f"c5q8.{nm}") for nm in ("gate", "up", "down"))
+    x = S.activations_f32(M, K, seed=0, name="c5q8.x")
+    wb = g.nbytes + u.nbytes + d.nbytes
+    per = {}
+    for th in sorted({threads, 1}, reverse=True):
+        out = np.zeros((M, K), dtype=np.float32)
+        O.ref_expert_chunk(x, out, g, u, d, F.Q8_0, K, IC, threads=th)
+        reps = 3
+        t = time.perf_counter()
+        for _ in range(reps):
+            O.ref_expert_chunk(x, out, g, u, d, F.Q8_0, K, IC, threads=th)
+        per[th] = (time.perf_counter() - t) / reps
+    windows = 8 * -(-14336 // IC)  # every expert holds tokens at T = 64
+    return {"s_per_window": round(per[threads], 4), "s_per_window_1_thread": round(per[1], 4),
+            "weight_GBps": round(wb / per[threads] / 1e9, 3), "cores": threads,
+            "layer_s_at_T64": round(windows * per[threads], 2),
+            "tokens_per_s_at_T64": round(64 / (windows * per[threads]), 2),
+            "kind": "reference",
+            "sample": f"one run_expert_chunk window: Q8_0, K=4096, IC={IC}, M={M}, 3 calls per "
+                      "thread count; layer time = 8 experts x 12 windows of it"}
 
 
 def run_reference(args):
@@ -942,6 +980,7 @@ def run_reference(args):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "reference_q8_0_config1": reference_q8_0_config1(threads),
+        "reference_expert_chunk_q8_0_config5": reference_expert_chunk_q8_0(threads),
     }
 
 
@@ -1009,6 +1048,9 @@ def main():
             ref = reference_q8_0_config1(threads)
             if ref:
                 line["reference_q8_0_config1"] = ref
+            ref = reference_expert_chunk_q8_0(threads)
+            if ref:
+                line["reference_expert_chunk_q8_0_config5"] = ref
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
