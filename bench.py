@@ -503,6 +503,7 @@ def time_tp(dev, world, rank, seed=0):
     from xwfes_b200 import tp
     from xwfes_b200 import ftc
     d = tp.DIMS_70B
+    hbm, bf16, _ = peaks()
     ops = tp.CudaOps(dev)
     shard_b = tp.weight_bytes(d) // world
     copies = min(4, max(1, -(-2 * L2_BYTES // shard_b)))
@@ -555,9 +556,14 @@ def time_tp(dev, world, rank, seed=0):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us = t.item() * 1e3
+        gbs = tp.weight_bytes(d) / (us * 1e-6) / 1e9
+        tfl = tp.flops(d, M) / (us * 1e-6) / 1e12
         out[str(M)] = {"us": round(us, 1), "tokens_per_s": round(M / (us * 1e-6), 1),
-                       "weight_GBps": round(tp.weight_bytes(d) / (us * 1e-6) / 1e9, 1),
-                       "tflops": round(tp.flops(d, M) / (us * 1e-6) / 1e12, 2)}
+                       "weight_GBps": round(gbs, 1), "tflops": round(tfl, 2),
+                       # fractions of the world's aggregate measured peaks
+                       "frac_of_hbm": round(gbs / (world * hbm), 3),
+                       "frac_of_bf16": round(tfl / (world * bf16), 3),
+                       "bound": "hbm" if M <= 16 else "tensor"}
     del blocks
     if peer is not None:
         dist.barrier(device_ids=[dev.index])  # no rank still writes into a peer's buffer
@@ -642,6 +648,7 @@ def time_ep(dev, world, rank):
     import torch.distributed as dist
     from xwfes_b200 import ep
     d = ep.DIMS_MIXTRAL
+    hbm, bf16, _ = peaks()
     E, U, K, FF = d["n_experts"], d["top_k"], d["n_embd"], d["n_ff"]
     e0, e1 = ep.expert_range(E, world, rank)
     mk = lambda nm, n, k: torch.from_numpy(np.stack(
@@ -683,9 +690,12 @@ def time_ep(dev, world, rank):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us = t.item() * 1e3
+        gbs = E * per_expert / (us * 1e-6) / 1e9
+        tfl = 2.0 * T * U * 3 * FF * K / (us * 1e-6) / 1e12
         out[str(T)] = {"us": round(us, 1), "tokens_per_s": round(T / (us * 1e-6), 1),
-                       "weight_GBps": round(E * per_expert / (us * 1e-6) / 1e9, 1),
-                       "tflops": round(2.0 * T * U * 3 * FF * K / (us * 1e-6) / 1e12, 2)}
+                       "weight_GBps": round(gbs, 1), "tflops": round(tfl, 2),
+                       "frac_of_hbm": round(gbs / (world * hbm), 3),
+                       "frac_of_bf16": round(tfl / (world * bf16), 3)}
     return {"workload": "config 5: Mixtral-8x7B-shaped MoE layer, expert-parallel, T tokens "
                         "split over the ranks",
             "parallelism": f"ep{world} ({E // world} experts per GPU; equal-split NCCL "
