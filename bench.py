@@ -591,6 +591,7 @@ def time_moe(dev):
     import torch
     from xwfes_b200 import ftc
     E, U, K, FF = 8, 2, 4096, 14336
+    hbm, bf16, _ = peaks()
     mk = lambda nm, n, k: torch.from_numpy(
         S.expert_weights(F.Q4_K, E, n, k, seed=0, name=f"moe.{nm}")).to(dev)
     layer = ftc.MoeLayer(mk("gate", FF, K), mk("up", FF, K), mk("down", K, FF), n_experts=E,
@@ -621,10 +622,12 @@ def time_moe(dev):
                 ts.append(e0.elapsed_time(e1) * 1e3)
         used = int((layer.routing(T)[2] > 0).sum().item())
         us = statistics.median(ts)
+        gbs = used * per_expert / (us * 1e-6) / 1e9
+        tfl = 2.0 * T * U * 3 * FF * K / (us * 1e-6) / 1e12
         out[str(T)] = {"us": round(us, 1), "tokens_per_s": round(T / (us * 1e-6), 1),
                        "experts_used": used,
-                       "weight_GBps": round(used * per_expert / (us * 1e-6) / 1e9, 1),
-                       "tflops": round(2.0 * T * U * 3 * FF * K / (us * 1e-6) / 1e12, 2),
+                       "weight_GBps": round(gbs, 1), "tflops": round(tfl, 2),
+                       "frac_of_hbm": round(gbs / hbm, 3), "frac_of_bf16": round(tfl / bf16, 3),
                        "path": "decode GEMVs" if 2 * T * U <= 8 else "grouped tcgen05 GEMMs"}
         del g
     return {"workload": "config 5: 8 experts x Q4_K gate/up 14336x4096 + down 4096x14336, "
