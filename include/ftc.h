@@ -401,6 +401,19 @@ int ftc_peer_ar_destroy(ftc_peer_ar* ar);
 int ftc_mul_mat_vec_allreduce(ftc_peer_ar* ar, int dtype, const void* w, int64_t N, int64_t K,
                                int64_t row_stride, const float* x, float* y, void* stream);
 
+/* The row-parallel down projection of a SiLU FFN at one token, with the
+ * activation computed as it is loaded:
+ *   y[n] = sum_k silu(gu[k]) * gu[up_offset + k] * W[n][k]
+ * silu(g) * u = g / (1 + exp(-g)) * u in fp32 (ft/src/cpu_backend.cpp:127),
+ * bit for bit what ftc_silu_mul_rows + ftc_mul_mat_vec give.  gu: DEVICE
+ * fp32 [gate (K) | ... | up (K)] (the output row of a stacked gate/up
+ * matmul), 16-byte aligned, up_offset >= K and a multiple of 4.  With ar
+ * (may be NULL) the product is also summed over the ranks in the kernel, as
+ * ftc_mul_mat_vec_allreduce.  Q4_K, 16-byte aligned rows. */
+int ftc_mul_mat_vec_silu(ftc_peer_ar* ar, int dtype, const void* w, int64_t N, int64_t K,
+                         int64_t row_stride, const float* gu, int64_t up_offset, float* y,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

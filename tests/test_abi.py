@@ -81,6 +81,20 @@ def test_down_axpy_validates_before_launch(lib):
     assert call(F.Q4_K, None, 0, 4096, rb, None, 3, None, None, 0, None) == 0
 
 
+def test_fused_silu_gemv_validates_before_launch(lib):
+    call = lib.ftc_mul_mat_vec_silu
+    rb = F.row_bytes(F.Q4_K, 3584)
+    assert call(None, F.Q4_K, None, 8192, 3584, rb, 16, 3584, 16, None) == -1
+    assert "null" in ftc.last_error()
+    assert call(None, F.Q8_0, 16, 8192, 3584, rb, 16, 3584, 16, None) == -2
+    assert call(None, F.Q4_K, 16, 8192, 3500, rb, 16, 3584, 16, None) == -1
+    assert "bad shape" in ftc.last_error()
+    assert call(None, F.Q4_K, 16, 8192, 3584, rb, 16, 3000, 16, None) == -1
+    assert "up_offset" in ftc.last_error()
+    assert call(None, F.Q4_K, 16, 8192, 3584, rb, 16, 3586, 16, None) == -1
+    assert "up_offset" in ftc.last_error()
+
+
 def _moe_desc(**kw):
     rs, rd = F.row_bytes(F.Q4_K, 1024), F.row_bytes(F.Q4_K, 2048)
     v = dict(dtype=F.Q4_K, n_experts=8, top_k=2, n_embd=1024, n_ff=2048, gate_exps=256,

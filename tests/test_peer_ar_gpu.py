@@ -107,6 +107,18 @@ elif mode == "fused":
     out["g_ref"] = yr.cpu().numpy()
     torch.cuda.synchronize()
     assert ftc.device_status() == 0
+elif mode == "fused_silu":
+    from xwfes_b200 import formats as F, synth as S
+    for i, (n, k) in enumerate([(8192, 3584), (4096, 1024)]):
+        w = torch.from_numpy(S.weight(F.Q4_K, n, k, seed=rank, name=f"ps.{{i}}")).cuda()
+        gu = (4 * torch.from_numpy(T.inputs(rank, 2 * k, 300 + i))).cuda().reshape(1, 2 * k)
+        yf = ar.silu_mul_mat_vec_sum(w, F.Q4_K, n, k, gu)
+        yr = ftc.mul_mat_vec(w, F.Q4_K, n, k, ftc.silu_mul_rows(gu, k))
+        ar.sum_(yr)
+        out[f"sf{{i}}"] = yf.cpu().numpy()
+        out[f"sr{{i}}"] = yr.cpu().numpy()
+    torch.cuda.synchronize()
+    assert ftc.device_status() == 0
 else:  # rank 1 stays out of the call; rank 0 must time out cleanly
     if rank == 0:
         t = torch.ones(8192, device="cuda")

@@ -175,4 +175,11 @@ __device__ __forceinline__ float decode_elem(int dtype, const uint8_t* row, int6
     }
 }
 
+// ------------------------------------------------------------ activation
+
+// silu(g) * u = g / (1 + exp(-g)) * u in fp32, the reference's expert FFN
+// activation (ft/src/cpu_backend.cpp:127); every kernel that applies it uses
+// this one expression, so fused and separate evaluations give the same bits.
+__device__ __forceinline__ float silu_gate(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
 }  // namespace ftc

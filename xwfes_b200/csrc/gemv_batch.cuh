@@ -58,6 +58,11 @@ struct GemvSpec {
     // Allreduce over a tensor-parallel group (one matrix, y the sum over the
     // ranks of their partial products): nullptr for a plain GEMV.
     const PeerView* peer;
+    // 0: x is the activation.  > 0: x holds a [gate | up] row, up at
+    // x + x_up floats (a multiple of 4), and the activation is
+    // silu_gate(gate[k], up[k]) -- the SiLU product folded into the
+    // activation load, bit for bit what a separate silu kernel would give.
+    int64_t x_up;
 };
 
 constexpr int64_t kGemvPrefetchWindow = 24ll << 20;

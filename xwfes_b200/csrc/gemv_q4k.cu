@@ -85,6 +85,7 @@ struct GemvBatch {
     // partial products, exchanged through peer memory (see peer_ar.cu)
     int fused;
     PeerView peer;
+    int64_t x_up;  // see GemvSpec::x_up
 };
 
 namespace {
@@ -137,14 +138,17 @@ __device__ __forceinline__ void plane_block(const float (&v)[8], int sb, int lan
 // sub-block sums and the block scale, laid out for the consumers:
 //   planes[(sb*4 + t)*kPlaneWords + plane*16 + u]   u = word within the lane's 64
 //   sums[(sb*4 + t)*2 + {0: low sub-block, 1: high}],  scales[sb]
-__device__ __forceinline__ void build_planes(const float* __restrict__ x, int nsb, int cw, int ncw,
-                                             int lane, uint32_t* planes, float* sums,
-                                             float* scales) {
+// kSilu: x is a [gate | up] row (up at x + x_up) and the activation is
+// silu_gate(gate, up).
+template <bool kSilu>
+__device__ __forceinline__ void build_planes(const float* __restrict__ x, int64_t x_up, int nsb,
+                                             int cw, int ncw, int lane, uint32_t* planes,
+                                             float* sums, float* scales) {
     // the warp's blocks go four at a time: all loads of a batch are in
     // flight together, so a long x costs one L2 round trip per batch
     constexpr int kBatch = 4;
     for (int sb0 = cw; sb0 < nsb; sb0 += kBatch * ncw) {
-        float4 a[kBatch], b[kBatch];
+        float4 a[kBatch], b[kBatch], ua[kBatch], ub[kBatch];
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
             const int sb = sb0 + i * ncw;
@@ -152,13 +156,25 @@ __device__ __forceinline__ void build_planes(const float* __restrict__ x, int ns
                 const float4* xp = reinterpret_cast<const float4*>(x + (int64_t)sb * 256 + 8 * lane);
                 a[i] = __ldg(xp);
                 b[i] = __ldg(xp + 1);
+                if (kSilu) {
+                    const float4* up = reinterpret_cast<const float4*>(x + x_up + (int64_t)sb * 256 +
+                                                                       8 * lane);
+                    ua[i] = __ldg(up);
+                    ub[i] = __ldg(up + 1);
+                }
             }
         }
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
             const int sb = sb0 + i * ncw;
             if (sb >= nsb) break;
-            const float v[8] = {a[i].x, a[i].y, a[i].z, a[i].w, b[i].x, b[i].y, b[i].z, b[i].w};
+            float v[8] = {a[i].x, a[i].y, a[i].z, a[i].w, b[i].x, b[i].y, b[i].z, b[i].w};
+            if (kSilu) {
+                const float u[8] = {ua[i].x, ua[i].y, ua[i].z, ua[i].w,
+                                    ub[i].x, ub[i].y, ub[i].z, ub[i].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = silu_gate(v[j], u[j]);
+            }
             plane_block(v, sb, lane, planes, sums, scales);
         }
     }
@@ -352,7 +368,7 @@ __device__ __noinline__ void fused_allreduce_tail(const GemvBatch& B, const Chun
     if (threadIdx.x == 0) peer_call_done(P.ctr, epoch);
 }
 
-template <int RPW>
+template <int RPW, bool kSilu>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int WK, int WR,
               int RC) {
@@ -478,7 +494,7 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
 
     // ---------------------------------------------------- consumer warps
     grid_dependency_wait();  // x may be the preceding kernel's output
-    build_planes(cw.x, nsb, warp, NCW, lane, planes, sums, scales);
+    build_planes<kSilu>(cw.x, B.x_up, nsb, warp, NCW, lane, planes, sums, scales);
     named_barrier(1, NCW * 32);
 
     const int wr = warp / WK, wk = warp % WK;
@@ -612,6 +628,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     if (g.sel && (g.sel_stride % 16 || g.sel_max < 0)) return FTC_E_UNSUPPORTED;
     if (g.peer && (P != 1 || g.per_matrix_x || g.sel || g.N[0] > g.peer->max_elems))
         return FTC_E_UNSUPPORTED;
+    if (g.x_up < 0 || g.x_up % 4) return FTC_E_UNSUPPORTED;  // up half 16-byte aligned
     Q4kPlan p;
     if (!plan_q4k(ntot, g.K, g.stride, p)) return FTC_E_UNSUPPORTED;
     static int sms = 0;
@@ -647,6 +664,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     const int nchunks = B.first_chunk[P];
     p.grid = std::min(nchunks, sms);
     B.fused = g.peer ? 1 : 0;
+    B.x_up = g.x_up;
     if (g.peer) {
         B.peer = *g.peer;
     }
@@ -674,7 +692,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     }
     const int nsb = (int)(g.K / 256);
     // opt in to large dynamic shared memory once per instantiation
-    static bool configured[3] = {false, false, false};
+    static bool configured[6] = {false, false, false, false, false, false};
     auto launch = [&](auto kern, int idx) -> int {
         if (!configured[idx]) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -696,9 +714,15 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
         if (e != cudaSuccess) return cuda_error(e, "launch gemv_q4k_dp4a");
         return FTC_OK;
     };
-    int rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4>, 2)
-           : p.RPW == 2 ? launch(gemv_q4k_dp4a<2>, 1)
-                        : launch(gemv_q4k_dp4a<1>, 0);
+    int rc;
+    if (g.x_up == 0)
+        rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, false>, 2)
+           : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, false>, 1)
+                        : launch(gemv_q4k_dp4a<1, false>, 0);
+    else
+        rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, true>, 5)
+           : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, true>, 4)
+                        : launch(gemv_q4k_dp4a<1, true>, 3);
     if (rc != FTC_OK) return rc;
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;

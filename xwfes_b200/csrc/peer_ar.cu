@@ -334,6 +334,43 @@ int ftc_mul_mat_vec_allreduce(ftc_peer_ar* ar, int dtype, const void* w, int64_t
     return rc ? rc : ok();
 }
 
+int ftc_mul_mat_vec_silu(ftc_peer_ar* ar, int dtype, const void* w, int64_t N, int64_t K,
+                         int64_t row_stride, const float* gu, int64_t up_offset, float* y,
+                         void* stream) {
+    using namespace ftc;
+    FTC_REQUIRE(w && gu && y, FTC_E_INVALID, "ftc_mul_mat_vec_silu: null pointer");
+    FTC_REQUIRE(dtype == FTC_Q4_K, FTC_E_UNSUPPORTED, "ftc_mul_mat_vec_silu: Q4_K weights only");
+    FTC_REQUIRE(N > 0 && K > 0 && K % 256 == 0 && row_stride >= (K / 256) * 144, FTC_E_INVALID,
+                "ftc_mul_mat_vec_silu: bad shape");
+    FTC_REQUIRE(up_offset >= K && up_offset % 4 == 0, FTC_E_INVALID,
+                "ftc_mul_mat_vec_silu: up_offset must be >= K and a multiple of 4");
+    FTC_REQUIRE(!ar || N <= ar->max_elems, FTC_E_INVALID,
+                "ftc_mul_mat_vec_silu: N exceeds the buffer's max_elems");
+    if (inject_fail("ftc_mul_mat_vec_silu"))
+        return set_error(FTC_E_INJECTED, "ftc_mul_mat_vec_silu: injected failure");
+    PeerView v;
+    if (ar) {
+        int rc = peer_ar_view(ar, &v);
+        if (rc) return rc;
+    }
+    GemvSpec g = {};
+    g.P = 1;
+    g.K = K;
+    g.stride = row_stride;
+    g.W[0] = static_cast<const uint8_t*>(w);
+    g.N[0] = N;
+    g.y[0] = y;
+    g.x[0] = gu;
+    g.x_up = up_offset;
+    g.peer = ar ? &v : nullptr;
+    const int rc = gemv_q4k_batch(g, (cudaStream_t)stream);
+    if (rc == FTC_E_UNSUPPORTED)
+        return set_error(rc, "ftc_mul_mat_vec_silu: shape or alignment not supported by the "
+                             "fused kernel (16-byte aligned rows and gu; use ftc_silu_mul_rows + "
+                             "ftc_mul_mat_vec)");
+    return rc ? rc : ok();
+}
+
 int ftc_peer_ar_destroy(ftc_peer_ar* ar) {
     using namespace ftc;
     if (!ar) return ok();

@@ -57,8 +57,6 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
     }
 }
 
-__device__ __forceinline__ float silu_gate(float g, float u) { return g / (1.f + expf(-g)) * u; }
-
 // fp32 rows: h[m][k] = silu(gu[m][k]) * gu[m][n + k], grid-stride over all
 // elements (decode-sized M has too few rows for one CTA per row).
 __global__ void silu_mul_rows_f32(const float* __restrict__ gu, int64_t ld, int64_t rows, int n,

@@ -68,6 +68,7 @@ SIGNATURES = {
     "ftc_peer_ar_sum_f32": (C.c_int, [_p, _p, _p, _i64, _p]),
     "ftc_peer_ar_destroy": (C.c_int, [_p]),
     "ftc_mul_mat_vec_allreduce": (C.c_int, [_p, C.c_int, _p, _i64, _i64, _i64, _p, _p, _p]),
+    "ftc_mul_mat_vec_silu": (C.c_int, [_p, C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
 }
 
 
@@ -175,6 +176,24 @@ def matmul_down_axpy(w, dtype, n_in, n, x, y, row_stride=None, ws=None, stream=N
                                      ws.data_ptr() if ws is not None else None,
                                      ws.numel() if ws is not None else 0, _stream(stream)),
           "ftc_matmul_down_axpy")
+    return y
+
+
+def mul_mat_vec_silu(w, dtype, n, k, gu, up_offset=None, y=None, row_stride=None, ar=None,
+                     stream=None):
+    """y = (silu(gate) * up) . W^T for one token, the SiLU product computed as
+    the GEMV loads its activation (ftc_mul_mat_vec_silu): ``gu`` fp32 CUDA
+    tensor holding [gate (k) | up (k)] (up at ``up_offset``, default k).
+    With ``ar`` (a PeerAllreduce) y is summed over its ranks as well."""
+    import torch
+    t = F.dtype_id(dtype)
+    if y is None:
+        y = torch.empty((1, n), dtype=torch.float32, device=gu.device)
+    rs = row_stride if row_stride is not None else row_bytes(t, k)
+    off = k if up_offset is None else up_offset
+    check(lib().ftc_mul_mat_vec_silu(ar._ar if ar is not None else None, t, w.data_ptr(), n, k, rs,
+                                     gu.data_ptr(), off, y.data_ptr(), _stream(stream)),
+          "ftc_mul_mat_vec_silu")
     return y
 
 
@@ -643,6 +662,14 @@ class PeerAllreduce:
                                               y.data_ptr(), _stream(stream)),
               "ftc_mul_mat_vec_allreduce")
         return y
+
+    def silu_mul_mat_vec_sum(self, w, dtype, n, k, gu, up_offset=None, y=None, row_stride=None,
+                             stream=None):
+        """y = sum over the ranks of (silu(gate) * up) . W^T for this rank's
+        shard W, gu = [gate (k) | up (k)] fp32 (ftc_mul_mat_vec_silu): the
+        SiLU product, the GEMV and the allreduce in one kernel."""
+        return mul_mat_vec_silu(w, dtype, n, k, gu, up_offset=up_offset, y=y,
+                                row_stride=row_stride, ar=self, stream=stream)
 
     def close(self):
         if self._ar:
