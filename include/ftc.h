@@ -132,6 +132,20 @@ int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* jo
 int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int64_t n_in,
                                  const void* w_host, int dtype, int64_t N, float* y);
 
+/* The routed experts of the engine's moe_ffn (ft/src/engine.cpp:179-241)
+ * after its router matmul, with host buffers: the reference's router bias
+ * (bias[E], may be NULL) is added to the logits, then ftc_moe_ffn runs on
+ * the device and its result is added into out:
+ *   out[t] += sum over t's top_k experts e of w_e * down_e . (silu(gate_e . x_t) * (up_e . x_t))
+ * desc: as for ftc_moe_ffn but gate_exps / up_exps / down_exps are the
+ * tensors' HOST data pointers (the GGUF mapping), resolved through the HBM
+ * cache like ftc_backend_matmul's weights; down planes in the standard layout
+ * (n_embd rows of n_ff).  logits: host fp32 [T][E]; x: host fp32 [T][n_embd];
+ * out: host fp32 [T][n_embd] (the engine's tmpo).  T == 0 changes nothing. */
+struct ftc_moe_desc; /* defined with the device MoE entry points below */
+int ftc_backend_moe_ffn(ftc_backend* be, const struct ftc_moe_desc* desc, const float* logits,
+                        const float* bias, const float* x, int64_t T, float* out);
+
 /* ft::IBackend::sync (ft/include/ft/backend.h:39). */
 int ftc_backend_sync(ftc_backend* be);
 

@@ -166,6 +166,41 @@ static void test_down_project(CudaBackend& be, DType t, int64_t n_ff, int64_t n_
     }
 }
 
+// The engine's routed experts through moe_ffn against the oracle's MoE
+// (the reference's routing and expert arithmetic, standard down layout).
+static void test_moe_ffn(CudaBackend& be, int64_t T, bool with_bias) {
+    const int64_t E = 8, U = 2, K = 1024, FF = 2048;
+    auto g = random_blocks(DType::Q4_K, E * FF, K), u = random_blocks(DType::Q4_K, E * FF, K);
+    auto dn = random_blocks(DType::Q4_K, E * K, FF);
+    HostTensor G = view(g, DType::Q4_K, K, FF), Uu = view(u, DType::Q4_K, K, FF);
+    HostTensor D = view(dn, DType::Q4_K, FF, K);
+    G.ne[2] = Uu.ne[2] = D.ne[2] = E;
+    std::vector<float> x((size_t)(T * K)), logits((size_t)(T * E)), bias;
+    for (auto& v : x) v = rnd();
+    for (auto& v : logits) v = rnd() * 2.f;
+    if (with_bias) {
+        bias.resize((size_t)E);
+        for (auto& v : bias) v = rnd();
+    }
+    std::vector<float> out((size_t)(T * K)), ref((size_t)(T * K), 0.f), biased = logits;
+    for (auto& v : out) v = rnd();
+    const std::vector<float> out0 = out;
+    CHECK(be.moe_ffn(x.data(), logits.data(), bias, T, U, G, Uu, D, out.data()), "moe_ffn handled");
+    if (with_bias)
+        for (int64_t t = 0; t < T; ++t)
+            for (int64_t e = 0; e < E; ++e) biased[(size_t)(t * E + e)] += bias[(size_t)e];
+    ftor_moe_ffn(x.data(), biased.data(), T, K, FF, E, U, g.data(), u.data(), dn.data(), FTOR_Q4_K,
+                 ref.data(), 8);
+    for (size_t i = 0; i < ref.size(); ++i) ref[i] += out0[i];
+    char msg[96];
+    std::snprintf(msg, sizeof msg, "moe_ffn T %lld bias %d", (long long)T, (int)with_bias);
+    CHECK(norm_err(out, ref) <= 2e-3, msg);
+    HostTensor Dn = view(dn, DType::Q4_K, K, FF);  // neuron-major down: not handled
+    Dn.ne[2] = E;
+    CHECK(!be.moe_ffn(x.data(), logits.data(), bias, T, U, G, Uu, Dn, out.data()),
+          "neuron-major down left to the streamer");
+}
+
 // Host-only checks (no device): the down-weight layout by shape.
 static void test_down_layout() {
     std::vector<uint8_t> b(16);
@@ -182,6 +217,13 @@ static void test_down_layout() {
         threw = true;
     }
     CHECK(threw, "no n_ff dimension throws");
+    // MoE expert planes: standard down handled on the device, others not
+    HostTensor g = view(b, DType::Q4_K, 4096, 14336), d = view(b, DType::Q4_K, 14336, 4096);
+    HostTensor dn = view(b, DType::Q4_K, 4096, 14336), g8 = view(b, DType::Q8_0, 4096, 14336);
+    g.ne[2] = d.ne[2] = dn.ne[2] = g8.ne[2] = 8;
+    CHECK(CudaBackend::moe_supported(g, g, d), "Q4_K standard down: device MoE");
+    CHECK(!CudaBackend::moe_supported(g, g, dn), "neuron-major down: streamer");
+    CHECK(!CudaBackend::moe_supported(g8, g8, d), "Q8_0 experts: streamer");
 }
 
 static void test_upload_and_errors(CudaBackend& be) {
@@ -217,6 +259,8 @@ int main(int argc, char** argv) {
             test_down_project(be, DType::Q4_K, 1024, 512, 3);
             test_down_project(be, DType::Q8_0, 96, 4096, 9);
             test_down_project(be, DType::Q6_K, 512, 512, 2);
+            test_moe_ffn(be, 1, false);
+            test_moe_ffn(be, 37, true);
             be.sync();
             if (g_fails) {
                 std::printf("%d checks FAILED\n", g_fails);

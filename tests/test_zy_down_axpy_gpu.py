@@ -4,8 +4,8 @@ over n_in rows of N weights, zero activations skipped, y accumulated.
 Checked against the CPU oracle and, through the golden fixture, against the
 reference's own outputs.  Tolerance as in the GEMV tests: max |y - ref| /
 (|ref| + 1e-2 rms(ref)) <= 2e-3 (the GPU sums row slabs separately).  Also
-runs the C++ adapter's down_project checks (tests/cpp/test_cuda_backend.cpp
---down-project).  The file runs late in the suite, after the kernels this
+runs the C++ adapter's down_project and moe_ffn checks
+(tests/cpp/test_cuda_backend.cpp --down-project).  The file runs late in the suite, after the kernels this
 path shares (dequant, GEMV, GEMM) are checked."""
 import subprocess
 

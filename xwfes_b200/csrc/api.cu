@@ -452,6 +452,63 @@ int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int
     return ok();
 }
 
+int ftc_backend_moe_ffn(ftc_backend* be, const ftc_moe_desc* desc, const float* logits,
+                        const float* bias, const float* x, int64_t T, float* out) {
+    int rc = bind(be);
+    if (rc) return rc;
+    FTC_REQUIRE(desc && T >= 0, FTC_E_INVALID, "ftc_backend_moe_ffn: null desc or T < 0");
+    if (T == 0) return ok();
+    FTC_REQUIRE(logits && x && out, FTC_E_INVALID, "ftc_backend_moe_ffn: null pointer");
+    // the desc is checked before any of its host ranges is touched
+    if (moe_workspace_bytes(desc, T) == 0) return FTC_E_INVALID;  // message set by the check
+    FTC_REQUIRE(desc->gate_exps && desc->up_exps && desc->down_exps, FTC_E_INVALID,
+                "ftc_backend_moe_ffn: null expert tensor");
+    FTC_REQUIRE(desc->gu_row_stride >= row_bytes(FTC_Q4_K, desc->n_embd) &&
+                    desc->gu_plane_stride >= desc->n_ff * desc->gu_row_stride &&
+                    desc->dn_row_stride >= row_bytes(FTC_Q4_K, desc->n_ff) &&
+                    desc->dn_plane_stride >= desc->n_embd * desc->dn_row_stride,
+                FTC_E_INVALID, "ftc_backend_moe_ffn: row or plane stride smaller than its rows");
+    if (inject_fail("ftc_backend_moe_ffn"))
+        return set_error(FTC_E_INJECTED, "ftc_backend_moe_ffn: injected failure");
+    std::lock_guard<std::mutex> lk(be->mu);
+    ftc_moe_desc d = *desc;
+    const int64_t E = d.n_experts, K = d.n_embd;
+    const void* dev[3] = {nullptr, nullptr, nullptr};
+    const void* host[3] = {d.gate_exps, d.up_exps, d.down_exps};
+    // each tensor's extent: E - 1 whole planes and the last plane's rows
+    const size_t gu_ext = (size_t)((E - 1) * d.gu_plane_stride + d.n_ff * d.gu_row_stride);
+    const size_t dn_ext = (size_t)((E - 1) * d.dn_plane_stride + K * d.dn_row_stride);
+    const size_t bytes[3] = {gu_ext, gu_ext, dn_ext};
+    for (int i = 0; i < 3; ++i)
+        if ((rc = be->resolve(host[i], bytes[i], &dev[i]))) return rc;
+    d.gate_exps = dev[0];
+    d.up_exps = dev[1];
+    d.down_exps = dev[2];
+    const size_t wsb = moe_workspace_bytes(&d, T);
+    FTC_REQUIRE(wsb > 0, FTC_E_INVALID, "ftc_backend_moe_ffn: bad desc");
+    const size_t lb = (size_t)(T * E) * 4, lo = (lb + 255) & ~(size_t)255;
+    const size_t xb = (size_t)(T * K) * 4;
+    if ((rc = be->pin_in.ensure(lo + xb)) || (rc = be->pin_out.ensure(xb)) ||
+        (rc = be->dx.ensure(lo + xb)) || (rc = be->dy.ensure(xb)) || (rc = be->dtmp.ensure(wsb)))
+        return rc;
+    float* pl = static_cast<float*>(be->pin_in.p);
+    std::memcpy(pl, logits, lb);
+    if (bias)  // r[j] += rbias[j] before the softmax (ft/src/engine.cpp:200-201)
+        for (int64_t t = 0; t < T; ++t)
+            for (int64_t e = 0; e < E; ++e) pl[t * E + e] += bias[e];
+    std::memcpy(static_cast<uint8_t*>(be->pin_in.p) + lo, x, xb);
+    FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, lo + xb, cudaMemcpyHostToDevice, be->stream));
+    const float* dl = static_cast<const float*>(be->dx.p);
+    const void* dxp = static_cast<const uint8_t*>(be->dx.p) + lo;
+    float* dy = static_cast<float*>(be->dy.p);
+    if ((rc = moe_ffn(&d, dl, dxp, FTC_F32, T, dy, be->dtmp.p, be->dtmp.cap, be->stream))) return rc;
+    FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, xb, cudaMemcpyDeviceToHost, be->stream));
+    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    const float* po = static_cast<const float*>(be->pin_out.p);
+    for (int64_t i = 0; i < T * K; ++i) out[i] += po[i];
+    return ok();
+}
+
 int ftc_backend_sync(ftc_backend* be) {
     int rc = bind(be);
     if (rc) return rc;

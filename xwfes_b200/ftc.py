@@ -34,6 +34,7 @@ SIGNATURES = {
     "ftc_matmul_down_axpy_workspace_bytes": (C.c_size_t, [C.c_int, _i64, _i64, _i64]),
     "ftc_matmul_down_axpy": (C.c_int, [C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p,
                                        C.c_size_t, _p]),
+    "ftc_backend_moe_ffn": (C.c_int, [_p, _p, _p, _p, _p, _i64, _p]),
     "ftc_backend_sync": (C.c_int, [_p]),
     "ftc_backend_stream": (_p, [_p]),
     "ftc_backend_device_ptr": (_p, [_p, _p]),
@@ -574,6 +575,32 @@ class CudaBackend:
         check(lib().ftc_backend_matmul_down_axpy(self._h, x.ctypes.data, M, n_in, W.ptr(),
                                                  W.dtype, W.cols(), y.ctypes.data),
               "ftc_backend_matmul_down_axpy")
+
+    def moe_ffn(self, x, logits, gate_exps, up_exps, down_exps, top_k, out, bias=None):
+        """ftc_backend_moe_ffn: the routed experts of the engine's moe_ffn with
+        host arrays; gate/up/down_exps are HostTensors with ne = (n_embd, n_ff,
+        E) / (n_ff, n_embd, E) (standard down layout); ``out`` fp32 [T][n_embd]
+        is accumulated."""
+        T, K = x.shape
+        E = gate_exps.ne[2]
+        assert x.dtype == np.float32 and x.flags.c_contiguous
+        assert logits.dtype == np.float32 and logits.flags.c_contiguous and logits.shape == (T, E)
+        assert out.dtype == np.float32 and out.flags.c_contiguous and out.shape == (T, K)
+        d = MoeDesc(dtype=gate_exps.dtype, n_experts=E, top_k=top_k, n_embd=K,
+                    n_ff=gate_exps.rows(), gate_exps=gate_exps.ptr(), up_exps=up_exps.ptr(),
+                    down_exps=down_exps.ptr(), gu_row_stride=gate_exps.row_stride_bytes(),
+                    gu_plane_stride=gate_exps.slice_bytes(),
+                    dn_row_stride=down_exps.row_stride_bytes(),
+                    dn_plane_stride=down_exps.slice_bytes())
+        for t in (gate_exps, up_exps, down_exps):
+            self._keep[t.ptr()] = t
+        b = None
+        if bias is not None:
+            bias = np.ascontiguousarray(bias, dtype=np.float32)
+            assert bias.shape == (E,)
+            b = bias.ctypes.data
+        check(lib().ftc_backend_moe_ffn(self._h, C.byref(d), logits.ctypes.data, b,
+                                        x.ctypes.data, T, out.ctypes.data), "ftc_backend_moe_ffn")
 
     def run_expert_chunk(self, x, out, gate, up, down, dtype, M, K, IC, gu_stride, dn_stride):
         """IBackend::run_expert_chunk with host addresses (ints) for the

@@ -66,6 +66,8 @@ struct HostTensor {
 
     int64_t cols() const { return ne[0]; }
     int64_t rows() const { return ne[1]; }
+    int64_t dim2() const { return ne[2]; }
+    int64_t dim3() const { return ne[3]; }
     size_t row_stride_bytes() const { return dtype_row_bytes(dtype, ne[0]); }
     size_t slice_bytes() const { return row_stride_bytes() * (size_t)ne[1]; }
     const uint8_t* slice(int64_t i2, int64_t i3 = 0) const {

@@ -80,6 +80,38 @@ void CudaBackend::down_project(const float* h, int64_t M, int64_t n_ff, const Ho
     for (size_t i = 0; i < t.size(); ++i) y[i] += t[i];
 }
 
+bool CudaBackend::moe_supported(const HostTensor& g, const HostTensor& u, const HostTensor& d) {
+    const int64_t K = g.cols(), F = g.rows(), E = g.dim2();
+    return g.dtype == DType::Q4_K && u.dtype == DType::Q4_K && d.dtype == DType::Q4_K && E >= 1 &&
+           u.cols() == K && u.rows() == F && u.dim2() == E && d.dim2() == E &&
+           d.cols() == F && d.rows() == K && F != K;  // square: the reference's layout
+}
+
+bool CudaBackend::moe_ffn(const float* xn, const float* router, const std::vector<float>& rbias,
+                          int64_t M, int64_t n_expert_used, const HostTensor& gexps,
+                          const HostTensor& uexps, const HostTensor& dexps, float* tmpo) {
+    if (!moe_supported(gexps, uexps, dexps)) return false;
+    const int64_t E = gexps.dim2();
+    if (!rbias.empty() && (int64_t)rbias.size() != E)
+        throw std::runtime_error("cuda backend: moe_ffn router bias size != n_experts");
+    ftc_moe_desc d;
+    d.dtype = FTC_Q4_K;
+    d.n_experts = E;
+    d.top_k = n_expert_used < E ? n_expert_used : E;  // std::min(n_expert_used, E), :183
+    d.n_embd = gexps.cols();
+    d.n_ff = gexps.rows();
+    d.gate_exps = gexps.data;
+    d.up_exps = uexps.data;
+    d.down_exps = dexps.data;
+    d.gu_row_stride = (int64_t)gexps.row_stride_bytes();
+    d.gu_plane_stride = (int64_t)gexps.slice_bytes();
+    d.dn_row_stride = (int64_t)dexps.row_stride_bytes();
+    d.dn_plane_stride = (int64_t)dexps.slice_bytes();
+    check(ftc_backend_moe_ffn(be_, &d, router, rbias.empty() ? nullptr : rbias.data(), xn, M, tmpo),
+          "moe_ffn");
+    return true;
+}
+
 void CudaBackend::upload(const HostTensor& t) {
     const size_t n = t.nbytes ? t.nbytes
                               : t.slice_bytes() * (size_t)t.ne[2] * (size_t)t.ne[3];

@@ -8,6 +8,7 @@
 #pragma once
 
 #include <string>
+#include <vector>
 
 #include "ft/backend.h"
 #include "ft/gguf.h"
@@ -61,6 +62,22 @@ public:
     // weights go through matmul_down_axpy, OutputRows weights through matmul
     // (the dequant GEMV / GEMM of every other projection).
     void down_project(const float* h, int64_t M, int64_t n_ff, const HostTensor& W, float* y);
+
+    // The routed experts of the engine's moe_ffn (ft/src/engine.cpp:179-241)
+    // after its router matmul, on the device (ftc_backend_moe_ffn): routing
+    // with the router bias (empty: none), token grouping, the expert FFNs and
+    // the weighted combine, added into tmpo [M][n_embd].  xn [M][n_embd] and
+    // router [M][E] are the engine's host buffers; the expert tensors are the
+    // model's gate_exps / up_exps / down_exps.  Returns false, touching
+    // nothing, when moe_supported() says no (the engine then keeps its
+    // ExpertStreamer loop, whose run_expert_chunk also runs here).
+    bool moe_ffn(const float* xn, const float* router, const std::vector<float>& rbias, int64_t M,
+                 int64_t n_expert_used, const HostTensor& gexps, const HostTensor& uexps,
+                 const HostTensor& dexps, float* tmpo);
+    // Q4_K expert planes with the down projection in the standard layout
+    // (n_embd rows of n_ff weights per expert).
+    static bool moe_supported(const HostTensor& gexps, const HostTensor& uexps,
+                              const HostTensor& dexps);
 
     // Load a tensor's blocks into HBM once (call at Engine::load time).
     void upload(const HostTensor& t);
