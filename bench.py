@@ -136,6 +136,22 @@ class ClockSampler:
 
 # ------------------------------------------------------------- our path
 
+def side_measurement(name, fn, on_error):
+    """A single-GPU measurement beside the headline one: a Python-level
+    failure in it is reported in the JSON line (and on stderr) instead of
+    costing the whole line.  Not used around collectives, which every rank
+    must enter alike."""
+    try:
+        return fn()
+    except Exception as e:  # noqa: BLE001 - reported, not hidden
+        import traceback
+        traceback.print_exc()
+        err = f"{name}: {type(e).__name__}: {e}"
+        if isinstance(on_error, dict):
+            return {k: {"error": err} for k in on_error}
+        return {"error": err}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -274,7 +290,9 @@ def run_ours(args, rank, world, local_rank):
                             "GBps": round(gbytes / (us * 1e-6) / 1e9, 0)}
         del gg
 
-    decode_extras = time_decode_extras(dev, dptr, stream)
+    decode_extras = side_measurement(
+        "decode_extras", lambda: time_decode_extras(dev, dptr, stream),
+        {"q8_0_config1": None, "batched": None, "q6_k_head": None})
 
     # e2e through the C ABI: host x in, host y out, per ftc_backend_matmul call
     ext = torch.cuda.ExternalStream(be.stream(), device=dev)
@@ -300,10 +318,10 @@ def run_ours(args, rank, world, local_rank):
     h2d = N_LAYERS * sum(4 * k for _, _, k in LAYER)
     d2h = N_LAYERS * sum(4 * n for _, n, _ in LAYER)
 
-    prefill = time_prefill(dev)
+    prefill = side_measurement("prefill", lambda: time_prefill(dev), None)
     gemm_status = ftc.device_status()
     tp_block = time_tp(dev, world, rank)
-    moe = time_moe(dev) if world == 1 else None
+    moe = side_measurement("moe", lambda: time_moe(dev), None) if world == 1 else None
     ep_layer = time_ep(dev, world, rank)
 
     # max over ranks
@@ -745,6 +763,8 @@ def time_prefill(dev, reps=20, copies=4):
 
 
 def prefill_summary(prefill, status):
+    if "error" in prefill:
+        return {**prefill, "device_status": status}
     _, bf16_peak, kind = peaks()
     big = [v["tflops"] for kk, v in prefill.items() if kk.endswith("_m8192")]
     best = max(v["tflops"] for v in prefill.values())
