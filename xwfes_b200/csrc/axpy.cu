@@ -26,8 +26,15 @@ namespace {
 constexpr int kAxpyThreads = 256;  // threads per CTA at most (8 columns each)
 constexpr int kAxpyMT = 8;         // tokens per CTA at most (1, 2, 4 or 8)
 constexpr int kAxpyMaxRows = 512;  // rows per slab (activations staged in shared memory)
-constexpr int kAxpyUnroll = 4;     // rows whose bytes are in flight per thread
-constexpr int kAxpyTargetCtas = 4 * 148;
+// rows whose bytes are in flight per thread: 8 for 1-2 tokens (a warp then
+// has 8 x 144 B of one Q4_K column of blocks outstanding, ~28 KB per SM at 3
+// CTAs per SM), 4 when 4-8 tokens per byte make the kernel less
+// latency-bound and the sums need the registers
+template <int MT>
+__host__ __device__ constexpr int axpy_unroll() { return MT <= 2 ? 8 : 4; }
+// 3 CTAs per SM: what the one-token Q4_K kernel (79 registers x 256 threads)
+// keeps resident, so its grid is a single wave
+constexpr int kAxpyTargetCtas = 3 * 148;
 
 enum { kGeneric = -1 };  // element-by-element decoder (any format, any alignment)
 
@@ -240,13 +247,14 @@ __global__ void __launch_bounds__(kAxpyThreads) rows_axpy(AxpyArgs a) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) acc[t][c] = 0.f;
     const uint8_t* base = a.w + i0 * a.stride;
+    constexpr int UR = axpy_unroll<MT>();
     int r = 0;
-    for (; r + kAxpyUnroll <= nr; r += kAxpyUnroll) {
-        typename F8::Raw raw[kAxpyUnroll];
+    for (; r + UR <= nr; r += UR) {
+        typename F8::Raw raw[UR];
 #pragma unroll
-        for (int u = 0; u < kAxpyUnroll; ++u) raw[u] = F8::load(base + (int64_t)(r + u) * a.stride, j0);
+        for (int u = 0; u < UR; ++u) raw[u] = F8::load(base + (int64_t)(r + u) * a.stride, j0);
 #pragma unroll
-        for (int u = 0; u < kAxpyUnroll; ++u) {
+        for (int u = 0; u < UR; ++u) {
             float w[8];
             F8::dec(raw[u], a.dtype, j0, a.N, w);
             axpy8(acc, xs, r + u, mc, w);
