@@ -3,9 +3,12 @@
 // the extern "C" entry points.
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <map>
 #include <mutex>
+#include <set>
 #include <string>
+#include <tuple>
 
 #include "common.cuh"
 
@@ -28,6 +31,33 @@ int cuda_error(cudaError_t e, const char* what) {
 
 int ok() {
     g_last_error.clear();
+    return FTC_OK;
+}
+
+int device_sms() {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<int> sms[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+    int v = sms[dev].load(std::memory_order_relaxed);
+    if (!v) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+            return 148;
+        sms[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
+int opt_in_smem(const void* fn, int bytes, const char* what) {
+    int dev = 0;
+    FTC_CUDA(cudaGetDevice(&dev));
+    static std::mutex mu;
+    static std::set<std::tuple<const void*, int, int>> done;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count(std::make_tuple(fn, dev, bytes))) return FTC_OK;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return cuda_error(e, what);
+    done.insert(std::make_tuple(fn, dev, bytes));
     return FTC_OK;
 }
 

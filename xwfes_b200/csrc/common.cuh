@@ -30,6 +30,14 @@ int ok();
         if (!(cond)) return ::ftc::set_error((code), (msg));      \
     } while (0)
 
+// Multiprocessor count of the current device (cached per device).
+int device_sms();
+
+// Lets kernel `fn` use `bytes` of dynamic shared memory on the current
+// device.  The attribute belongs to the device's context, so it is set once
+// per (kernel, device, size), not once per process.
+int opt_in_smem(const void* fn, int bytes, const char* what);
+
 // Host-side fault injection: when the environment variable FTC_INJECT_FAIL
 // names an entry point (or "all"), that entry point returns FTC_E_INJECTED
 // before launching anything.  Used by the failure-path tests; no GPU fault.

@@ -719,13 +719,9 @@ template <class C, typename OP>
 int launch(const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx, int M, int N, int K,
            void* y, int ytype, const GemmGroups& grp, int64_t max_units, int sms,
            cudaStream_t st) {
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc<C, OP>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm_q4k_tc)");
-        configured = true;
-    }
+    const int rc = opt_in_smem(reinterpret_cast<const void*>(gemm_q4k_tc<C, OP>), C::SMEM,
+                               "cudaFuncSetAttribute(gemm_q4k_tc)");
+    if (rc) return rc;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_units, sms));
     gemm_q4k_tc<C, OP><<<grid, C::THREADS, C::SMEM, st>>>(tw, tw2, tx, M, N, K, y, ytype, grp);
     return FTC_OK;
@@ -786,15 +782,6 @@ struct SplitScratch {
 
 std::mutex g_split_mu;
 SplitScratch g_split[64];  // per device
-
-int device_sms() {
-    static int sms[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) dev = 0;
-    if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    return sms[dev] > 0 ? sms[dev] : 148;
-}
 
 // The device's split-K scratch, allocated on first use (never freed, never
 // moved: graphs that captured its address stay valid).  Inside a stream

@@ -563,8 +563,7 @@ bool plan_q4k(int64_t Ntot, int64_t K, int64_t stride, Q4kPlan& p) {
     p.WK = (nsb + 7) / 8;
     if (p.WK > 15) return false;
     p.WR = std::max(1, (kMaxThreads / 32 - 1) / p.WK);  // consumer warps + 1 producer
-    static int sms = 0;
-    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int sms = device_sms();
     // rows per chunk: ~48 KB chunks, but small enough that every SM gets two
     int64_t rc = std::max<int64_t>(1, 49152 / stride + p.WR / 2);
     rc = std::min<int64_t>(rc, std::max<int64_t>(p.WR, Ntot / (2 * (int64_t)sms)));
@@ -631,8 +630,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     if (g.x_up < 0 || g.x_up % 4) return FTC_E_UNSUPPORTED;  // up half 16-byte aligned
     Q4kPlan p;
     if (!plan_q4k(ntot, g.K, g.stride, p)) return FTC_E_UNSUPPORTED;
-    static int sms = 0;
-    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int sms = device_sms();
     const int RC = balance_rc(P, g.N, p.RPW * p.WR, sms);
     GemvBatch B = {};
     B.P = P;
@@ -692,14 +690,10 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     }
     const int nsb = (int)(g.K / 256);
     // opt in to large dynamic shared memory once per instantiation
-    static bool configured[6] = {false, false, false, false, false, false};
-    auto launch = [&](auto kern, int idx) -> int {
-        if (!configured[idx]) {
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)kMaxSmem);
-            if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemv_q4k_dp4a)");
-            configured[idx] = true;
-        }
+    auto launch = [&](auto kern, int) -> int {
+        const int orc = opt_in_smem(reinterpret_cast<const void*>(kern), (int)kMaxSmem,
+                                    "cudaFuncSetAttribute(gemv_q4k_dp4a)");
+        if (orc) return orc;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(p.grid);
         cfg.blockDim = dim3(p.threads);

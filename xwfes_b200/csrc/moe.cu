@@ -277,8 +277,7 @@ __global__ void moe_silu_f32(const float* __restrict__ gu, int rows, int n_ff,
 }
 
 int grid_for(int64_t n) {
-    static int sms = 0;
-    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int sms = device_sms();
     return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8));
 }
 
@@ -452,13 +451,10 @@ int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dty
                           2 * (int64_t)F, st);
     if (rc) return rc;
     {
-        static bool configured = false;
         const size_t smem = (size_t)F * 4;
-        if (!configured) {
-            FTC_CUDA(cudaFuncSetAttribute(moe_silu_scale, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)(kMaxFf * 4)));
-            configured = true;
-        }
+        if ((rc = opt_in_smem(reinterpret_cast<const void*>(moe_silu_scale), (int)(kMaxFf * 4),
+                              "cudaFuncSetAttribute(moe_silu_scale)")))
+            return rc;
         moe_silu_scale<<<R, 512, smem, st>>>(gu, xs, F, h, hs);
         FTC_CUDA(cudaGetLastError());
     }
@@ -560,12 +556,9 @@ int moe_experts(const ftc_moe_desc* d, const void* x, int x_dtype, int64_t rows,
                           d->gu_row_stride, xg, FTC_F16, R, counts, offsets, mr, gu, FTC_F32,
                           2 * (int64_t)F, st);
     if (rc) return rc;
-    static bool configured = false;
-    if (!configured) {
-        FTC_CUDA(cudaFuncSetAttribute(moe_silu_scale, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)(kMaxFf * 4)));
-        configured = true;
-    }
+    if ((rc = opt_in_smem(reinterpret_cast<const void*>(moe_silu_scale), (int)(kMaxFf * 4),
+                          "cudaFuncSetAttribute(moe_silu_scale)")))
+        return rc;
     moe_silu_scale<<<R, 512, (size_t)F * 4, st>>>(gu, xs, F, h, hs);
     FTC_CUDA(cudaGetLastError());
     // down projection; the epilogue undoes h's row scales (exact)

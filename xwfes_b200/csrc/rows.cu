@@ -118,19 +118,15 @@ int silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h
                 "ftc_silu_mul_rows: fp16 rows need an even n and 4-byte alignment");
     if (rows == 0) return FTC_OK;
     if (h) {
-        static int sms = 0;
-        if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+        const int sms = device_sms();
         const int64_t total = rows * n;
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8));
         silu_mul_rows_f32<<<grid, 256, 0, st>>>(gu, ld, rows, (int)n, h);
     } else if (n <= kSiluCacheMax) {
-        static bool configured = false;
-        if (!configured) {
-            FTC_CUDA(cudaFuncSetAttribute(silu_mul_rows_f16<true>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kSiluCacheMax * (int)sizeof(float)));
-            configured = true;
-        }
+        const int orc = opt_in_smem(reinterpret_cast<const void*>(silu_mul_rows_f16<true>),
+                                    kSiluCacheMax * (int)sizeof(float),
+                                    "cudaFuncSetAttribute(silu_mul_rows_f16)");
+        if (orc) return orc;
         silu_mul_rows_f16<true><<<(int)rows, 1024, (size_t)n * sizeof(float), st>>>(
             gu, ld, (int)n, static_cast<__half*>(out16), row_exp);
     } else {
@@ -167,8 +163,7 @@ int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld,
 int silu_mul(const float* g, const float* u, int64_t n, float* h, cudaStream_t st) {
     FTC_REQUIRE(g && u && h && n >= 0, FTC_E_INVALID, "ftc_silu_mul: bad argument");
     if (n == 0) return FTC_OK;
-    static int sms = 0;
-    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int sms = device_sms();
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8));
     silu_mul_kernel<<<grid, 256, 0, st>>>(g, u, n, h);
     FTC_CUDA(cudaGetLastError());
