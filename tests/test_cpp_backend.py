@@ -29,6 +29,21 @@ def compile_test(out):
     return out
 
 
+# the reference tree's headers, where the reference is checked out (CPU-only check)
+REF_INCLUDE = os.environ.get("FT_REF_INCLUDE", "/root/reference/ft-igpu-src/include")
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_INCLUDE), reason="reference tree not present")
+def test_adapter_compiles_against_reference_headers():
+    """cuda_backend.cpp drops into the reference tree as is: it compiles
+    against the reference's own, unmodified ft/ headers (C++20, as its
+    CMake build)."""
+    r = subprocess.run(["g++", "-std=c++20", "-Wall", "-fsyntax-only", "-I", REF_INCLUDE,
+                        "-I", HOST, "-I", os.path.join(ROOT, "include"),
+                        os.path.join(HOST, "cuda_backend.cpp")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
 def test_adapter_compiles(tmp_path):
     assert os.path.exists(compile_test(str(tmp_path / "test_cuda_backend")))
 

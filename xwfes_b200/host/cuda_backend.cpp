@@ -82,7 +82,10 @@ void CudaBackend::down_project(const float* h, int64_t M, int64_t n_ff, const Ho
 
 bool CudaBackend::moe_supported(const HostTensor& g, const HostTensor& u, const HostTensor& d) {
     const int64_t K = g.cols(), F = g.rows(), E = g.dim2();
-    return g.dtype == DType::Q4_K && u.dtype == DType::Q4_K && d.dtype == DType::Q4_K && E >= 1 &&
+    // type ids compared as GGML ids: the reference's own DType has no Q4_K
+    // member until the K-quants are added to it
+    const auto q4k = [](const HostTensor& t) { return (int)t.dtype == FTC_Q4_K; };
+    return q4k(g) && q4k(u) && q4k(d) && E >= 1 &&
            u.cols() == K && u.rows() == F && u.dim2() == E && d.dim2() == E &&
            d.cols() == F && d.rows() == K && F != K;  // square: the reference's layout
 }
