@@ -85,15 +85,18 @@ bool CudaBackend::moe_supported(const HostTensor& g, const HostTensor& u, const 
     // type ids compared as GGML ids: the reference's own DType has no Q4_K
     // member until the K-quants are added to it
     const auto q4k = [](const HostTensor& t) { return (int)t.dtype == FTC_Q4_K; };
-    return q4k(g) && q4k(u) && q4k(d) && E >= 1 &&
-           u.cols() == K && u.rows() == F && u.dim2() == E && d.dim2() == E &&
+    // shapes the device MoE takes (ftc_moe_ffn): 1..256 experts, K and n_ff
+    // whole super-blocks, n_ff <= 49152
+    return q4k(g) && q4k(u) && q4k(d) && E >= 1 && E <= 256 && K % 256 == 0 && F % 256 == 0 &&
+           F <= 49152 && u.cols() == K && u.rows() == F && u.dim2() == E && d.dim2() == E &&
            d.cols() == F && d.rows() == K && F != K;  // square: the reference's layout
 }
 
 bool CudaBackend::moe_ffn(const float* xn, const float* router, const std::vector<float>& rbias,
                           int64_t M, int64_t n_expert_used, const HostTensor& gexps,
                           const HostTensor& uexps, const HostTensor& dexps, float* tmpo) {
-    if (!moe_supported(gexps, uexps, dexps)) return false;
+    if (!moe_supported(gexps, uexps, dexps) || n_expert_used < 1 || n_expert_used > 8)
+        return false;
     const int64_t E = gexps.dim2();
     if (!rbias.empty() && (int64_t)rbias.size() != E)
         throw std::runtime_error("cuda backend: moe_ffn router bias size != n_experts");

@@ -75,7 +75,9 @@ public:
                  int64_t n_expert_used, const HostTensor& gexps, const HostTensor& uexps,
                  const HostTensor& dexps, float* tmpo);
     // Q4_K expert planes with the down projection in the standard layout
-    // (n_embd rows of n_ff weights per expert).
+    // (n_embd rows of n_ff weights per expert), 1..256 experts, n_embd and
+    // n_ff multiples of 256, n_ff <= 49152.  moe_ffn also needs
+    // 1 <= n_expert_used <= 8.
     static bool moe_supported(const HostTensor& gexps, const HostTensor& uexps,
                               const HostTensor& dexps);
 
