@@ -123,12 +123,25 @@ def flops(d, M):
 
 
 class CudaOps:
-    """The block's matmuls on this GPU through the library's kernels."""
+    """The block's matmuls on this GPU through the library's kernels: up to
+    ``gemv_max_m`` rows through the fp32 decode GEMV (8 rows per pass over
+    the weight), more through the tcgen05 GEMM on row-scaled fp16 operands."""
 
-    def __init__(self, device):
+    def __init__(self, device, gemv_max_m=8):
         import torch
         from . import ftc
         self.torch, self.ftc, self.device = torch, ftc, device
+        self.gemv_max_m = max(8, int(gemv_max_m))
+
+    def _gemv_rows(self, x, w, n, k):
+        """x . W^T for M <= gemv_max_m rows, 8 rows per GEMV launch."""
+        M = x.shape[0]
+        if M <= 8:
+            return self.ftc.mul_mat_vec(w, F.Q4_K, n, k, x)
+        y = self.torch.empty((M, n), dtype=self.torch.float32, device=x.device)
+        for m0 in range(0, M, 8):
+            self.ftc.mul_mat_vec(w, F.Q4_K, n, k, x[m0:m0 + 8], y=y[m0:m0 + 8])
+        return y
 
     def upload(self, arr):
         return self.torch.from_numpy(arr).to(self.device)
@@ -138,11 +151,11 @@ class CudaOps:
         ``peer`` (one token) the product is also summed over the ranks."""
         ftc, M = self.ftc, gu.shape[0]
         wt, wn, wk = w
-        if M <= 8:
+        if M <= self.gemv_max_m:
             h = ftc.silu_mul_rows(gu, n)
             if peer is not None:
                 return peer.mul_mat_vec_sum(wt, F.Q4_K, wn, wk, h)
-            return ftc.mul_mat_vec(wt, F.Q4_K, wn, wk, h)
+            return self._gemv_rows(h, wt, wn, wk)
         x16, e = ftc.silu_mul_rows(gu, n, to_f16=True)
         return ftc.gemm_rowscaled(wt, F.Q4_K, wn, wk, x16, e)
 
@@ -161,6 +174,9 @@ class CudaOps:
                 w, n, _ = ws[0]
                 return [ftc.mul_mat_vec(w, F.Q4_K, n, k, x)]
             return ftc.mul_mat_vec_multi([w for w, _, _ in ws], F.Q4_K, [n for _, n, _ in ws], k, x)
+        if M <= self.gemv_max_m:
+            x = x.contiguous()
+            return [self._gemv_rows(x, w, n, k) for w, n, _ in ws]
         x16, e = ftc.rows_to_f16(x)
         return [ftc.gemm_rowscaled(w, F.Q4_K, n, k, x16, e) for w, n, _ in ws]
 
