@@ -179,6 +179,19 @@ struct ftc_backend {
     DevBuf dx, dy, dwin, dtmp;
     std::mutex mu;
 
+    // ftc_backend_matmul's per-call work (copy in, GEMV or GEMM, copy out)
+    // captured once per (weight, shape) and replayed as a CUDA graph: one
+    // launch instead of three to six API calls.  On with
+    // FTC_BACKEND_GRAPHS=1 at creation.  The graphs hold the staging
+    // buffers' addresses, so all of them are dropped when a buffer moves.
+    bool use_graphs = false;
+    std::map<std::tuple<const void*, int64_t, int64_t, int64_t, int>, cudaGraphExec_t> graphs;
+    void* graph_bufs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    void drop_graphs() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        graphs.clear();
+    }
+
     // Cached entry that fully covers [p, p + n), or nullptr.
     const CacheEntry* find(const void* p, size_t n) const {
         const uintptr_t a = (uintptr_t)p;
@@ -253,6 +266,8 @@ int ftc_backend_create(int device, ftc_backend** out) {
                 "ftc_backend_create: libftcuda is built for sm_100a (B200) only");
     ftc_backend* be = new ftc_backend();
     be->device = device;
+    const char* g = std::getenv("FTC_BACKEND_GRAPHS");
+    be->use_graphs = g && std::strcmp(g, "1") == 0;
     be->name = std::string("CUDA:") + prop.name;
     be->mem = prop.totalGlobalMem;
     cudaError_t e = cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking);
@@ -268,6 +283,7 @@ void ftc_backend_destroy(ftc_backend* be) {
     if (!be) return;
     cudaSetDevice(be->device);
     if (be->stream) cudaStreamSynchronize(be->stream);
+    be->drop_graphs();
     for (auto& kv : be->cache) cudaFree(kv.second.dev);
     be->pin_in.release();
     be->pin_out.release();
@@ -307,6 +323,7 @@ int ftc_backend_evict(ftc_backend* be, const void* host) {
     auto it = be->cache.find((uintptr_t)host);
     FTC_REQUIRE(it != be->cache.end(), FTC_E_INVALID, "ftc_backend_evict: range not cached");
     FTC_CUDA(cudaStreamSynchronize(be->stream));
+    be->drop_graphs();  // they may read the evicted copy
     cudaFree(it->second.dev);
     be->cached -= it->second.nbytes;
     be->cache.erase(it);
@@ -356,25 +373,57 @@ int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K, co
     const size_t x16b = tc ? ((size_t)(M * K) * 2 + 255) & ~(size_t)255 : 0;
     if (tc && (rc = be->dtmp.ensure(x16b + (size_t)M * 4))) return rc;
     std::memcpy(be->pin_in.p, x, xb);
-    FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, xb, cudaMemcpyHostToDevice, be->stream));
     const float* dx = static_cast<const float*>(be->dx.p);
     float* dy = static_cast<float*>(be->dy.p);
-    if (tc) {
-        void* x16 = be->dtmp.p;
-        int32_t* row_exp = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(be->dtmp.p) + x16b);
-        if ((rc = rows_to_f16(dx, FTC_F32, M, K, K, x16, row_exp, be->stream)) ||
-            (rc = gemm_q4k_rowscaled(dW, N, K, stride, x16, M, dy, FTC_F32, row_exp, be->stream)))
-            return rc;
-    } else {
-        for (int64_t m0 = 0; m0 < M; m0 += 8) {
-            const int64_t mc = M - m0 < 8 ? M - m0 : 8;
-            if ((rc = mul_mat_vec(dtype, dW, N, K, stride, dx + m0 * K, mc, dy + m0 * N,
-                                  be->stream)))
-                return rc;
+    cudaStream_t st = be->stream;
+    auto enqueue = [&]() -> int {
+        FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, xb, cudaMemcpyHostToDevice, st));
+        int erc;
+        if (tc) {
+            void* x16 = be->dtmp.p;
+            int32_t* row_exp = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(be->dtmp.p) + x16b);
+            if ((erc = rows_to_f16(dx, FTC_F32, M, K, K, x16, row_exp, st)) ||
+                (erc = gemm_q4k_rowscaled(dW, N, K, stride, x16, M, dy, FTC_F32, row_exp, st)))
+                return erc;
+        } else {
+            for (int64_t m0 = 0; m0 < M; m0 += 8) {
+                const int64_t mc = M - m0 < 8 ? M - m0 : 8;
+                if ((erc = mul_mat_vec(dtype, dW, N, K, stride, dx + m0 * K, mc, dy + m0 * N, st)))
+                    return erc;
+            }
         }
+        FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, st));
+        return FTC_OK;
+    };
+    if (be->use_graphs) {
+        void* bufs[5] = {be->pin_in.p, be->pin_out.p, be->dx.p, be->dy.p, be->dtmp.p};
+        if (std::memcmp(bufs, be->graph_bufs, sizeof(bufs)) != 0) {
+            be->drop_graphs();
+            std::memcpy(be->graph_bufs, bufs, sizeof(bufs));
+        }
+        const auto key = std::make_tuple(dW, M, K, N, dtype);
+        auto it = be->graphs.find(key);
+        if (it == be->graphs.end()) {
+            // relaxed: a kernel's first launch may set its shared-memory attribute
+            FTC_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+            const int erc = enqueue();
+            cudaGraph_t g = nullptr;
+            const cudaError_t ce = cudaStreamEndCapture(st, &g);
+            if (erc || ce != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                return erc ? erc : cuda_error(ce, "ftc_backend_matmul: graph capture");
+            }
+            cudaGraphExec_t ex = nullptr;
+            const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+            cudaGraphDestroy(g);
+            if (ie != cudaSuccess) return cuda_error(ie, "ftc_backend_matmul: graph instantiate");
+            it = be->graphs.emplace(key, ex).first;
+        }
+        FTC_CUDA(cudaGraphLaunch(it->second, st));
+    } else if ((rc = enqueue())) {
+        return rc;
     }
-    FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, be->stream));
-    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    FTC_CUDA(cudaStreamSynchronize(st));
     std::memcpy(y, be->pin_out.p, yb);
     return ok();
 }
