@@ -317,6 +317,9 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
     h2d = N_LAYERS * sum(4 * k for _, _, k in LAYER)
     d2h = N_LAYERS * sum(4 * n for _, n, _ in LAYER)
+    e2e_graphs = side_measurement(
+        "e2e_graph_replay",
+        lambda: time_e2e_graphs(dev, local_rank, hosts, xs_host, e2e_steps, step_bytes), None)
 
     prefill = side_measurement("prefill", lambda: time_prefill(dev), None)
     gemm_status = ftc.device_status()
@@ -391,6 +394,7 @@ def run_ours(args, rank, world, local_rank):
         "decode_batched": decode_extras["batched"],
         "q6_k_head": decode_extras["q6_k_head"],
         "q8_0_config1": decode_extras["q8_0_config1"],
+        "e2e_graph_replay": e2e_graphs,
         "prefill_dequant_gemm": prefill_summary(prefill, gemm_status),
         "tp_block": tp_block,
         "moe": moe,
@@ -400,6 +404,51 @@ def run_ours(args, rank, world, local_rank):
         "setup_s": round(setup_s, 1),
     }
     return line
+
+
+def time_e2e_graphs(dev, local_rank, hosts, xs_host, steps, step_bytes):
+    """The e2e pass through a second backend created with FTC_BACKEND_GRAPHS=1
+    (each ftc_backend_matmul replays a cached CUDA graph of its copy-in,
+    GEMV and copy-out): same calls, same host buffers, weights uploaded to
+    its own cache first."""
+    import torch
+    from xwfes_b200 import ftc
+    old = os.environ.get("FTC_BACKEND_GRAPHS")
+    os.environ["FTC_BACKEND_GRAPHS"] = "1"
+    try:
+        be = ftc.CudaBackend(local_rank)
+    finally:
+        if old is None:
+            os.environ.pop("FTC_BACKEND_GRAPHS", None)
+        else:
+            os.environ["FTC_BACKEND_GRAPHS"] = old
+    try:
+        for T in hosts.values():
+            be.upload(T)
+        yh = {name: np.empty((1, n), dtype=np.float32) for name, n, _ in LAYER}
+
+        def step():
+            for li in range(N_LAYERS):
+                for name, n, k in LAYER:
+                    be.matmul(xs_host[X_OF[name]], 1, k, hosts[(li, name)], yh[name])
+
+        for _ in range(3):  # the first pass captures the graphs
+            step()
+        ext = torch.cuda.ExternalStream(be.stream(), device=dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(ext)
+        for _ in range(steps):
+            step()
+        ev1.record(ext)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / steps
+        return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(ms, 4), "steps": steps,
+                "api": "ftc_backend_matmul with FTC_BACKEND_GRAPHS=1 (one cached CUDA graph "
+                       "launch per call), pinned staging, sync per call"}
+    finally:
+        be.close()
 
 
 def time_decode_extras(dev, dptr, stream, reps=20):
