@@ -265,7 +265,10 @@ int ftc_peer_ar_open(ftc_peer_ar* ar, const void* handles) {
             const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
             if (e != cudaSuccess) {
                 for (int j = 0; j < q; ++j)
-                    if (ar->peer_base[j]) cudaIpcCloseMemHandle(ar->peer_base[j]);
+                    if (ar->peer_base[j]) {
+                        cudaIpcCloseMemHandle(ar->peer_base[j]);
+                        ar->peer_base[j] = nullptr;  // destroy must not close it again
+                    }
                 return cuda_error(e, "ftc_peer_ar_open: cudaIpcOpenMemHandle");
             }
             ar->peer_base[q] = p;

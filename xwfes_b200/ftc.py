@@ -662,7 +662,10 @@ class PeerAllreduce:
     def _agree(self, errs, step):
         bad = [(r, e) for r, e in enumerate(errs) if e is not None]
         if bad:
-            self.close()
+            try:
+                self.close()
+            except FtcError:
+                self._ar = None  # the set-up failure is the error to report
             raise RuntimeError(f"PeerAllreduce: {step} failed on rank(s) "
                                + "; ".join(f"{r}: {e}" for r, e in bad))
 
