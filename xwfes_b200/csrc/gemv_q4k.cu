@@ -689,7 +689,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
         p.grid = B.cta_first[P];
     }
     const int nsb = (int)(g.K / 256);
-    // opt in to large dynamic shared memory once per instantiation
+    // opt in to large dynamic shared memory once per instantiation and device
     auto launch = [&](auto kern, int) -> int {
         const int orc = opt_in_smem(reinterpret_cast<const void*>(kern), (int)kMaxSmem,
                                     "cudaFuncSetAttribute(gemv_q4k_dp4a)");
