@@ -110,3 +110,41 @@ def test_a_failed_mapping_stops_every_rank(tmp_path):
     for r, x in enumerate(res):
         assert "ftc_peer_ar_open failed on rank(s) 0" in x["error"]
         assert [c[0] for c in x["log"]] == ["create", "open", "destroy"]
+
+
+class RecordingLib:
+    """Records the arguments of the fused GEMV entries."""
+
+    def __init__(self):
+        self.args = None
+
+    def ftc_mul_mat_vec_silu(self, *a):
+        self.args = a
+        return 0
+
+    def ftc_row_bytes(self, t, k):
+        return (k // 256) * 144
+
+    def ftc_last_error(self):
+        return b""
+
+
+def test_fused_silu_binding_passes_offsets_and_buffer(monkeypatch):
+    from xwfes_b200 import formats as F, ftc
+    rec = RecordingLib()
+    monkeypatch.setattr(ftc, "_lib", rec)
+    w = torch.zeros(64, dtype=torch.uint8)
+    gu = torch.zeros((1, 2 * 512 + 64), dtype=torch.float32)
+    y = torch.zeros((1, 8), dtype=torch.float32)
+    ftc.mul_mat_vec_silu(w, F.Q4_K, 8, 512, gu, up_offset=576, y=y, stream=0)
+    ar_, t, wp, n, k, rs, gp, off, yp, st = rec.args
+    assert ar_ is None and t == F.Q4_K and (n, k, rs, off) == (8, 512, 288, 576)
+    assert (wp, gp, yp) == (w.data_ptr(), gu.data_ptr(), y.data_ptr())
+    ftc.mul_mat_vec_silu(w, F.Q4_K, 8, 512, gu, y=y, stream=0)
+    assert rec.args[7] == 512  # up half right after the gate half by default
+
+    class FakeAr:
+        _ar = 0x1234
+
+    ftc.mul_mat_vec_silu(w, F.Q4_K, 8, 512, gu, y=y, ar=FakeAr(), stream=0)
+    assert rec.args[0] == 0x1234
