@@ -35,6 +35,16 @@ def test_every_declared_symbol_is_exported(lib):
     assert set(syms) == set(ftc.SIGNATURES), "ctypes signatures out of sync with include/ftc.h"
 
 
+@pytest.mark.parametrize("lang,std", [("c", "-std=c99"), ("c++", "-std=c++17")])
+def test_header_compiles_as_c_and_cpp(lang, std):
+    """include/ftc.h is a plain C header (an FFI binding or a C engine can
+    include it), warning-free in C and C++."""
+    cc = "gcc" if lang == "c" else "g++"
+    r = subprocess.run([cc, "-x", lang, std, "-Wall", "-Wextra", "-Werror", "-fsyntax-only",
+                        os.path.join(ROOT, "include", "ftc.h")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
 def test_row_bytes_matches_formats(lib):
     for t in (F.F32, F.F16, F.BF16, F.Q4_0, F.Q4_1, F.Q8_0, F.Q4_K, F.Q6_K):
         for k in (256, 4096, 14336):
