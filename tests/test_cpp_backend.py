@@ -16,7 +16,8 @@ def compile_test(out):
     if not os.path.exists(ftc.LIB_PATH):
         build.build()
     O.lib()  # builds oracle/liboracle.so if needed
-    cmd = ["g++", "-std=c++17", "-O2", "-I", os.path.join(HOST, "compat"), "-I", HOST,
+    cmd = ["g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-Werror",
+           "-I", os.path.join(HOST, "compat"), "-I", HOST,
            "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "oracle"),
            os.path.join(ROOT, "tests", "cpp", "test_cuda_backend.cpp"),
            os.path.join(HOST, "cuda_backend.cpp"), os.path.join(HOST, "gguf.cpp"),
