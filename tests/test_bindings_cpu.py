@@ -2,7 +2,6 @@
 the CPU with a stand-in for libftcuda.so: the MoE descriptor built from the
 expert HostTensors, the router bias, the down projection's shapes and its
 workspace request."""
-import ctypes as C
 
 import numpy as np
 import pytest
