@@ -23,6 +23,7 @@ For N>1 every rank runs the same workload on its own GPU (replicas; the
 decode GEMV does not shard): value = sum over ranks, time = max over ranks.
 """
 import argparse
+import atexit
 import json
 import os
 import statistics
@@ -42,6 +43,12 @@ METRIC = "Q4_K dequant-GEMV HBM GB/s (% of peak) & prefill dequant-GEMM TFLOPS"
 LAYER = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
          ("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)]
 N_LAYERS = 8
+# the workload both arms report (the reference arm times a bounded sample of it)
+CONFIG = {
+    "workload": "config 2: Q4_K decode GEMV, Llama-3-8B layer shapes (q,k,v,o 4096/1024x4096; "
+                "gate,up 14336x4096; down 4096x14336), batch 1, fp32 activations",
+    "l2": "inputs larger than L2: each GPU step streams 8 distinct layer copies (982 MB)",
+}
 # activation vector each GEMV reads (q/k/v share one, gate/up share one)
 X_OF = {"q": "attn_in", "k": "attn_in", "v": "attn_in", "o": "attn_out", "gate": "ffn_in",
         "up": "ffn_in", "down": "ffn_mid"}
@@ -75,9 +82,13 @@ def make_weights(seed=0):
 # ------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi samples (every 100 ms) of one GPU's clocks and throttle
-    reasons while the timed region runs; the GPU is picked by PCI bus id."""
-    Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples (every 100 ms) of one GPU's clocks, power, load and
+    throttle reasons over the whole measured run; the GPU is picked by its
+    PCI bus id (nvidia-smi's domain:bus:device.function form).  The summary
+    keeps the samples taken under load (utilization >= 50 %), so a timed
+    region shorter than the sampling period is still covered by the kernels
+    around it that run the same code."""
+    Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -85,6 +96,16 @@ class ClockSampler:
         self.bus = (bus_id or "").lower()
         self.lines = []
         self.proc = None
+
+    @staticmethod
+    def bus_id_of(props):
+        """nvidia-smi's bus id string of a torch device (e.g. 00000000:1b:00.0)."""
+        dom = getattr(props, "pci_domain_id", None)
+        bus = getattr(props, "pci_bus_id", None)
+        devn = getattr(props, "pci_device_id", None)
+        if bus is None or devn is None:
+            return ""
+        return f"{dom or 0:08x}:{bus:02x}:{devn:02x}.0"
 
     def __enter__(self):
         try:
@@ -102,36 +123,44 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
+        proc, self.proc = self.proc, None
+        if proc:
+            proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
+                proc.kill()
             self.t.join(timeout=5)
 
     def summary(self):
-        sm, mx, pw, reasons = [], None, [], set()
+        sm, mx, pw, reasons, n_all = [], None, [], set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         rows = [[v.strip() for v in ln.split(",")] for ln in self.lines]
         rows = [f for f in rows if len(f) >= 9]
-        mine = [f for f in rows if self.bus and f[0].lower().endswith(self.bus)]
+        mine = [f for f in rows if self.bus and f[0].lower().endswith(self.bus[-12:])]
+        matched = bool(mine)
         if not mine and rows:  # bus id unknown: the first GPU listed
             first = rows[0][0]
             mine = [f for f in rows if f[0] == first]
         for f in mine:
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-                pw.append(float(f[3]))
+                clk, mxc, p, util = float(f[1]), float(f[2]), float(f[3]), float(f[4])
             except ValueError:
                 continue
+            n_all += 1
+            mx = mxc
+            if util < 50:
+                continue
+            sm.append(clk)
+            pw.append(p)
             for nm, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "power_w_median": statistics.median(pw) if pw else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "samples_all": n_all,
+                "gpu": self.bus if matched else "unmatched (first GPU listed)",
+                "window": "whole run (set-up excluded), samples with utilization >= 50 %"}
 
 
 # ------------------------------------------------------------- our path
@@ -160,6 +189,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     be = ftc.CudaBackend(local_rank)
+    clk = ClockSampler(ClockSampler.bus_id_of(torch.cuda.get_device_properties(dev)))
 
     t0 = time.time()
     layers = make_weights(seed=0)
@@ -216,6 +246,8 @@ def run_ours(args, rank, world, local_rank):
             launch(*key, s, nxt=order[(i + 1) % len(order)])
 
     sp = stream.cuda_stream
+    clk.__enter__()
+    atexit.register(clk.__exit__, None, None, None)  # also on an error path
     with torch.cuda.stream(stream):
         step(sp)  # eager warm-up outside capture
     torch.cuda.synchronize()
@@ -238,10 +270,7 @@ def run_ours(args, rank, world, local_rank):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    props = torch.cuda.get_device_properties(dev)
-    bus = getattr(props, "pci_bus_id", None)
-    smi_id = f"{bus:02x}:{getattr(props, 'pci_device_id', 0):02x}.0" if bus is not None else ""
-    with ClockSampler(smi_id) as clk, torch.cuda.stream(stream):
+    with torch.cuda.stream(stream):
         ev0.record(stream)
         for _ in range(args.steps):
             graph.replay()  # replays on the current stream == `stream`
@@ -305,7 +334,7 @@ def run_ours(args, rank, world, local_rank):
 
     for _ in range(3):
         e2e_step()
-    e2e_steps = max(3, args.steps // 50)
+    e2e_steps = max(20, min(args.steps, 200))
     barrier()
     torch.cuda.synchronize()
     ev0.record(ext)
@@ -326,6 +355,7 @@ def run_ours(args, rank, world, local_rank):
     tp_block = time_tp(dev, world, rank)
     moe = side_measurement("moe", lambda: time_moe(dev), None) if world == 1 else None
     ep_layer = time_ep(dev, world, rank)
+    clk.__exit__(None, None, None)
 
     # max over ranks
     t = torch.tensor([ms, e2e_ms, k_ms], device=dev, dtype=torch.float64)
@@ -338,6 +368,7 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return None
     hbm, _, peak_kind = peaks()
+    prefill_sum = prefill_summary(prefill, gemm_status)
     gbs = step_bytes * world / (ms * 1e-3) / 1e9
     k_gbs = k_bytes / (k_ms * 1e-3) / 1e9
     line = {
@@ -353,12 +384,10 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded Q4_K blocks and N(0,1) fp32 activations, config 2 distributions)",
-        "config": {
-            "workload": "config 2: Q4_K decode GEMV, Llama-3-8B layer shapes "
-                        "(q,k,v,o 4096/1024x4096; gate,up 14336x4096; down 4096x14336), batch 1",
+        "config": CONFIG,
+        "step": {
             "layers_per_step": N_LAYERS,
             "bytes_per_step": step_bytes,
-            "l2": "inputs larger than L2: 8 distinct layer copies (982 MB) per step",
             "parallelism": f"replicas x{world}",
             "graph": "CUDA graph of the step: 8 layers x 4 launches (q/k/v grouped, o, "
                      "gate/up grouped, down), programmatic dependent launch between them; "
@@ -381,7 +410,9 @@ def run_ours(args, rank, world, local_rank):
             "bytes_per_launch": k_bytes,
             "per_group": per_group,
             "us_per_launch": round(k_ms * 1e3, 3),
+            "prefill_gemm": gemm_roofline(prefill_sum, short=True),
         },
+        "roofline_gemm": gemm_roofline(prefill_sum),
         "e2e": {
             "value": round(step_bytes / (e2e_ms * 1e-3) / 1e9 * world, 2),
             "unit": "GB/s",
@@ -395,7 +426,7 @@ def run_ours(args, rank, world, local_rank):
         "q6_k_head": decode_extras["q6_k_head"],
         "q8_0_config1": decode_extras["q8_0_config1"],
         "e2e_graph_replay": e2e_graphs,
-        "prefill_dequant_gemm": prefill_summary(prefill, gemm_status),
+        "prefill_dequant_gemm": prefill_sum,
         "tp_block": tp_block,
         "moe": moe,
         "ep_moe": ep_layer,
@@ -826,6 +857,42 @@ def prefill_summary(prefill, status):
             "dtype": "bf16 x bf16(dequantized Q4_K) -> fp32 accumulate -> bf16"}
 
 
+def gemm_roofline(prefill_sum, short=False):
+    """The metric's second half as a roofline object: config 3's dequant-GEMM
+    (gemm_q4k_tc) at M = 8192, mean of both shapes, against the measured
+    dense bf16 peak; per-M figures beside it."""
+    if not prefill_sum or "value" not in prefill_sum:
+        return prefill_sum
+    per = prefill_sum["per_shape"]
+    per_m = {}
+    for m in PREFILL_M:
+        v = [r["tflops"] for kk, r in per.items() if kk.endswith(f"_m{m}")]
+        per_m[str(m)] = round(sum(v) / len(v), 1)
+    out = {"bound": "tensor", "kernel": "gemm_q4k_tc (tcgen05, TMEM accumulator), config 3",
+           "achieved": prefill_sum["value"], "peak": prefill_sum["peak"], "unit": "TFLOP/s",
+           "frac": prefill_sum["frac_of_peak"], "tflops_per_M": per_m}
+    if not short:
+        out.update({"peak_kind": prefill_sum["peak_kind"], "traffic": gemm_traffic_from_profiles(),
+                    "flops_per_launch": "2*M*N*K (M=8192: 962.1 GFLOP per shape)",
+                    "device_status": prefill_sum.get("device_status")})
+    return out
+
+
+def gemm_traffic_from_profiles():
+    """dram bytes per launch of the config-3 GEMM from profiles/gemm_q4k_prefill.md
+    (line 'traffic_bytes_per_launch: N'), or None."""
+    p = os.path.join(ROOT, "profiles", "gemm_q4k_prefill.md")
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(ln.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
 def traffic_from_profiles():
     """dram bytes per launch of the dominant kernel from the committed ncu
     summary (profiles/gemv_q4k_decode.md, line 'traffic_bytes_per_launch: N')."""
@@ -935,27 +1002,49 @@ def run_down_axpy(reps=50):
 
 # ----------------------------------------------------------- CPU baselines
 
-def cpu_sample(threads, budget_s=10.0):
-    """The CPU port of CpuBackend::matmul (oracle) over one config-2 layer,
-    repeated within about budget_s seconds."""
+def cpu_port_run(threads, warmup, steps=None, budget_s=15.0, max_s=150.0):
+    """The CPU port of CpuBackend::matmul (oracle) on config 2 with ``threads``
+    host threads.  One step = the seven GEMVs of one Llama-3-8B Q4_K layer, or,
+    when ``steps`` layers would take longer than ``max_s``, one of the seven
+    (in rotation) so the run stays bounded.  ``steps`` None: as many layer
+    steps as fit in about ``budget_s``.  Per-step times are taken one by one;
+    the rate uses their median (host noise shows in min / max)."""
     from oracle import oracle as O
     L = make_weights(seed=0)[0]
     xs = {nm: S.activations_f32(1, ln, seed=0, name=nm) for nm, ln in X_LEN.items()}
-    wbytes, xybytes = layer_bytes()
+    gemv_bytes = {name: F.row_bytes(F.Q4_K, k) * n + 4 * (n + k) for name, n, k in LAYER}
 
-    def one():
-        for name, n, k in LAYER:
-            O.matmul(xs[X_OF[name]], L[name], F.Q4_K, k, threads=threads)
+    def gemv(name, k):
+        O.matmul(xs[X_OF[name]], L[name], F.Q4_K, k, threads=threads)
 
+    def layer():
+        for name, _, k in LAYER:
+            gemv(name, k)
+        return sum(gemv_bytes.values())
+
+    for _ in range(max(1, warmup)):
+        layer()
     t = time.perf_counter()
-    one()
+    layer()
     t1 = time.perf_counter() - t
-    reps = max(1, min(50, int(budget_s / max(t1, 1e-3))))
-    t = time.perf_counter()
-    for _ in range(reps):
-        one()
-    dt = (time.perf_counter() - t) / reps
-    return (wbytes + xybytes) / dt / 1e9, reps, dt
+    if steps is None:
+        steps = max(3, int(budget_s / max(t1, 1e-3)))
+    per_gemv = steps * t1 > max_s
+    times, nbytes = [], []
+    for i in range(steps):
+        t = time.perf_counter()
+        if per_gemv:
+            name, _, k = LAYER[i % len(LAYER)]
+            gemv(name, k)
+            nbytes.append(gemv_bytes[name])
+        else:
+            nbytes.append(layer())
+        times.append(time.perf_counter() - t)
+    rates = sorted(b / t / 1e9 for b, t in zip(nbytes, times))
+    return {"gbs": statistics.median(rates), "gbs_min": rates[0], "gbs_max": rates[-1],
+            "steps": steps, "ms_per_step": 1e3 * statistics.median(times),
+            "step": "one GEMV of the layer, in rotation" if per_gemv else
+                    "one Llama-3-8B Q4_K layer (7 GEMVs)"}
 
 
 def reference_q8_0_config1(threads):
@@ -1018,27 +1107,10 @@ def run_reference(args):
     reference cannot run Q4_K (no decoder), so the timed arm is the port of
     its CpuBackend::matmul (same row split, dot_row_f32 arithmetic) over the
     same Q4_K layer; its own Q8_0 number is reported beside it."""
-    from oracle import oracle as O
     threads = os.cpu_count() or 1
-    L = make_weights(seed=0)[0]
-    xs = {nm: S.activations_f32(1, ln, seed=0, name=nm) for nm, ln in X_LEN.items()}
-    wbytes, xybytes = layer_bytes()
-
-    def one():
-        for name, n, k in LAYER:
-            O.matmul(xs[X_OF[name]], L[name], F.Q4_K, k, threads=threads)
-
-    for _ in range(min(args.warmup, 2)):
-        one()
-    t = time.perf_counter()
-    one()
-    t1 = time.perf_counter() - t
-    steps = max(3, min(args.steps, int(90.0 / max(t1, 1e-3))))
-    t = time.perf_counter()
-    for _ in range(steps):
-        one()
-    dt = (time.perf_counter() - t) / steps
-    gbs = (wbytes + xybytes) / dt / 1e9
+    r = cpu_port_run(threads, args.warmup, steps=args.steps)
+    gbs = r["gbs"]
+    steps = args.steps
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -1046,19 +1118,20 @@ def run_reference(args):
         "unit": "GB/s",
         "n_gpus": args.gpus,
         "steps": steps,
-        "warmup": min(args.warmup, 2),
-        "ms_per_step": round(dt * 1e3, 3),
+        "warmup": args.warmup,
+        "ms_per_step": round(r["ms_per_step"], 3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded Q4_K blocks and N(0,1) fp32 activations, config 2 distributions)",
-        "config": {"workload": "config 2: Q4_K decode GEMV, Llama-3-8B layer shapes, batch 1",
-                   "layers_per_step": 1, "parallelism": "host threads"},
+        "config": CONFIG,
+        "step": {"parallelism": f"{threads} host threads", "sample": r["step"]},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"one Llama-3-8B Q4_K layer (7 GEMVs, {wbytes} B) per step; "
-                                   "the reference has no Q4_K decoder, so this is the oracle "
-                                   "port of its CpuBackend::matmul"},
+                         "gbs_min": round(r["gbs_min"], 3), "gbs_max": round(r["gbs_max"], 3),
+                         "sample": f"{r['step']} per step, median of per-step rates; the "
+                                   "reference has no Q4_K decoder, so this is the oracle port "
+                                   "of its CpuBackend::matmul"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "reference_q8_0_config1": reference_q8_0_config1(threads),
@@ -1121,12 +1194,13 @@ def main():
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            gbs, reps, dt = cpu_sample(threads)
+            r = cpu_port_run(threads, warmup=2)
             line["cpu_baseline"] = {
-                "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                "sample": f"one Q4_K layer (7 GEMVs) x {reps} reps, {dt * 1e3:.1f} ms each; the "
-                          "reference has no Q4_K decoder, so this is the oracle port of its "
-                          "CpuBackend::matmul"}
+                "value": round(r["gbs"], 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                "gbs_min": round(r["gbs_min"], 3), "gbs_max": round(r["gbs_max"], 3),
+                "sample": f"{r['step']} x {r['steps']} steps, median {r['ms_per_step']:.1f} ms; "
+                          "the reference has no Q4_K decoder, so this is the oracle port of "
+                          "its CpuBackend::matmul"}
             ref = reference_q8_0_config1(threads)
             if ref:
                 line["reference_q8_0_config1"] = ref

@@ -78,7 +78,13 @@ int ftc_backend_info(ftc_backend* be, char* name, size_t cap, uint64_t* mem_byte
 /* Upload a GGUF tensor's raw blocks to HBM once (Engine::load time,
  * ft/src/engine.cpp:318-382).  The cache is keyed by the host address range
  * [host, host + nbytes); later calls whose weight pointer falls inside that
- * range use the device copy.  Re-uploading the same range is a no-op. */
+ * range use the device copy.  Re-uploading the same range is a no-op.
+ * Lifetime rule: the caller keeps [host, host + nbytes) mapped and unchanged
+ * until ftc_backend_evict or ftc_backend_destroy (the engine's GGUF mapping
+ * outlives its backend).  Only ranges passed here are ever cached: weights
+ * the entry points below meet outside every uploaded range are copied to
+ * the device for that call alone, so freeing or rewriting such a buffer
+ * after the call is always safe. */
 int ftc_backend_upload(ftc_backend* be, const void* host, size_t nbytes);
 /* Drop the cached copy of the range that starts at `host`. */
 int ftc_backend_evict(ftc_backend* be, const void* host);
@@ -89,8 +95,9 @@ int ftc_backend_cached_bytes(ftc_backend* be, uint64_t* bytes);
  *   y[m][n] = sum_k x[m][k] * W[n][k]   for m < M, n < N
  * x: host fp32 [M][K]; w_host: the tensor's host data pointer (HostTensor::
  * data), dtype and N rows of ceil(K/block) blocks; y: host fp32 [M][N].
- * Uploads W on first use if no cached range covers it.  Returns with y
- * written.  Unlike the reference's CpuBackend::matmul
+ * A W inside an uploaded range is read from HBM; any other W is copied to
+ * the device for this call only (nothing is cached implicitly).  Returns
+ * with y written.  Unlike the reference's CpuBackend::matmul
  * (ft/src/cpu_backend.cpp:90-104), which folds all M rows into y[n], every
  * row m gets its own output row.  Q4_K with M > 8 runs on the tensor cores
  * (ftc_rows_to_f16 + ftc_gemm_rowscaled: fp16 operands, fp32 accumulation);
@@ -127,8 +134,9 @@ int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* jo
  * W_i = row i of w_host (N weights, row_bytes(dtype, N) bytes per row; the
  * reference's transposed "down" layout, n_in rows = neurons); rows with
  * x[m][i] == 0 add nothing.  x: host fp32 [M][n_in]; y: host fp32 [M][N],
- * accumulated.  The weight resolves through the HBM cache like
- * ftc_backend_matmul's.  M == 0 or n_in == 0 changes nothing. */
+ * accumulated.  The weight resolves like ftc_backend_matmul's: the HBM
+ * copy of an uploaded range, else a copy for this call only.  M == 0 or
+ * n_in == 0 changes nothing. */
 int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int64_t n_in,
                                  const void* w_host, int dtype, int64_t N, float* y);
 
@@ -138,8 +146,9 @@ int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int
  * the device and its result is added into out:
  *   out[t] += sum over t's top_k experts e of w_e * down_e . (silu(gate_e . x_t) * (up_e . x_t))
  * desc: as for ftc_moe_ffn but gate_exps / up_exps / down_exps are the
- * tensors' HOST data pointers (the GGUF mapping), resolved through the HBM
- * cache like ftc_backend_matmul's weights; down planes in the standard layout
+ * tensors' HOST data pointers (the GGUF mapping), resolved like
+ * ftc_backend_matmul's weights (uploaded: HBM copy; else copied for this
+ * call); down planes in the standard layout
  * (n_embd rows of n_ff).  logits: host fp32 [T][E]; x: host fp32 [T][n_embd];
  * out: host fp32 [T][n_embd] (the engine's tmpo).  T == 0 changes nothing. */
 struct ftc_moe_desc; /* defined with the device MoE entry points below */

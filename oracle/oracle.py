@@ -22,10 +22,22 @@ _i64 = C.c_int64
 _p = C.c_void_p
 
 
+def reference_tree():
+    """The reference's source tree (the directory holding its ``src/`` and
+    ``include/``): ``$FT_REF_SRC`` when set, else ``reference/ft-igpu-src``
+    checked out beside this repository, else None."""
+    env = os.environ.get("FT_REF_SRC")
+    if env:
+        return env if os.path.isdir(env) else None
+    side = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference", "ft-igpu-src")
+    return side if os.path.isdir(os.path.join(side, "src")) else None
+
+
 def build():
     """Compile liboracle.so (and _ref/libftref.so where the reference tree
     exists) with oracle/Makefile."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    ref = reference_tree()
+    subprocess.run(["make", "-s", "-C", HERE] + ([f"REF_SRC={ref}"] if ref else []), check=True)
 
 
 def _load(path):

@@ -239,7 +239,32 @@ static void test_upload_and_errors(CudaBackend& be) {
         threw = true;
     }
     CHECK(threw, "mismatched K throws std::runtime_error");
+    be.evict(W);  // before w's memory is freed
     be.sync();
+}
+
+// One host buffer rewritten with other weights between calls (same address,
+// other blocks and formats): a weight that was never uploaded is copied per
+// call, so every call must see the current bytes.
+static void test_reused_host_buffer(CudaBackend& be) {
+    const int64_t K = 4096, M = 3;
+    std::vector<uint8_t> buf(dtype_row_bytes(DType::Q4_K, K) * 1024);
+    std::vector<float> x((size_t)(M * K));
+    for (auto& v : x) v = rnd();
+    const DType types[4] = {DType::Q4_K, DType::Q4_K, DType::Q8_0, DType::Q6_K};
+    const int64_t rows[4] = {1024, 1024, 512, 512};
+    for (int c = 0; c < 4; ++c) {
+        auto w = random_blocks(types[c], rows[c], K);
+        std::memcpy(buf.data(), w.data(), w.size());
+        HostTensor W = view(buf, types[c], K, rows[c]);
+        std::vector<float> y((size_t)(M * rows[c]), NAN), ref((size_t)(M * rows[c]));
+        be.matmul(x.data(), M, K, W, y.data());
+        ftor_matmul(x.data(), M, K, w.data(), (int)types[c], rows[c],
+                    (int64_t)W.row_stride_bytes(), ref.data(), 8);
+        char msg[96];
+        std::snprintf(msg, sizeof msg, "reused host buffer, case %d", c);
+        CHECK(rel_err(y, ref) <= 2e-3, msg);
+    }
 }
 
 int main(int argc, char** argv) {
@@ -281,6 +306,7 @@ int main(int argc, char** argv) {
         test_matmul(be, DType::Q8_0, 512, 4096, 20);     // GEMV, 8 rows per pass
         test_expert_chunk_windows(be);
         test_upload_and_errors(be);
+        test_reused_host_buffer(be);
     } catch (const std::exception& e) {
         std::printf("FAIL exception: %s\n", e.what());
         ++g_fails;

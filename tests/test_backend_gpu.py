@@ -80,6 +80,28 @@ def test_weight_cache_upload_once(be):
     assert be.device_ptr(W) is None
 
 
+def test_reused_host_buffer_is_not_served_stale(be, oracle):
+    """A weight that was never uploaded is copied per call: rewriting the
+    same host buffer (same address, new blocks, even a different format)
+    between calls must change the result.  An implicit address-keyed cache
+    returned the first weight's device copy here."""
+    from xwfes_b200 import ftc
+    n, k, m = 512, 4096, 3
+    buf = np.zeros(ftc.row_bytes(F.Q4_K, k) * 2 * n, dtype=np.uint8)
+    x = S.activations_f32(m, k, seed=7)
+    cases = ((F.Q4_K, 2 * n, 1), (F.Q4_K, 2 * n, 2), (F.Q8_0, n, 3), (F.Q6_K, n, 4))
+    for t, rows, seed in cases:
+        w = S.weight(t, rows, k, seed=seed, name="reuse")
+        buf[:w.size] = w.reshape(-1)
+        W = ftc.HostTensor(buf[:w.size].reshape(w.shape), t, (k, rows))
+        assert W.ptr() == buf.ctypes.data
+        y = np.full((m, rows), np.nan, dtype=np.float32)
+        be.matmul(x, m, k, W, y)
+        ref = oracle.matmul(x, w, t, k, threads=THREADS)
+        assert rel_err(y, ref) <= 2e-3, F.NAMES[t]
+    assert be.device_ptr(ftc.HostTensor(buf, F.Q8_0, (k, n))) is None  # nothing cached
+
+
 def test_expert_chunk_reference_chunker_case(be, golden):
     """ft/src/tests/test_core.cpp:307-346 shapes (F32, K=16, FF=48, M=3,
     windows of 8) against the reference's run_expert_chunk outputs, with

@@ -18,7 +18,7 @@ def test_reference_arm_prints_one_contract_line():
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["unit"] == "GB/s" and d["value"] > 0
-    assert d["higher_is_better"] is True and d["steps"] >= 3
+    assert d["higher_is_better"] is True and d["steps"] == 3 and d["warmup"] == 3
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert cb["value"] == d["value"]

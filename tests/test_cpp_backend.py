@@ -30,11 +30,18 @@ def compile_test(out):
     return out
 
 
+def _ref_include():
+    from oracle import oracle as O
+    tree = O.reference_tree()
+    return os.path.join(tree, "include") if tree else ""
+
+
 # the reference tree's headers, where the reference is checked out (CPU-only check)
-REF_INCLUDE = os.environ.get("FT_REF_INCLUDE", "/root/reference/ft-igpu-src/include")
+REF_INCLUDE = _ref_include()
 
 
-@pytest.mark.skipif(not os.path.isdir(REF_INCLUDE), reason="reference tree not present")
+@pytest.mark.skipif(not REF_INCLUDE or not os.path.isdir(REF_INCLUDE),
+                    reason="reference tree not present")
 def test_adapter_compiles_against_reference_headers():
     """cuda_backend.cpp drops into the reference tree as is: it compiles
     against the reference's own, unmodified ft/ headers (C++20, as its

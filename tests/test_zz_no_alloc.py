@@ -2,12 +2,16 @@
 device memory (fixed-budget engines, code inside another component's stream
 capture).  It must give the same result as the allocating entry point,
 ftc_backend_run_expert_chunk, call after call, although both calls reuse the
-library's one static scratch array.
+library's one static scratch array; and both must match the CPU oracle's
+restatement of the reference's CpuBackend::run_expert_chunk
+(ft/src/cpu_backend.cpp:106-149), so a fault in the kernels they share
+cannot pass unseen.
 
 Kept in its own file, collected last, so that a failure here cannot stop a
 `-x` run before the other tests have run; it also passes on its own in a
 fresh process."""
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -66,7 +70,7 @@ def case(t, M, K, IC, seed):
     return x, out, gate, up, down
 
 
-def test_static_scratch_matches_allocating_entry_point_twice(ftc):
+def test_static_scratch_matches_allocating_entry_point_twice(ftc, oracle):
     be = ftc.CudaBackend(0)
     try:
         # two calls in a row, different formats and sizes: the second must
@@ -75,15 +79,25 @@ def test_static_scratch_matches_allocating_entry_point_twice(ftc):
             x, out, gate, up, down = case(t, M, K, IC, seed)
             got = run_static(ftc, t, x, out, gate, up, down, M, K, IC)
             want = run_allocating(be, t, x, out, gate, up, down, M, K, IC)
+            ref = out.copy()
+            oracle.expert_chunk(x, ref, gate, up, down, t, K, IC, threads=os.cpu_count() or 8)
             assert rel_err(got, want) <= 2e-3, F.NAMES[t]
+            assert rel_err(got, ref) <= 2e-3, F.NAMES[t]
+            assert rel_err(want, ref) <= 2e-3, F.NAMES[t]
     finally:
         be.close()
 
 
-def test_static_scratch_rejects_oversized_windows(ftc):
+def test_static_scratch_rejects_oversized_windows(ftc, oracle):
     dummy = torch.zeros(16, dtype=torch.uint8, device="cuda")
     p = dummy.data_ptr()
     rc = ftc.lib().ftc_expert_chunk_static(F.Q4_K, p, p, p, p, p, 2, 256, MAX_HC, 144, 144, None)
     assert rc == -1 and "FTC_EXPERT_STATIC_MAX_HC" in ftc.last_error()
-    # a window that fits is accepted again afterwards (nothing was launched)
-    assert ftc.device_status() == 0
+    assert ftc.device_status() == 0  # nothing was launched
+    # a window that fits is accepted afterwards, and still matches the oracle
+    t, M, K, IC = F.Q4_K, 2, 1024, MAX_HC // 2
+    x, out, gate, up, down = case(t, M, K, IC, 5)
+    got = run_static(ftc, t, x, out, gate, up, down, M, K, IC)
+    ref = out.copy()
+    oracle.expert_chunk(x, ref, gate, up, down, t, K, IC, threads=os.cpu_count() or 8)
+    assert rel_err(got, ref) <= 2e-3

@@ -220,15 +220,36 @@ struct ftc_backend {
         return FTC_OK;
     }
 
-    // Device address of host range [p, p + n): cached copy, else uploaded.
-    int resolve(const void* p, size_t n, const void** dev) {
-        const CacheEntry* e = find(p, n);
-        if (!e) {
-            int rc = upload(p, n);
-            if (rc) return rc;
-            e = find(p, n);
+    // Device addresses of n host ranges.  A range inside a tensor passed to
+    // upload() uses that HBM copy; any other range is copied, on the
+    // backend's stream, into the per-call window buffer `dwin` and used from
+    // there for this call only.  Nothing is cached implicitly, so a host
+    // buffer that the caller frees or rewrites after the call can never be
+    // served later from a stale device copy.  *streamed tells whether any
+    // range went through the window buffer.
+    int resolve(int n, const void* const* host, const size_t* bytes, const void** dev,
+                bool* streamed) {
+        size_t off[4] = {0, 0, 0, 0}, total = 0;
+        for (int i = 0; i < n; ++i) {
+            const CacheEntry* e = find(host[i], bytes[i]);
+            if (e) {
+                dev[i] = static_cast<const uint8_t*>(e->dev) + ((const uint8_t*)host[i] - e->host);
+            } else {
+                dev[i] = nullptr;
+                off[i] = total;
+                total += (bytes[i] + 255) & ~(size_t)255;
+            }
         }
-        *dev = static_cast<const uint8_t*>(e->dev) + ((const uint8_t*)p - e->host);
+        *streamed = total > 0;
+        if (!total) return FTC_OK;
+        int rc = dwin.ensure(total);
+        if (rc) return rc;
+        for (int i = 0; i < n; ++i)
+            if (!dev[i]) {
+                void* d = static_cast<uint8_t*>(dwin.p) + off[i];
+                FTC_CUDA(cudaMemcpyAsync(d, host[i], bytes[i], cudaMemcpyHostToDevice, stream));
+                dev[i] = d;
+            }
         return FTC_OK;
     }
 };
@@ -360,7 +381,9 @@ int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K, co
     std::lock_guard<std::mutex> lk(be->mu);
     const int64_t stride = row_bytes(dtype, K);
     const void* dW = nullptr;
-    if ((rc = be->resolve(w_host, (size_t)(stride * N), &dW))) return rc;
+    const size_t wb = (size_t)(stride * N);
+    bool streamed = false;
+    if ((rc = be->resolve(1, &w_host, &wb, &dW, &streamed))) return rc;
     const size_t xb = (size_t)(M * K) * 4, yb = (size_t)(M * N) * 4;
     if ((rc = be->pin_in.ensure(xb)) || (rc = be->pin_out.ensure(yb)) || (rc = be->dx.ensure(xb)) ||
         (rc = be->dy.ensure(yb)))
@@ -395,7 +418,8 @@ int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K, co
         FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, st));
         return FTC_OK;
     };
-    if (be->use_graphs) {
+    // Graphs only for resident weights: a streamed weight's copy is per call.
+    if (be->use_graphs && !streamed) {
         void* bufs[5] = {be->pin_in.p, be->pin_out.p, be->dx.p, be->dy.p, be->dtmp.p};
         if (std::memcmp(bufs, be->graph_bufs, sizeof(bufs)) != 0) {
             be->drop_graphs();
@@ -453,25 +477,8 @@ int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* jo
     const void* win[3] = {job->gate, job->up, job->down};
     const size_t wbytes[3] = {gu_bytes, gu_bytes, dn_bytes};
     const void* dev[3] = {nullptr, nullptr, nullptr};
-    size_t stream_off[3], stream_total = 0;
-    for (int i = 0; i < 3; ++i) {
-        const CacheEntry* e = be->find(win[i], wbytes[i]);
-        if (e) {
-            dev[i] = static_cast<const uint8_t*>(e->dev) + ((const uint8_t*)win[i] - e->host);
-        } else {
-            stream_off[i] = stream_total;
-            stream_total += (wbytes[i] + 255) & ~(size_t)255;
-        }
-    }
-    if (stream_total) {
-        if ((rc = be->dwin.ensure(stream_total))) return rc;
-        for (int i = 0; i < 3; ++i)
-            if (!dev[i]) {
-                void* d = static_cast<uint8_t*>(be->dwin.p) + stream_off[i];
-                FTC_CUDA(cudaMemcpyAsync(d, win[i], wbytes[i], cudaMemcpyHostToDevice, be->stream));
-                dev[i] = d;
-            }
-    }
+    bool streamed = false;
+    if ((rc = be->resolve(3, win, wbytes, dev, &streamed))) return rc;
     const size_t xb = (size_t)(M * K) * 4, hb = (size_t)(M * IC) * 4;
     if ((rc = be->pin_in.ensure(2 * xb)) || (rc = be->pin_out.ensure(xb)) ||
         (rc = be->dx.ensure(2 * xb)) || (rc = be->dtmp.ensure(3 * hb + 768)))
@@ -510,7 +517,9 @@ int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int
     std::lock_guard<std::mutex> lk(be->mu);
     const int64_t stride = row_bytes(dtype, N);
     const void* dW = nullptr;
-    if ((rc = be->resolve(w_host, (size_t)(stride * n_in), &dW))) return rc;
+    const size_t wb = (size_t)(stride * n_in);
+    bool streamed = false;
+    if ((rc = be->resolve(1, &w_host, &wb, &dW, &streamed))) return rc;
     const size_t xb = (size_t)(M * n_in) * 4, yb = (size_t)(M * N) * 4;
     const size_t xo = (xb + 255) & ~(size_t)255;
     const size_t wsb = down_axpy_workspace_bytes(dtype, n_in, N, M);
@@ -558,8 +567,8 @@ int ftc_backend_moe_ffn(ftc_backend* be, const ftc_moe_desc* desc, const float* 
     const size_t gu_ext = (size_t)((E - 1) * d.gu_plane_stride + d.n_ff * d.gu_row_stride);
     const size_t dn_ext = (size_t)((E - 1) * d.dn_plane_stride + K * d.dn_row_stride);
     const size_t bytes[3] = {gu_ext, gu_ext, dn_ext};
-    for (int i = 0; i < 3; ++i)
-        if ((rc = be->resolve(host[i], bytes[i], &dev[i]))) return rc;
+    bool streamed = false;
+    if ((rc = be->resolve(3, host, bytes, dev, &streamed))) return rc;
     d.gate_exps = dev[0];
     d.up_exps = dev[1];
     d.down_exps = dev[2];

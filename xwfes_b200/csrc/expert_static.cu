@@ -21,7 +21,10 @@
 //     that overlap on the GPU (different streams, no ordering) race on it.
 //   * The first call on each device looks up the array's device address with
 //     cudaGetSymbolAddress (with that device current) and caches it; make
-//     that first call before any stream capture.
+//     that first call before any stream capture.  The cached address belongs
+//     to the device's primary context: after cudaDeviceReset (which destroys
+//     that context and the array with it) do not call this entry again in
+//     the same process.
 #include <mutex>
 
 #include "common.cuh"

@@ -500,13 +500,15 @@ class HostTensor:
 class CudaBackend:
     """Python mirror of the ft::IBackend a CUDA build plugs in
     (ft/include/ft/backend.h:21-40), over the ftc_backend_* C ABI.  Host
-    buffers in, host buffers out; weights cached in HBM by host address."""
+    buffers in, host buffers out.  Weights passed to ``upload`` stay in HBM
+    (keyed by host address; the HostTensor is kept alive until ``evict``);
+    any other weight is copied to the device for the one call."""
 
     def __init__(self, device=0):
         h = C.c_void_p()
         check(lib().ftc_backend_create(device, C.byref(h)), "ftc_backend_create")
         self._h = h
-        self._keep = {}  # host tensors whose addresses key the cache, by address
+        self._keep = {}  # uploaded host tensors (their addresses key the cache)
 
     def close(self):
         if self._h:
@@ -559,7 +561,6 @@ class CudaBackend:
         """IBackend::matmul: x fp32 [M][K] host, y fp32 [M][N] host (written)."""
         assert x.dtype == np.float32 and x.flags.c_contiguous and x.size >= M * K
         assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * W.rows()
-        self._keep[W.ptr()] = W
         check(lib().ftc_backend_matmul(self._h, x.ctypes.data, M, K, W.ptr(), W.dtype,
                                        W.rows(), y.ctypes.data), "ftc_backend_matmul")
 
@@ -571,7 +572,6 @@ class CudaBackend:
         assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * W.cols()
         if n_in > W.rows():
             raise ValueError("matmul_down_axpy: n_in exceeds W.rows()")
-        self._keep[W.ptr()] = W
         check(lib().ftc_backend_matmul_down_axpy(self._h, x.ctypes.data, M, n_in, W.ptr(),
                                                  W.dtype, W.cols(), y.ctypes.data),
               "ftc_backend_matmul_down_axpy")
@@ -592,8 +592,6 @@ class CudaBackend:
                     gu_plane_stride=gate_exps.slice_bytes(),
                     dn_row_stride=down_exps.row_stride_bytes(),
                     dn_plane_stride=down_exps.slice_bytes())
-        for t in (gate_exps, up_exps, down_exps):
-            self._keep[t.ptr()] = t
         b = None
         if bias is not None:
             bias = np.ascontiguousarray(bias, dtype=np.float32)

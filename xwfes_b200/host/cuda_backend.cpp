@@ -124,6 +124,8 @@ void CudaBackend::upload(const HostTensor& t) {
     check(ftc_backend_upload(be_, t.data, n), "upload");
 }
 
+void CudaBackend::evict(const HostTensor& t) { check(ftc_backend_evict(be_, t.data), "evict"); }
+
 size_t CudaBackend::upload_all(const Gguf& model) {
     size_t total = 0;
     for (const auto& kv : model.tensors()) {

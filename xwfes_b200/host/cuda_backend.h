@@ -81,8 +81,12 @@ public:
     static bool moe_supported(const HostTensor& gexps, const HostTensor& uexps,
                               const HostTensor& dexps);
 
-    // Load a tensor's blocks into HBM once (call at Engine::load time).
+    // Load a tensor's blocks into HBM once (call at Engine::load time).  The
+    // host blocks must stay mapped and unchanged until evict() or the
+    // backend's destruction; tensors never uploaded are copied per call.
     void upload(const HostTensor& t);
+    // Drop the HBM copy of an uploaded tensor (before its host memory goes).
+    void evict(const HostTensor& t);
     // Every tensor of a model file, blocks unchanged (the engine's load step,
     // ft/src/engine.cpp:282-396): later matmuls and expert chunks on these
     // tensors find their device copies instead of copying per call.
