@@ -3,7 +3,8 @@ is captured once and replayed as a CUDA graph.  The replayed work is the
 same kernels on the same buffers, so every output must equal the direct
 path's bit for bit: repeated calls (replays), a new shape, a larger call that
 moves the staging buffers (all graphs dropped and captured again), and a
-call after the weight was evicted.  Runs late in the suite."""
+call after the weight was evicted (copied for that call, not replayed).
+Graphs are kept for uploaded weights only.  Runs late in the suite."""
 import numpy as np
 import pytest
 
@@ -39,6 +40,8 @@ def test_graph_replays_equal_direct_calls(ftc, monkeypatch):
     for graphs in (False, True):
         be = backend(ftc, monkeypatch, graphs)
         try:
+            for W in Ws + [W8]:
+                be.upload(W)
             got = []
             for rep in range(2):
                 for wi, m in calls:

@@ -568,10 +568,10 @@ class CudaBackend:
         """ft::matmul_down_axpy: y[m] += x_m . W over the first ``n_in`` rows of
         W (``W.cols()`` weights each); x fp32 [M][n_in], y fp32 [M][W.cols()]
         host arrays, y accumulated."""
-        assert x.dtype == np.float32 and x.flags.c_contiguous and x.size >= M * n_in
-        assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * W.cols()
         if n_in > W.rows():
             raise ValueError("matmul_down_axpy: n_in exceeds W.rows()")
+        assert x.dtype == np.float32 and x.flags.c_contiguous and x.size >= M * n_in
+        assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * W.cols()
         check(lib().ftc_backend_matmul_down_axpy(self._h, x.ctypes.data, M, n_in, W.ptr(),
                                                  W.dtype, W.cols(), y.ctypes.data),
               "ftc_backend_matmul_down_axpy")
