@@ -124,6 +124,7 @@ int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dty
 
 // status readers of the translation units whose kernels use bounded waits
 int devstat_gemv_q4k(int clear);
+int devstat_gemv_imma(int clear);
 int devstat_gemm_q4k(int clear);
 int devstat_peer_ar(int clear);
 
@@ -608,7 +609,7 @@ int ftc_device_status(void* stream, int* status) {
     FTC_REQUIRE(status, FTC_E_INVALID, "ftc_device_status: null status");
     FTC_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
     int v = 0;
-    for (int (*rd)(int) : {devstat_gemv_q4k, devstat_gemm_q4k, devstat_peer_ar}) {
+    for (int (*rd)(int) : {devstat_gemv_q4k, devstat_gemv_imma, devstat_gemm_q4k, devstat_peer_ar}) {
         const int s = rd(1);
         FTC_REQUIRE(s >= 0, FTC_E_CUDA, "ftc_device_status: cannot read the status word");
         v |= s;

@@ -10,7 +10,9 @@
 // 8 x 57 KB) stay L1/L2-resident.
 //
 // Kernels:
-//   gemv_q4k     Q4_K, 16-byte aligned rows: registers only.  An octet of 8
+//   gemv_q4k     Q4_K, 16-byte aligned rows, when the integer tensor-core
+//                kernel (gemv_imma.cu, 2..8 rows) does not take the shape:
+//                registers only.  An octet of 8
 //                lanes covers one 144-byte super-block: every lane reads the
 //                16-byte header and one 16-byte slice of the 128 code bytes
 //                (32 weights: 16 of sub-block 2g, 16 of sub-block 2g+1).
@@ -22,6 +24,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemv_batch.cuh"
 
 namespace ftc {
 namespace {
@@ -372,13 +375,37 @@ int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float*
                         int64_t stride, int64_t K, const float* x, cudaStream_t st, int n_next,
                         const uint8_t* const* next_w, const int64_t* next_bytes);
 
+int gemv_q4k_imma_batch(const GemvSpec& g, int64_t M, int64_t ldx, cudaStream_t st);
+
 namespace {
+
+// Q4_K with 2..8 tokens: the integer tensor-core kernel (gemv_imma.cu) for
+// P matrices sharing x; FTC_E_UNSUPPORTED when it does not apply.
+int imma_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y, int64_t stride,
+               int64_t K, const float* x, int64_t M, cudaStream_t st) {
+    GemvSpec g = {};
+    g.P = P;
+    g.K = K;
+    g.stride = stride;
+    g.x[0] = x;
+    for (int i = 0; i < P; ++i) {
+        g.W[i] = W[i];
+        g.N[i] = N[i];
+        g.y[i] = y[i];
+    }
+    return gemv_q4k_imma_batch(g, M, K, st);
+}
 
 template <int M>
 int launch_m(int dtype, const uint8_t* W, int64_t stride, int N, int64_t K, const float* x,
              float* y, cudaStream_t st) {
     if (M == 1 && dtype == FTC_Q4_K) {
         const int rc = gemv_q4k_fast(W, stride, N, K, x, y, st);
+        if (rc != FTC_E_UNSUPPORTED) return rc;
+    }
+    if (M > 1 && dtype == FTC_Q4_K) {
+        const int64_t n64 = N;
+        const int rc = imma_multi(1, &W, &n64, &y, stride, K, x, M, st);
         if (rc != FTC_E_UNSUPPORTED) return rc;
     }
     const Fmt f = fmt_of(dtype);
@@ -445,6 +472,17 @@ int mul_mat_vec_multi(int dtype, int P, const void* const* w, const int64_t* N, 
                                                row_stride, K, x, st, n_next,
                                                reinterpret_cast<const uint8_t* const*>(next_w),
                                                next_bytes);
+            if (rc != FTC_E_UNSUPPORTED) return rc;
+        }
+    }
+    if (dtype == FTC_Q4_K && M > 1 && M <= 8 && x && row_stride >= row_bytes(dtype, K)) {
+        bool args_ok = true;
+        for (int i = 0; i < P && args_ok; ++i) args_ok = w[i] && y[i] && N[i] > 0;
+        if (args_ok) {
+            if (inject_fail("ftc_mul_mat_vec"))
+                return set_error(FTC_E_INJECTED, "ftc_mul_mat_vec_multi: injected failure");
+            const int rc = imma_multi(P, reinterpret_cast<const uint8_t* const*>(w), N, y,
+                                      row_stride, K, x, M, st);
             if (rc != FTC_E_UNSUPPORTED) return rc;
         }
     }
