@@ -484,8 +484,10 @@ def time_e2e_graphs(dev, local_rank, hosts, xs_host, steps, step_bytes):
 
 def time_decode_extras(dev, dptr, stream, reps=20):
     """Config 2's other cases: the same 8 layer copies at batch 4 and 8 (one
-    ftc_mul_mat_vec launch per matrix, graph-replayed), and the Q6_K output
-    head (128256 x 4096, 431 MB, larger than L2) at batch 1."""
+    ftc_mul_mat_vec_multi launch per group of matrices sharing activations --
+    q/k/v, o, gate/up, down -- graph-replayed), and the Q6_K output head
+    (128256 x 4096, 431 MB, larger than L2) at batch 1."""
+    import ctypes as C
     import torch
     from xwfes_b200 import ftc
     L = ftc.lib()
@@ -499,13 +501,22 @@ def time_decode_extras(dev, dptr, stream, reps=20):
               for nm, ln in X_LEN.items()}
         ym = {name: torch.empty((m, n), dtype=torch.float32, device=dev) for name, n, _ in LAYER}
 
+        gargs = []
+        for li in range(N_LAYERS):
+            for _, members in GROUPS:
+                P = len(members)
+                k = SHAPE[members[0]][1]
+                gargs.append((P, (C.c_void_p * P)(*[dptr[(li, mm)] for mm in members]),
+                              (C.c_int64 * P)(*[SHAPE[mm][0] for mm in members]), k,
+                              xm[X_OF[members[0]]].data_ptr(),
+                              (C.c_void_p * P)(*[ym[mm].data_ptr() for mm in members])))
+
         def bstep():
-            for li in range(N_LAYERS):
-                for name, n, k in LAYER:
-                    rc = L.ftc_mul_mat_vec(F.Q4_K, dptr[(li, name)], n, k, F.row_bytes(F.Q4_K, k),
-                                           xm[X_OF[name]].data_ptr(), m, ym[name].data_ptr(), sp)
-                    if rc:
-                        raise ftc.FtcError("ftc_mul_mat_vec", rc, ftc.last_error())
+            for P, wa, na, k, xp, ya in gargs:
+                rc = L.ftc_mul_mat_vec_multi(F.Q4_K, P, wa, na, k, F.row_bytes(F.Q4_K, k), xp, m,
+                                             ya, sp)
+                if rc:
+                    raise ftc.FtcError("ftc_mul_mat_vec_multi", rc, ftc.last_error())
 
         with torch.cuda.stream(stream):
             bstep()  # eager warm-up outside capture
@@ -577,7 +588,8 @@ def time_decode_extras(dev, dptr, stream, reps=20):
     del g, w1
     return {"q8_0_config1": q8,
             "batched": {"workload": "config 2 layer x 8 copies, fp32 activations, batch 4 and 8 "
-                                    "(gemv_q4k batched kernel, one launch per matrix)",
+                                    "(gemv_q4k_imma: integer tensor path, one launch per group "
+                                    "of matrices sharing activations)",
                         "per_batch": batched},
             "q6_k_head": {"workload": "config 2 Q6_K output head 128256x4096, batch 1", **head}}
 

@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "cuda_backend.h"
+#include "ft/gguf.h"
 #include "ftoracle.h"
 
 using namespace ft;
@@ -267,9 +268,89 @@ static void test_reused_host_buffer(CudaBackend& be) {
     }
 }
 
+// A model file through the engine's load path: ft::Gguf maps it, upload_all
+// puts every tensor's blocks into HBM unchanged (ft/src/gguf.cpp:129-137 plus
+// the K-quants), then matmuls on the 2-D weights and expert-chunk windows
+// inside the 3-D expert tensor run from the device copies, against the
+// oracle on the mapped bytes.
+static void test_gguf_model(CudaBackend& be, const char* path) {
+    Gguf model(path);
+    size_t total = 0;
+    for (const auto& kv : model.tensors()) total += kv.second.nbytes;
+    const size_t up = be.upload_all(model);
+    CHECK(up == total, "upload_all uploads every tensor");
+    int matmuls = 0, chunks = 0;
+    for (const auto& kv : model.tensors()) {
+        const HostTensor& W = kv.second;
+        const int t = (int)W.dtype;
+        if (W.dim2() == 1 && (t == FTOR_Q4_K || t == FTOR_Q6_K || t == FTOR_Q8_0)) {
+            for (int64_t M : {1, 3, 16}) {
+                const int64_t K = W.cols(), N = W.rows();
+                std::vector<float> x((size_t)(M * K));
+                for (auto& v : x) v = rnd();
+                std::vector<float> y((size_t)(M * N), NAN), ref((size_t)(M * N));
+                be.matmul(x.data(), M, K, W, y.data());
+                ftor_matmul(x.data(), M, K, W.data, t, N, (int64_t)W.row_stride_bytes(),
+                            ref.data(), 8);
+                const bool tc = t == FTOR_Q4_K && M > 8;
+                char msg[160];
+                std::snprintf(msg, sizeof msg, "gguf matmul %s M %lld", W.name.c_str(),
+                              (long long)M);
+                CHECK((tc ? norm_err(y, ref) : rel_err(y, ref)) <= 2e-3, msg);
+                ++matmuls;
+            }
+        }
+        if (W.dim2() > 1 && t == FTOR_Q4_K) {  // expert planes: windows of plane 1 in place
+            const int64_t K = W.cols(), FF = W.rows(), M = 4, C = 128;
+            const size_t rs = W.row_stride_bytes();
+            const uint8_t* plane = W.slice(1);
+            std::vector<float> x((size_t)(M * K)), out((size_t)(M * K), 0.f),
+                ref((size_t)(M * K), 0.f);
+            for (auto& v : x) v = rnd();
+            for (int64_t i0 = 0; i0 + C <= FF; i0 += C) {
+                ExpertChunkJob job;
+                job.x = x.data();
+                job.out = out.data();
+                job.gate = plane + i0 * rs;
+                job.up = plane + i0 * rs;
+                job.down = plane + i0 * rs;
+                job.dt = W.dtype;
+                job.M = M;
+                job.K = K;
+                job.IC = C;
+                job.gate_up_row_stride = rs;
+                job.down_row_stride = rs;
+                be.run_expert_chunk(job);
+                ftor_expert_chunk(x.data(), ref.data(), plane + i0 * rs, plane + i0 * rs,
+                                  plane + i0 * rs, t, M, K, C, (int64_t)rs, (int64_t)rs, 8);
+                ++chunks;
+            }
+            CHECK(rel_err(out, ref) <= 2e-3, "gguf expert chunks from the uploaded planes");
+        }
+    }
+    CHECK(matmuls >= 3 && chunks >= 1, "the model has 2-D weights and an expert tensor");
+    for (const auto& kv : model.tensors()) be.evict(kv.second);
+}
+
 int main(int argc, char** argv) {
     test_down_layout();
     const char* mode = argc > 1 ? argv[1] : "";
+    if (std::strcmp(mode, "--gguf") == 0 && argc > 2) {
+        try {
+            CudaBackend be(0);
+            test_gguf_model(be, argv[2]);
+            be.sync();
+        } catch (const std::exception& e) {
+            std::printf("FAIL exception: %s\n", e.what());
+            ++g_fails;
+        }
+        if (g_fails) {
+            std::printf("%d checks FAILED\n", g_fails);
+            return 1;
+        }
+        std::printf("all tests passed\n");
+        return 0;
+    }
     if (std::strcmp(mode, "--host-only") == 0) {
         if (g_fails) return 1;
         std::printf("all tests passed\n");

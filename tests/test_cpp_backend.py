@@ -68,3 +68,27 @@ def test_adapter_passes_on_gpu(tmp_path):
     exe = compile_test(str(tmp_path / "test_cuda_backend"))
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "all tests passed" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_gguf_file_upload_and_matmul_on_gpu(tmp_path):
+    """A small model file (Q4_K, Q6_K and Q8_0 weights and a 4-expert Q4_K
+    tensor, written by tests/gguf_write.py) loaded by the engine-side reader,
+    uploaded whole with CudaBackend::upload_all, then matmuls (M = 1, 3, 16)
+    and expert-chunk windows on the device copies against the oracle."""
+    import gguf_write as G
+    from xwfes_b200 import formats as F, synth as S
+    ggml = {F.Q4_K: 12, F.Q6_K: 14, F.Q8_0: 8}
+    specs = [("blk.0.attn_q.weight", F.Q4_K, 512, 1024, 1),
+             ("blk.0.ffn_down.weight", F.Q6_K, 256, 512, 1),
+             ("blk.0.attn_k.weight", F.Q8_0, 128, 1024, 1),
+             ("blk.0.ffn_gate_exps.weight", F.Q4_K, 256, 1024, 4)]
+    tensors = []
+    for name, t, n, k, e in specs:
+        raw = b"".join(S.weight(t, n, k, seed=10 + p, name=name).tobytes() for p in range(e))
+        dims = (k, n) if e == 1 else (k, n, e)
+        tensors.append((name, dims, ggml[t], raw))
+    path = G.write_gguf(str(tmp_path / "tiny.gguf"), [("general.name", G.STR, "tiny")], tensors)
+    exe = compile_test(str(tmp_path / "test_cuda_backend"))
+    r = subprocess.run([exe, "--gguf", path], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "all tests passed" in r.stdout, r.stdout + r.stderr
