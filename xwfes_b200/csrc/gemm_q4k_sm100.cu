@@ -93,23 +93,31 @@ constexpr int kTeamWarps = 8;  // dequant warps per team
 // each team has its own NAT-stage slice of the dequantized weight ring and
 // its own RAWT-slot slice of the raw ring, so every ring has one producer and
 // one consumer and an mbarrier is never waited on more than one phase ahead.
-template <int BN_, int DT_, int NAT_, int NB_, int RAWT_, bool ATM_ = false>
+// MI MMA-issuing threads (1 or 2, in separate warps) take alternate k-steps
+// of every tile, each into its own accumulator; the epilogue adds them in
+// issuer order.  One issuing thread spends ~640 cycles of its own per 64-wide
+// k-step (waits, fence, descriptors, four MMAs, two commits), which bounds
+// small token counts, where the MMAs themselves are short.
+template <int BN_, int DT_, int NAT_, int NB_, int RAWT_, bool ATM_ = false, int MI_ = 1>
 struct Cfg {
-    static constexpr int BN = BN_, DT = DT_, NAT = NAT_, NB = NB_, RAWT = RAWT_;
+    static constexpr int BN = BN_, DT = DT_, NAT = NAT_, NB = NB_, RAWT = RAWT_, MI = MI_;
+    static_assert(MI == 1 || MI == 2, "one or two MMA issuers");
     // ATM: dequantized weight stages live in tensor memory (tcgen05.st by the
-    // dequant warps, read by the MMA as its A operand), after the two
+    // dequant warps, read by the MMA as its A operand), after the
     // accumulators; otherwise in shared memory (128-byte swizzle).
     static constexpr bool ATM = ATM_;
     static constexpr int NA = DT * NAT;           // dequantized weight stages
     static constexpr int RAW = DT * RAWT;         // raw super-block slots
-    static constexpr int WARPS = 2 + kEpiWarps + DT * kTeamWarps + 1;
+    static constexpr int WARPS = 2 + kEpiWarps + DT * kTeamWarps + 1 + (MI - 1);
     static constexpr int THREADS = 32 * WARPS;
-    static constexpr int RAW_WARP = WARPS - 1;    // issues the raw weight tiles
+    static constexpr int RAW_WARP = 2 + kEpiWarps + DT * kTeamWarps;  // issues the raw weight tiles
+    static constexpr int MMA2_WARP = RAW_WARP + 1;                     // second issuer (MI == 2)
     static constexpr int A_BYTES = BM * BK * 2;   // 16 KB
     static constexpr int B_BYTES = BN * BK * 2;
-    static constexpr int A_COL0 = 2 * BN;         // first TMEM column of the A stages (ATM)
+    static constexpr int ACC_COLS = 2 * MI * BN;  // [2 tiles in flight][MI issuers] accumulators
+    static constexpr int A_COL0 = ACC_COLS;       // first TMEM column of the A stages (ATM)
     static constexpr int A_COLS = BK / 2;         // 32 columns: 64 16-bit k per lane
-    static constexpr int TMEM_COLS = ATM ? 512 : 2 * BN;  // two accumulators (+ A stages)
+    static constexpr int TMEM_COLS = ATM ? 512 : (ACC_COLS <= 256 ? 256 : 512);
     static_assert(!ATM || A_COL0 + NA * A_COLS <= 512, "tensor memory");
     // shared layout (all tiles 1024-byte aligned)
     static constexpr int OFF_A = 0;
@@ -342,7 +350,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             mbar_init(&raw_empty[s], kTeamWarps);
         }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_full[s], C::MI);
             mbar_init(&acc_empty[s], kEpiWarps);
         }
         *abort_flag = 0;
@@ -437,11 +445,14 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 }
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || (C::MI == 2 && warp == C::MMA2_WARP)) {
         // ---------------------------------------------------------- MMA
+        // issuer j takes the k-steps ks of a unit with (ks - first) % MI == j
+        const int j = warp == 1 ? 0 : 1;
         if (lane == 0) {
             constexpr uint32_t fmt = std::is_same<OP, __half>::value ? 0u : 1u;
-            uint32_t kc = 0;
+            uint32_t kc = 0, last_kc = 0;
+            bool any = false;
             int i = 0;
             for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++i) {
                 const int b = i & 1;
@@ -451,9 +462,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 const uint32_t idesc = idesc_f16(fmt, BM, (uint32_t)min(BN, (tile_at(tile).rows + 15) & ~15));
                 if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
-                for (int ks = sb0 * 4; ks < sb1 * 4; ++ks) {
-                    const bool acc = ks != sb0 * 4;  // the unit's first k-step overwrites
+                const uint32_t d_tmem = tmem_base + (uint32_t)((b * C::MI + j) * BN);
+                bool acc = false;  // the issuer's first k-step of the unit overwrites
+                for (int ks = sb0 * 4; ks < sb1 * 4; ++ks, ++kc) {
+                    if (C::MI == 2 && ((ks - sb0 * 4) & 1) != j) continue;
                     const RingPos<C> rp(kc >> 2, (int)(kc & 3));
                     const int sa = rp.a_stage, s = kc % C::NB;
                     if (!mbar_wait(&a_full[sa], rp.a_phase) ||
@@ -476,13 +488,15 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                     }
                     umma_commit(&a_empty[sa]);
                     umma_commit(&b_empty[s]);
-                    ++kc;
+                    acc = true;
+                    any = true;
+                    last_kc = kc;
                 }
                 if (*abort_flag) break;
                 umma_commit(&acc_full[b]);
             }
-            // wait for the last MMAs to retire before TMEM can be released
-            if (kc > 0) mbar_wait(&b_empty[(kc - 1) % C::NB], ((kc - 1) / C::NB) & 1);
+            // wait for this issuer's last MMAs to retire before TMEM can be released
+            if (any) mbar_wait(&b_empty[last_kc % C::NB], (last_kc / C::NB) & 1);
         }
     } else if (warp < 2 + kEpiWarps) {
         // ---------------------------------------------------------- epilogue
@@ -503,7 +517,21 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             tc_fence_after();
             const int n = t.nt * BM + nl;
             const int64_t col = (int64_t)t.set * N + n;
-            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN);
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * C::MI * BN);
+            // the tile's accumulator: issuer 0's plus (MI == 2) issuer 1's, in that order
+            auto load_acc = [&](int c0, uint32_t (&r)[32]) {
+                tmem_ld_32x32b_x32(taddr + c0, r);
+                if constexpr (C::MI == 2) {
+                    uint32_t r2[32];
+                    tmem_ld_32x32b_x32(taddr + BN + c0, r2);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj)
+                        r[jj] = __float_as_uint(__uint_as_float(r[jj]) + __uint_as_float(r2[jj]));
+                } else {
+                    tmem_ld_wait();
+                }
+            };
             bool last = true;
             if (S > 1) {
                 // partial slot (tile, split): [quadrant][row][32 columns] fp32
@@ -511,8 +539,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
 #pragma unroll 1
                 for (int c0 = 0; c0 < t.rows; c0 += 32) {
                     uint32_t r[32];
-                    tmem_ld_32x32b_x32(taddr + c0, r);
-                    tmem_ld_wait();
+                    load_acc(c0, r);
                     const int jn = min(32, t.rows - c0);
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
@@ -587,8 +614,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
 #pragma unroll 1
                 for (int c0 = 0; c0 < t.rows; c0 += 32) {
                     uint32_t r[32];
-                    tmem_ld_32x32b_x32(taddr + c0, r);
-                    tmem_ld_wait();
+                    load_acc(c0, r);
                     const int64_t y0 = (int64_t)(t.row0 + c0) * grp.ldy + col;
                     const int jn = min(32, t.rows - c0);
                     if (grp.row_exp) {  // exact power-of-two row scales (warp-uniform branch)
@@ -859,14 +885,19 @@ int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2,
         }
     }
     const int64_t units = max_tiles * grp.splits;
-    // small token counts: A stages in tensor memory (no shared-memory A
-    // stores or A reads by the MMA); large: the 256-token tile, which halves
-    // the weight traffic per FLOP and needs all 512 TMEM columns for its two
-    // accumulators
+    // up to 64 tokens: two MMA issuers (their accumulators and the A stages
+    // all in tensor memory); up to 128: A stages in tensor memory (no
+    // shared-memory A stores or A reads by the MMA); larger: the 256-token
+    // tile, which halves the weight traffic per FLOP and needs all 512 TMEM
+    // columns for its two accumulators
+    using C64 = Cfg<64, 1, 8, 6, 6, true, 2>;
     using C128 = Cfg<128, 1, 4, 5, 3, true>;
     using C256 = Cfg<256, 1, 3, 3, 3>;
     int rc;
-    if (BN == 128)
+    if (BN == 64)
+        rc = bf ? launch<C64, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st)
+                : launch<C64, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st);
+    else if (BN == 128)
         rc = bf ? launch<C128, __nv_bfloat16>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st)
                 : launch<C128, __half>(tw, tw2, tx, M, N, K, y, y_dtype, grp, units, sms, st);
     else
@@ -922,7 +953,7 @@ int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void
     FTC_REQUIRE(row_stride >= (K / 256) * 144 && row_stride % 16 == 0 && (uintptr_t)w % 16 == 0,
                 FTC_E_INVALID, "ftc_gemm: weight rows must be 16-byte aligned");
     FTC_REQUIRE((uintptr_t)x % 16 == 0, FTC_E_INVALID, "ftc_gemm: activations must be 16-byte aligned");
-    const int BN = M <= 128 ? 128 : 256;
+    const int BN = M <= 64 ? 64 : M <= 128 ? 128 : 256;
     CUtensorMap tw;
     XMaps tx;
     if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm"))) return rc;
@@ -948,7 +979,7 @@ int gemm_q4k_rowscaled(const void* w, int64_t N, int64_t K, int64_t row_stride, 
     FTC_REQUIRE(row_stride >= (K / 256) * 144 && row_stride % 16 == 0 && (uintptr_t)w % 16 == 0 &&
                     (uintptr_t)x16 % 16 == 0,
                 FTC_E_INVALID, "ftc_gemm_rowscaled: operands must be 16-byte aligned");
-    const int BN = M <= 128 ? 128 : 256;
+    const int BN = M <= 64 ? 64 : M <= 128 ? 128 : 256;
     CUtensorMap tw;
     XMaps tx;
     if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm_rowscaled")))
@@ -985,7 +1016,7 @@ int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64
     FTC_REQUIRE((uintptr_t)x % 16 == 0, FTC_E_INVALID,
                 "gemm_q4k_grouped: activations must be 16-byte aligned");
     FTC_REQUIRE(ldy >= n_sets * N, FTC_E_INVALID, "gemm_q4k_grouped: output pitch too small");
-    const int BN = max_rows_per_group <= 128 ? 128 : 256;
+    const int BN = max_rows_per_group <= 64 ? 64 : max_rows_per_group <= 128 ? 128 : 256;
     CUtensorMap tw, tw2;
     XMaps tx;
     if ((rc = weight_map(&tw, w, N, K, row_stride, G, plane_stride, "gemm_q4k_grouped"))) return rc;

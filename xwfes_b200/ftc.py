@@ -12,7 +12,8 @@ import numpy as np
 from . import formats as F
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libftcuda.so")
+# FTC_LIB overrides the library path (e.g. a build of the sources elsewhere)
+LIB_PATH = os.environ.get("FTC_LIB") or os.path.join(PKG, "libftcuda.so")
 
 _p = C.c_void_p
 _i64 = C.c_int64
