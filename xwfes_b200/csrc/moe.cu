@@ -284,6 +284,7 @@ int grid_for(int64_t n) {
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 constexpr int64_t kMaxFf = 49152;  // h row kept in shared memory by moe_silu_scale
+constexpr int64_t kFusedSiluMaxFf = 8192;  // decode down GEMV takes silu(gate) * up itself
 
 // Decode (few tokens): every (token, slot) pair is a GEMV over its expert's
 // weights, which streams each chosen expert once at HBM speed; the
@@ -414,8 +415,11 @@ int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dty
                 g.sel_slot[i] = r;
             }
         if ((rc = gemv_q4k_batch(g, st))) return rc;
-        moe_silu_f32<<<grid_for((int64_t)R * F), 256, 0, st>>>(gu, R, F, h32);
-        FTC_CUDA(cudaGetLastError());
+        // down: for short n_ff the GEMV takes silu(gate) * up from the pair's
+        // [gate | up] row as it loads its activation (the same fp32
+        // expression as moe_silu_f32), one launch less; for long rows every
+        // CTA reading the whole [gate | up] row costs more than the launch
+        // (n_ff = 14336: 72 -> 78 us per layer), so moe_silu_f32 runs first
         GemvSpec dn = {};
         dn.P = R;
         dn.K = F;
@@ -424,14 +428,23 @@ int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dty
         dn.sel = idx;
         dn.sel_stride = d->dn_plane_stride;
         dn.sel_max = E - 1;
+        dn.x_up = F <= kFusedSiluMaxFf ? F : 0;
         for (int r = 0; r < R; ++r) {
             dn.W[r] = static_cast<const uint8_t*>(d->down_exps);
             dn.N[r] = K;
             dn.y[r] = yd + (int64_t)r * K;
-            dn.x[r] = h32 + (int64_t)r * F;
+            dn.x[r] = gu + (int64_t)r * 2 * F;
             dn.sel_slot[r] = r;
         }
-        if ((rc = gemv_q4k_batch(dn, st))) return rc;
+        rc = dn.x_up ? gemv_q4k_batch(dn, st) : FTC_E_UNSUPPORTED;
+        if (rc == FTC_E_UNSUPPORTED) {
+            moe_silu_f32<<<grid_for((int64_t)R * F), 256, 0, st>>>(gu, R, F, h32);
+            FTC_CUDA(cudaGetLastError());
+            dn.x_up = 0;
+            for (int r = 0; r < R; ++r) dn.x[r] = h32 + (int64_t)r * F;
+            rc = gemv_q4k_batch(dn, st);
+        }
+        if (rc) return rc;
         moe_combine<<<grid_for((int64_t)T * K / 4), 256, 0, st>>>(yd, nullptr, nullptr, idx, wts,
                                                                   rank, (int)T, U, K, out);
         FTC_CUDA(cudaGetLastError());

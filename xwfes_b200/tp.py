@@ -25,7 +25,8 @@ into one weight, and so are its gate and up rows, so each group is one
 matmul launch (rows are independent: the stacked product is the row-wise
 concatenation of the separate ones, bit for bit); silu(gate) * up is taken
 on the [gate | up] output rows by one kernel that also produces the fp16
-operand of the down GEMM.  Matmuls: M <= 8 tokens use the decode
+operand of the down GEMM (at one token, by the down GEMV itself as it loads
+its activation: ftc_mul_mat_vec_silu).  Matmuls: M <= 8 tokens use the decode
 GEMV (fp32 activations), larger M the tcgen05 GEMM on fp16 rows with
 power-of-two row scales (ftc_rows_to_f16 / ftc_gemm_rowscaled), fp32 outputs.
 The allreduce sums fp32 partials: small ones (decode-sized M) through
@@ -45,6 +46,10 @@ from . import formats as F, synth as S
 # config 4: Llama-3-70B layer shapes
 DIMS_70B = {"n_embd": 8192, "n_ff": 28672, "n_q": 8192, "n_kv": 1024}
 QK = 256  # Q4_K super-block
+# longest n_ff slice whose down GEMV takes silu(gate) * up itself (measured:
+# at 28672 the fused GEMV is 11 us slower than SiLU + GEMV, each CTA then
+# reading 229 KB of [gate | up]; at 3584 it saves the SiLU launch)
+FUSED_SILU_MAX_K = 8192
 
 
 def col_rows(n, G, r):
@@ -151,6 +156,14 @@ class CudaOps:
         ``peer`` (one token) the product is also summed over the ranks."""
         ftc, M = self.ftc, gu.shape[0]
         wt, wn, wk = w
+        if M == 1 and wk == n and n <= FUSED_SILU_MAX_K and gu.is_contiguous() and n % 4 == 0:
+            # one token, a rank's short n_ff slice: the SiLU product is taken
+            # as the GEMV loads its activation (no separate launch), with the
+            # allreduce fused too.  Every CTA of that GEMV reads the whole
+            # [gate | up] row, so for long rows the separate SiLU is faster.
+            if peer is not None:
+                return peer.silu_mul_mat_vec_sum(wt, F.Q4_K, wn, wk, gu, up_offset=n)
+            return ftc.mul_mat_vec_silu(wt, F.Q4_K, wn, wk, gu, up_offset=n)
         if M <= self.gemv_max_m:
             h = ftc.silu_mul_rows(gu, n)
             if peer is not None:
