@@ -936,6 +936,24 @@ def run_ncu_probe():
     return 0
 
 
+def run_ncu_imma_probe():
+    """Three batch-4 grouped gate+up launches (2 x 14336x4096 Q4_K, 66 MB, 4
+    tokens): the small case for ncu captures of the integer tensor-core GEMV
+    (gemv_q4k_imma)."""
+    import torch
+    from xwfes_b200 import ftc
+    dev = torch.device("cuda", 0)
+    ws = [torch.from_numpy(S.weight(F.Q4_K, 14336, 4096, seed=0, name=f"L0.{m}")).to(dev)
+          for m in ("gate", "up")]
+    x = torch.from_numpy(S.activations_f32(4, 4096, seed=0, name="ffn_in")).to(dev)
+    for _ in range(3):
+        ys = ftc.mul_mat_vec_multi(ws, F.Q4_K, [14336, 14336], 4096, x)
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": "gemv_q4k_imma gate+up 2x14336x4096 M=4 x3", "y0": float(ys[0][0, 0]),
+                      "status": ftc.device_status()}))
+    return 0
+
+
 def run_ncu_gemm_probe():
     """Three config-3 dequant-GEMM launches (W 33 MB, X 16 MB, Y 58 MB on the
     device): the small case for ncu captures of the tensor-core kernel."""
@@ -1163,6 +1181,9 @@ def main():
     ap.add_argument("--ncu", action="store_true",
                     help="profiling mode: a few launches of the dominant kernel "
                          "(grouped gate+up Q4_K GEMV) on one layer copy, no timing")
+    ap.add_argument("--ncu-imma", action="store_true",
+                    help="profiling mode: three batch-4 grouped gate+up launches of the integer "
+                         "tensor-core GEMV (2 x 14336x4096), no timing")
     ap.add_argument("--ncu-gemm-split", action="store_true",
                     help="profiling mode: three split-K dequant-GEMM launches on a TP rank's "
                          "q/k/v shard (1280x8192, M=16), no timing")
@@ -1181,6 +1202,8 @@ def main():
 
     if args.ncu:
         return run_ncu_probe()
+    if args.ncu_imma:
+        return run_ncu_imma_probe()
     if args.ncu_gemm:
         return run_ncu_gemm_probe()
     if args.ncu_gemm_split:
