@@ -83,11 +83,13 @@ def make_weights(seed=0):
 
 class ClockSampler:
     """nvidia-smi samples (every 100 ms) of one GPU's clocks, power, load and
-    throttle reasons over the whole measured run; the GPU is picked by its
-    PCI bus id (nvidia-smi's domain:bus:device.function form).  The summary
-    keeps the samples taken under load (utilization >= 50 %), so a timed
-    region shorter than the sampling period is still covered by the kernels
-    around it that run the same code."""
+    throttle reasons, each stamped with the host time it arrived; the GPU is
+    picked by its PCI bus id (nvidia-smi's domain:bus:device.function form).
+    The timed region of a step (K x ~0.3 ms) is shorter than the sampling
+    period, so the caller replays the same step graph back to back for a
+    couple of seconds right after it and marks that window; the summary
+    keeps the samples inside the window (or, without one, the samples taken
+    at >= 50 % utilization)."""
     Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -96,6 +98,7 @@ class ClockSampler:
         self.bus = (bus_id or "").lower()
         self.lines = []
         self.proc = None
+        self.window = None
 
     @staticmethod
     def bus_id_of(props):
@@ -120,7 +123,15 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def load_window(self, replay, seconds=2.0):
+        """Run replay() (one batch of back-to-back step replays, synchronised)
+        until `seconds` have passed and mark that span as the window."""
+        t0 = time.time()
+        while time.time() - t0 < seconds:
+            replay()
+        self.window = (t0, time.time())
 
     def __exit__(self, *a):
         proc, self.proc = self.proc, None
@@ -135,7 +146,9 @@ class ClockSampler:
     def summary(self):
         sm, mx, pw, reasons, n_all = [], None, [], set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        rows = [[v.strip() for v in ln.split(",")] for ln in self.lines]
+        w = self.window
+        rows = [[v.strip() for v in ln.split(",")] for t, ln in self.lines
+                if w is None or w[0] + 0.15 <= t <= w[1]]
         rows = [f for f in rows if len(f) >= 9]
         mine = [f for f in rows if self.bus and f[0].lower().endswith(self.bus[-12:])]
         matched = bool(mine)
@@ -149,7 +162,7 @@ class ClockSampler:
                 continue
             n_all += 1
             mx = mxc
-            if util < 50:
+            if w is None and util < 50:
                 continue
             sm.append(clk)
             pw.append(p)
@@ -160,7 +173,9 @@ class ClockSampler:
                 "power_w_median": statistics.median(pw) if pw else None,
                 "reasons": sorted(reasons), "samples": len(sm), "samples_all": n_all,
                 "gpu": self.bus if matched else "unmatched (first GPU listed)",
-                "window": "whole run (set-up excluded), samples with utilization >= 50 %"}
+                "window": (f"{w[1] - w[0]:.1f} s of back-to-back replays of the timed step graph, "
+                           "right after the timed region" if w else
+                           "whole run (set-up excluded), samples with utilization >= 50 %")}
 
 
 # ------------------------------------------------------------- our path
@@ -278,6 +293,15 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
     barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
+
+    # clocks under this load: the same step graph back to back, untimed
+    def replay_batch():
+        with torch.cuda.stream(stream):
+            for _ in range(100):
+                graph.replay()
+        torch.cuda.synchronize()
+
+    clk.load_window(replay_batch)
 
     # dominant kernel alone: the gate/up launch over the 8 layer copies, graph-replayed
     g2 = torch.cuda.CUDAGraph()

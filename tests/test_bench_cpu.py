@@ -35,3 +35,22 @@ def test_warmup_below_three_is_refused():
     r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--warmup", "2"],
                        cwd=ROOT, capture_output=True, text=True, timeout=120)
     assert r.returncode != 0 and "warmup" in r.stderr
+
+
+def test_clock_summary_keeps_the_load_window():
+    """Samples outside the marked replay window (idle clocks before and
+    after it) are left out; without a window, only samples under load."""
+    import time
+    import bench
+    c = bench.ClockSampler("00000000:e5:00.0")
+    t = time.time()
+    c.lines = [(t + 0.1 * i, f"00000000:E5:00.0, {1965 if 10 <= i < 30 else 600}, 1965, 700, "
+                f"{90 if 10 <= i < 30 else 0}, Not Active, Not Active, Not Active, "
+                f"{'Active' if i == 35 else 'Not Active'}") for i in range(40)]
+    s = c.summary()
+    assert s["samples"] == 20 and s["sm_mhz"] == 1965.0 and s["reasons"] == []
+    c.window = (t + 1.0, t + 3.0)
+    s = c.summary()
+    assert s["samples"] == s["samples_all"] == 19
+    assert s["sm_mhz"] == 1965.0 and s["reasons"] == []
+    assert s["gpu"] == "00000000:e5:00.0" and "replays" in s["window"]
