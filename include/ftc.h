@@ -101,7 +101,14 @@ int ftc_backend_cached_bytes(ftc_backend* be, uint64_t* bytes);
  * (ft/src/cpu_backend.cpp:90-104), which folds all M rows into y[n], every
  * row m gets its own output row.  Q4_K with M > 8 runs on the tensor cores
  * (ftc_rows_to_f16 + ftc_gemm_rowscaled: fp16 operands, fp32 accumulation);
- * everything else on the fp32 GEMV, 8 rows per pass over the weight. */
+ * everything else on the fp32 GEMV, 8 rows per pass over the weight.
+ * Per-call latency: x and y of up to 1 MiB move through the backend's pinned
+ * buffers by a copy kernel and direct stores instead of the copy engines,
+ * and a call on an uploaded weight replays a CUDA graph of its copy-in,
+ * matmul and copy-out, captured on the first call with that (weight, M, K,
+ * N, dtype) and kept until the staging buffers move or the backend is
+ * destroyed.  FTC_BACKEND_GRAPHS=0 in the environment at ftc_backend_create
+ * turns the graphs off. */
 int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K,
                        const void* w_host, int dtype, int64_t N, float* y);
 

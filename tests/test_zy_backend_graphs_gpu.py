@@ -1,5 +1,6 @@
-"""ftc_backend_matmul with FTC_BACKEND_GRAPHS=1: each (weight, shape) call
-is captured once and replayed as a CUDA graph.  The replayed work is the
+"""ftc_backend_matmul's graph replay (the default; FTC_BACKEND_GRAPHS=0 at
+creation turns it off): each (weight, shape) call is captured once and
+replayed as a CUDA graph.  The replayed work is the
 same kernels on the same buffers, so every output must equal the direct
 path's bit for bit: repeated calls (replays), a new shape, a larger call that
 moves the staging buffers (all graphs dropped and captured again), and a
@@ -24,9 +25,9 @@ def ftc():
 
 def backend(ftc, monkeypatch, graphs):
     if graphs:
-        monkeypatch.setenv("FTC_BACKEND_GRAPHS", "1")
-    else:
         monkeypatch.delenv("FTC_BACKEND_GRAPHS", raising=False)
+    else:
+        monkeypatch.setenv("FTC_BACKEND_GRAPHS", "0")
     return ftc.CudaBackend(0)
 
 

@@ -94,6 +94,7 @@ int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void
              int64_t M, void* y, int y_dtype, cudaStream_t st);
 int gemm_q4k_rowscaled(const void* w, int64_t N, int64_t K, int64_t row_stride, const void* x16,
                        int64_t M, void* y, int y_dtype, const int32_t* row_exp, cudaStream_t st);
+int copy_f32(float* dst, const float* src, int64_t n, cudaStream_t st);
 int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld, void* out,
                 int32_t* row_exp, cudaStream_t st);
 int silu_mul_rows(const float* gu, int64_t rows, int64_t n, int64_t ld, float* h, void* out16,
@@ -137,6 +138,10 @@ using namespace ftc;
 namespace {
 
 // Growable device / pinned-host buffer owned by a backend.
+// ftc_backend_matmul moves x and y of at most this many bytes with a copy
+// kernel and direct stores into pinned memory instead of the copy engines.
+constexpr size_t kKernelCopyMax = 1 << 20;
+
 struct DevBuf {
     void* p = nullptr;
     size_t cap = 0;
@@ -182,10 +187,11 @@ struct ftc_backend {
 
     // ftc_backend_matmul's per-call work (copy in, GEMV or GEMM, copy out)
     // captured once per (weight, shape) and replayed as a CUDA graph: one
-    // launch instead of three to six API calls.  On with
-    // FTC_BACKEND_GRAPHS=1 at creation.  The graphs hold the staging
+    // launch instead of three to six API calls.  On unless
+    // FTC_BACKEND_GRAPHS=0 at creation.  The graphs hold the staging
     // buffers' addresses, so all of them are dropped when a buffer moves.
     bool use_graphs = false;
+    bool uva = false;  // pinned host buffers are addressable from kernels
     std::map<std::tuple<const void*, int64_t, int64_t, int64_t, int>, cudaGraphExec_t> graphs;
     void* graph_bufs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     void drop_graphs() {
@@ -289,7 +295,8 @@ int ftc_backend_create(int device, ftc_backend** out) {
     ftc_backend* be = new ftc_backend();
     be->device = device;
     const char* g = std::getenv("FTC_BACKEND_GRAPHS");
-    be->use_graphs = g && std::strcmp(g, "1") == 0;
+    be->use_graphs = !(g && std::strcmp(g, "0") == 0);
+    be->uva = prop.unifiedAddressing != 0;
     be->name = std::string("CUDA:") + prop.name;
     be->mem = prop.totalGlobalMem;
     cudaError_t e = cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking);
@@ -398,10 +405,22 @@ int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K, co
     if (tc && (rc = be->dtmp.ensure(x16b + (size_t)M * 4))) return rc;
     std::memcpy(be->pin_in.p, x, xb);
     const float* dx = static_cast<const float*>(be->dx.p);
-    float* dy = static_cast<float*>(be->dy.p);
+    // Small calls (decode): a copy engine transfer on each side of the GEMV
+    // costs more than the GEMV (~7 us each on B200).  Instead a copy kernel
+    // reads x from the pinned buffer (the GEMV behind it starts early and
+    // prefetches its weights meanwhile), and the GEMV stores y straight into
+    // the pinned output buffer; both reached through unified addressing.
+    const bool small = be->uva && !tc && xb <= kKernelCopyMax && yb <= kKernelCopyMax;
+    float* dy = small ? static_cast<float*>(be->pin_out.p) : static_cast<float*>(be->dy.p);
     cudaStream_t st = be->stream;
     auto enqueue = [&]() -> int {
-        FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, xb, cudaMemcpyHostToDevice, st));
+        if (small) {
+            const int crc = copy_f32(static_cast<float*>(be->dx.p),
+                                     static_cast<const float*>(be->pin_in.p), M * K, st);
+            if (crc) return crc;
+        } else {
+            FTC_CUDA(cudaMemcpyAsync(be->dx.p, be->pin_in.p, xb, cudaMemcpyHostToDevice, st));
+        }
         int erc;
         if (tc) {
             void* x16 = be->dtmp.p;
@@ -416,7 +435,7 @@ int ftc_backend_matmul(ftc_backend* be, const float* x, int64_t M, int64_t K, co
                     return erc;
             }
         }
-        FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, st));
+        if (!small) FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dy, yb, cudaMemcpyDeviceToHost, st));
         return FTC_OK;
     };
     // Graphs only for resident weights: a streamed weight's copy is per call.

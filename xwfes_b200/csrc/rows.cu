@@ -12,15 +12,39 @@
 //                 into fp32 rows, or straight into fp16 rows with their
 //                 power-of-two scales (bit for bit rows_to_f16 of the fp32
 //                 result).
+//   copy_f32      a small float copy as a kernel, for the per-call host-buffer
+//                 path: x from pinned host memory into device memory (reached
+//                 through unified addressing), so that the launch behind it
+//                 on the same stream can start early instead of waiting for a
+//                 copy engine.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace ftc {
 namespace {
+
+// dst[i] = src[i]; 16-byte moves when both are 16-byte aligned.  The next
+// grid on the stream may start at once (programmatic dependent launch); it
+// reads dst only after its griddepcontrol.wait, i.e. after this grid ends.
+__global__ void copy_f32_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n,
+                                int vec) {
+    grid_launch_dependents();
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+    if (vec) {
+        const int64_t n4 = n / 4;
+        for (int64_t i = tid; i < n4; i += nth)
+            reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+        for (int64_t i = 4 * n4 + tid; i < n; i += nth) dst[i] = src[i];
+    } else {
+        for (int64_t i = tid; i < n; i += nth) dst[i] = src[i];
+    }
+}
 
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
@@ -156,6 +180,20 @@ int rows_to_f16(const void* x, int x_dtype, int64_t rows, int64_t K, int64_t ld,
                                                       row_exp);
     else
         return set_error(FTC_E_UNSUPPORTED, "ftc_rows_to_f16: x must be fp32, bf16 or fp16");
+    FTC_CUDA(cudaGetLastError());
+    return FTC_OK;
+}
+
+int copy_f32(float* dst, const float* src, int64_t n, cudaStream_t st) {
+    FTC_REQUIRE(dst && src && n >= 0, FTC_E_INVALID, "copy_f32: bad argument");
+    if (n == 0) return FTC_OK;
+    const int vec = ((uintptr_t)dst % 16 == 0 && (uintptr_t)src % 16 == 0) ? 1 : 0;
+    // one 16-byte move per thread: every load of a pinned source is in
+    // flight at once, so the copy costs about one PCIe round trip
+    const int64_t per = vec ? 4 : 1;
+    const int grid = (int)std::max<int64_t>(
+        1, std::min<int64_t>((n + 256 * per - 1) / (256 * per), (int64_t)device_sms()));
+    copy_f32_kernel<<<grid, 256, 0, st>>>(dst, src, n, vec);
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;
 }

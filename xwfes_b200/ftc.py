@@ -471,6 +471,7 @@ class HostTensor:
         self.name = name
         if self.data.nbytes < self.row_stride_bytes() * self.ne[1] * self.ne[2] * self.ne[3]:
             raise ValueError("HostTensor: data smaller than its shape")
+        self._base = self.data.ctypes.data  # the array owns its buffer: fixed address
 
     def cols(self):
         return self.ne[0]
@@ -485,7 +486,7 @@ class HostTensor:
         return self.row_stride_bytes() * self.ne[1]
 
     def ptr(self, offset=0):
-        return self.data.ctypes.data + offset
+        return self._base + offset
 
     def slice(self, e):
         """Host address of expert plane e (HostTensor::slice)."""
@@ -560,10 +561,13 @@ class CudaBackend:
 
     def matmul(self, x, M, K, W, y):
         """IBackend::matmul: x fp32 [M][K] host, y fp32 [M][N] host (written)."""
+        n = W.ne[1]
         assert x.dtype == np.float32 and x.flags.c_contiguous and x.size >= M * K
-        assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * W.rows()
-        check(lib().ftc_backend_matmul(self._h, x.ctypes.data, M, K, W.ptr(), W.dtype,
-                                       W.rows(), y.ctypes.data), "ftc_backend_matmul")
+        assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * n
+        rc = _lib.ftc_backend_matmul(self._h, x.ctypes.data, M, K, W._base, W.dtype, n,
+                                     y.ctypes.data)
+        if rc:
+            raise FtcError("ftc_backend_matmul", rc, last_error())
 
     def matmul_down_axpy(self, x, M, n_in, W, y):
         """ft::matmul_down_axpy: y[m] += x_m . W over the first ``n_in`` rows of
