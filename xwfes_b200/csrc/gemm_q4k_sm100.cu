@@ -106,6 +106,12 @@ struct Cfg {
     // dequant warps, read by the MMA as its A operand), after the
     // accumulators; otherwise in shared memory (128-byte swizzle).
     static constexpr bool ATM = ATM_;
+    // On the 256-token tile every pipeline wait sleeps between tests (the
+    // thread wakes when the phase completes), so waiting warps leave their
+    // issue slots to the dequant and MMA warps (measured: M = 2048 and 8192
+    // 2.7-3.7 % faster).  The smaller tiles, bound by the dequant warps'
+    // latency, lose to the wake-up delay (2-4 % at 16-64 tokens) and poll.
+    static constexpr uint32_t SLEEP_NS = BN_ >= 256 ? 20000u : 0u;
     static constexpr int NA = DT * NAT;           // dequantized weight stages
     static constexpr int RAW = DT * RAWT;         // raw super-block slots
     static constexpr int WARPS = 2 + kEpiWarps + DT * kTeamWarps + 1 + (MI - 1);
@@ -405,7 +411,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 const uint32_t bytes = (uint32_t)xbox_rows(xb, BN) * BK * 2;
                 for (int ks = sb0 * 4; ks < sb1 * 4; ++ks) {
                     const int s = kc % C::NB;
-                    if (!mbar_wait(&b_empty[s], ((kc / C::NB) & 1) ^ 1)) { *abort_flag = 1; break; }
+                    if (!mbar_wait(&b_empty[s], ((kc / C::NB) & 1) ^ 1, C::SLEEP_NS)) {
+                        *abort_flag = 1;
+                        break;
+                    }
                     mbar_arrive_expect_tx(&b_full[s], bytes);
                     tma_load_2d(sB + s * C::B_BYTES, xm, ks * BK, t.row0, &b_full[s], pol_x);
                     ++kc;
@@ -413,7 +422,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             }
             if (*abort_flag) {  // let issued copies land before the CTA leaves
                 for (uint32_t j = kc > (uint32_t)C::NB ? kc - C::NB : 0; j < kc; ++j)
-                    mbar_wait(&b_full[j % C::NB], (j / C::NB) & 1);
+                    mbar_wait(&b_full[j % C::NB], (j / C::NB) & 1, C::SLEEP_NS);
             }
         }
     } else if (warp == C::RAW_WARP) {
@@ -431,7 +440,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 const CUtensorMap* wm = t.set ? &tm_w2 : &tm_w;
                 for (int sb = sb0; sb < sb1; ++sb) {
                     const RingPos<C> rp(rc, 0);
-                    if (!mbar_wait(&raw_empty[rp.raw_slot], rp.raw_phase ^ 1)) { *abort_flag = 1; break; }
+                    if (!mbar_wait(&raw_empty[rp.raw_slot], rp.raw_phase ^ 1, C::SLEEP_NS)) {
+                        *abort_flag = 1;
+                        break;
+                    }
                     mbar_arrive_expect_tx(&raw_full[rp.raw_slot], kRawBytes);
                     tma_load_3d(sRaw + rp.raw_slot * kRawBytes, wm, sb * 144, t.nt * BM, t.g,
                                 &raw_full[rp.raw_slot], pol_w);
@@ -441,7 +453,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             if (*abort_flag) {  // let issued copies land before the CTA leaves
                 for (uint32_t j = rc > (uint32_t)C::RAW ? rc - C::RAW : 0; j < rc; ++j) {
                     const RingPos<C> rp(j, 0);
-                    mbar_wait(&raw_full[rp.raw_slot], rp.raw_phase);
+                    mbar_wait(&raw_full[rp.raw_slot], rp.raw_phase, C::SLEEP_NS);
                 }
             }
         }
@@ -460,7 +472,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 const int tile = unit_at(u, split, sb0, sb1);
                 // MMA N = the tile's tokens rounded up to 16
                 const uint32_t idesc = idesc_f16(fmt, BM, (uint32_t)min(BN, (tile_at(tile).rows + 15) & ~15));
-                if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
+                if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1, C::SLEEP_NS)) {
+                    *abort_flag = 1;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)((b * C::MI + j) * BN);
                 bool acc = false;  // the issuer's first k-step of the unit overwrites
@@ -468,8 +483,8 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                     if (C::MI == 2 && ((ks - sb0 * 4) & 1) != j) continue;
                     const RingPos<C> rp(kc >> 2, (int)(kc & 3));
                     const int sa = rp.a_stage, s = kc % C::NB;
-                    if (!mbar_wait(&a_full[sa], rp.a_phase) ||
-                        !mbar_wait(&b_full[s], (kc / C::NB) & 1)) {
+                    if (!mbar_wait(&a_full[sa], rp.a_phase, C::SLEEP_NS) ||
+                        !mbar_wait(&b_full[s], (kc / C::NB) & 1, C::SLEEP_NS)) {
                         *abort_flag = 1;
                         break;
                     }
@@ -496,7 +511,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 umma_commit(&acc_full[b]);
             }
             // wait for this issuer's last MMAs to retire before TMEM can be released
-            if (any) mbar_wait(&b_empty[last_kc % C::NB], (last_kc / C::NB) & 1);
+            if (any) mbar_wait(&b_empty[last_kc % C::NB], (last_kc / C::NB) & 1, C::SLEEP_NS);
         }
     } else if (warp < 2 + kEpiWarps) {
         // ---------------------------------------------------------- epilogue
@@ -513,7 +528,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             int split, sb0, sb1;
             const int tile = unit_at(u, split, sb0, sb1);
             const TileRef t = tile_at(tile);
-            if (!mbar_wait_warp(&acc_full[b], (i >> 1) & 1)) { *abort_flag = 1; break; }
+            if (!mbar_wait_warp(&acc_full[b], (i >> 1) & 1, C::SLEEP_NS)) {
+                *abort_flag = 1;
+                break;
+            }
             tc_fence_after();
             const int n = t.nt * BM + nl;
             const int64_t col = (int64_t)t.set * N + n;
@@ -662,7 +680,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 if ((int)(rc % C::DT) != team) continue;
                 const RingPos<C> rp0(rc, 0);
                 const int rs = rp0.raw_slot;
-                if (!mbar_wait_warp(&raw_full[rs], rp0.raw_phase)) { *abort_flag = 1; break; }
+                if (!mbar_wait_warp(&raw_full[rs], rp0.raw_phase, C::SLEEP_NS)) {
+                    *abort_flag = 1;
+                    break;
+                }
                 const uint8_t* blk = sRaw + rs * kRawBytes + r * 144;
                 float fdl[8], fnml[8];      // per sub-block: d*sc, -dmin*m
                 uint32_t dl2[8], nml2[8];   // the same as fp16 pairs (fp16 operands)
@@ -671,7 +692,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 for (int g = 0; g < 4; ++g) {
                     const RingPos<C> rp(rc, g);
                     const int s = rp.a_stage;
-                    if (!mbar_wait_warp(&a_empty[s], rp.a_phase ^ 1)) { *abort_flag = 1; break; }
+                    if (!mbar_wait_warp(&a_empty[s], rp.a_phase ^ 1, C::SLEEP_NS)) {
+                        *abort_flag = 1;
+                        break;
+                    }
                     if constexpr (C::ATM) tc_fence_after();  // the MMA that read the stage is done
                     const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g + 16 * h);
                     const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};

@@ -74,16 +74,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// The same test, but a thread whose phase is not complete yet may sleep for
+// up to `suspend_ns` (it wakes when the phase completes): for warps that wait
+// long (a whole tile) and would otherwise take issue slots from the warps
+// doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t suspend_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ void record_timeout() {
     atomicCAS(&g_dev_status, FTC_DEVSTAT_OK, FTC_DEVSTAT_WAIT_TIMEOUT);
 }
 
 // Single-thread wait for the phase with the given parity.  Returns false
 // (and records FTC_DEVSTAT_WAIT_TIMEOUT) after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// suspend_ns > 0: sleep between tests (see mbar_try_wait_sleep).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint32_t suspend_ns = 0) {
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (suspend_ns ? mbar_try_wait_sleep(bar, parity, suspend_ns) : mbar_try_wait(bar, parity))
+            return true;
         if ((i & 255u) == 255u) {
             const uint64_t now = global_ns();
             if (t0 == 0) {
@@ -98,11 +118,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 
 // Whole-warp wait: every lane polls (so every lane acquires the phase), the
 // decision to stop is warp-uniform, and lane 0 owns the time limit.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
+                                               uint32_t suspend_ns = 0) {
     const int lane = threadIdx.x & 31;
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
-        const bool done = mbar_try_wait(bar, parity);
+        const bool done = suspend_ns ? mbar_try_wait_sleep(bar, parity, suspend_ns)
+                                     : mbar_try_wait(bar, parity);
         if (__all_sync(0xffffffffu, done)) return true;
         if ((i & 255u) == 255u) {
             int late = 0;
