@@ -911,6 +911,7 @@ def gemm_roofline(prefill_sum, short=False):
            "frac": prefill_sum["frac_of_peak"], "tflops_per_M": per_m}
     if not short:
         out.update({"peak_kind": prefill_sum["peak_kind"], "traffic": gemm_traffic_from_profiles(),
+                    "traffic_case": "14336x4096, M=8192 (one ncu capture, profiles/gemm_q4k_prefill.md)",
                     "flops_per_launch": "2*M*N*K (M=8192: 962.1 GFLOP per shape)",
                     "device_status": prefill_sum.get("device_status")})
     return out
@@ -981,12 +982,13 @@ def run_ncu_imma_probe():
 
 
 def run_ncu_gemm_probe():
-    """Three config-3 dequant-GEMM launches (W 33 MB, X 16 MB, Y 58 MB on the
-    device): the small case for ncu captures of the tensor-core kernel."""
+    """Three config-3 dequant-GEMM launches at the roofline's M = 8192 (W 33 MB,
+    X 67 MB, Y 235 MB on the device, ~0.9 ms each): the case for ncu captures
+    of the tensor-core kernel."""
     import torch
     from xwfes_b200 import ftc
     dev = torch.device("cuda", 0)
-    n, k, m = 14336, 4096, 2048
+    n, k, m = 14336, 4096, 8192
     w = torch.from_numpy(S.weight(F.Q4_K, n, k, seed=0, name=f"p.{n}x{k}")).to(dev)
     x = torch.from_numpy(S.activations_bf16(m, k, seed=0, name=f"p.{m}")).to(dev).view(
         torch.bfloat16)
@@ -994,7 +996,7 @@ def run_ncu_gemm_probe():
     for _ in range(3):
         ftc.gemm(w, F.Q4_K, n, k, x, y=y, y_dtype=F.BF16)
     torch.cuda.synchronize()
-    print(json.dumps({"probe": "gemm_q4k_tc 14336x4096 M=2048 x3", "status": ftc.device_status()}))
+    print(json.dumps({"probe": "gemm_q4k_tc 14336x4096 M=8192 x3", "status": ftc.device_status()}))
     return 0
 
 
