@@ -73,6 +73,41 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     return m;
 }
 
+// Inclusive prefix sum of v over the CTA (blockDim a multiple of 32): warp
+// scans by shuffles, then one scan of the warp totals -- two barriers
+// instead of one per doubling step.  *total gets the CTA's sum; warp_tot
+// (32 ints of shared memory) may be reused after the caller's next barrier.
+__device__ __forceinline__ int block_incl_scan(int v, int* warp_tot, int* total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_tot[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        int t = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += n;
+        }
+        if (lane < nw) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    *total = warp_tot[nw - 1];
+    return v + (w > 0 ? warp_tot[w - 1] : 0);
+}
+
+// Threads of the routing CTA: the tokens rounded up to whole warps (the
+// kernel's barriers cost in proportion to the CTA's size, and decode routes
+// one token).
+int route_threads(int64_t T) {
+    const int64_t t = std::max<int64_t>(32, (T + 31) / 32 * 32);
+    return (int)std::min<int64_t>(t, kRouteThreads);
+}
+
 // One CTA routes all T tokens and builds the expert grouping:
 //   idx[t*U+u], w[t*U+u]  chosen experts and renormalised weights
 //   counts[e], offsets[e] rows of expert e in expert order (offsets[E] = T*U)
@@ -86,7 +121,7 @@ moe_route(const float* __restrict__ logits, int T, int E, int U, int32_t* __rest
     __shared__ int s_count[kMaxExperts];
     __shared__ int s_first[kMaxExperts];
     __shared__ int s_off[kMaxExperts];
-    __shared__ int s_scan[kRouteThreads];
+    __shared__ int s_wtot[32];
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         s_count[e] = 0;
         s_first[e] = INT32_MAX;
@@ -156,21 +191,15 @@ moe_route(const float* __restrict__ logits, int T, int E, int U, int32_t* __rest
             if (t < T)
                 for (int u = 0; u < U; ++u)
                     if (idx[t * U + u] == e) slot = u;
-            s_scan[threadIdx.x] = slot >= 0;
-            __syncthreads();
-            for (int o = 1; o < (int)blockDim.x; o <<= 1) {  // inclusive scan
-                const int v = (int)threadIdx.x >= o ? s_scan[threadIdx.x - o] : 0;
-                __syncthreads();
-                s_scan[threadIdx.x] += v;
-                __syncthreads();
-            }
+            int chunk_total = 0;
+            const int incl = block_incl_scan(slot >= 0 ? 1 : 0, s_wtot, &chunk_total);
             if (slot >= 0) {
-                const int row = s_off[e] + carry + s_scan[threadIdx.x] - 1;
+                const int row = s_off[e] + carry + incl - 1;
                 pos[t * U + slot] = row;
                 row_token[row] = t;
             }
-            carry += s_scan[blockDim.x - 1];
-            __syncthreads();
+            carry += chunk_total;
+            __syncthreads();  // s_wtot is rewritten by the next chunk's scan
         }
     }
 }
@@ -379,8 +408,8 @@ int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dty
     const int E = (int)d->n_experts, U = (int)d->top_k, K = (int)d->n_embd, F = (int)d->n_ff;
     const int R = (int)(T * U);
 
-    moe_route<<<1, kRouteThreads, 0, st>>>(logits, (int)T, E, U, idx, wts, counts, offsets, rank,
-                                           pos, row_token);
+    moe_route<<<1, route_threads(T), 0, st>>>(logits, (int)T, E, U, idx, wts, counts, offsets,
+                                              rank, pos, row_token);
     FTC_CUDA(cudaGetLastError());
     if (decode_path(*d, T)) {
         // fp32 tokens, then one GEMV launch for gate and up of every (token,
@@ -492,8 +521,8 @@ int moe_route_only(const float* logits, int64_t T, int64_t E, int64_t U, int32_t
     // arrays are written, the per-token ones may be empty (null)
     FTC_REQUIRE(counts && offsets && rank && (T == 0 || (logits && idx && w && pos && row_token)),
                 FTC_E_INVALID, "ftc_moe_route: null pointer");
-    moe_route<<<1, kRouteThreads, 0, st>>>(logits, (int)T, (int)E, (int)U, idx, w, counts, offsets,
-                                           rank, pos, row_token);
+    moe_route<<<1, route_threads(T), 0, st>>>(logits, (int)T, (int)E, (int)U, idx, w, counts,
+                                              offsets, rank, pos, row_token);
     FTC_CUDA(cudaGetLastError());
     return FTC_OK;
 }
