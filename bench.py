@@ -68,6 +68,14 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def peaks_sustained():
+    """MEASURED_PEAKS.json's sustained bf16 GEMM rate (TFLOP/s), or None."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get("bf16_tflops_sustained")
+    return None
+
+
 def layer_bytes():
     w = sum(F.row_bytes(F.Q4_K, k) * n for _, n, k in LAYER)
     xy = sum(4 * (n + k) for _, n, k in LAYER)
@@ -88,8 +96,8 @@ class ClockSampler:
     The timed region of a step (K x ~0.3 ms) is shorter than the sampling
     period, so the caller replays the same step graph back to back for a
     couple of seconds right after it and marks that window; the summary
-    keeps the samples inside the window (or, without one, the samples taken
-    at >= 50 % utilization)."""
+    keeps the samples inside the window (the whole run without one) taken
+    at >= 50 % utilization."""
     Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -162,7 +170,7 @@ class ClockSampler:
                 continue
             n_all += 1
             mx = mxc
-            if w is None and util < 50:
+            if util < 50:  # idle moments (host work) inside the window too
                 continue
             sm.append(clk)
             pw.append(p)
@@ -375,6 +383,8 @@ def run_ours(args, rank, world, local_rank):
         lambda: time_e2e_direct(dev, local_rank, hosts, xs_host, e2e_steps, step_bytes), None)
 
     prefill = side_measurement("prefill", lambda: time_prefill(dev), None)
+    gemm_sustained = side_measurement("gemm_sustained",
+                                      lambda: time_gemm_sustained(dev, clk.bus), None)
     gemm_status = ftc.device_status()
     tp_block = time_tp(dev, world, rank)
     moe = side_measurement("moe", lambda: time_moe(dev), None) if world == 1 else None
@@ -436,7 +446,7 @@ def run_ours(args, rank, world, local_rank):
             "us_per_launch": round(k_ms * 1e3, 3),
             "prefill_gemm": gemm_roofline(prefill_sum, short=True),
         },
-        "roofline_gemm": gemm_roofline(prefill_sum),
+        "roofline_gemm": gemm_roofline(prefill_sum, sustained_run=gemm_sustained),
         "e2e": {
             "value": round(step_bytes / (e2e_ms * 1e-3) / 1e9 * world, 2),
             "unit": "GB/s",
@@ -880,6 +890,47 @@ def time_prefill(dev, reps=20, copies=4):
     return out
 
 
+def time_gemm_sustained(dev, bus, seconds=2.0, copies=4):
+    """Config 3 at M = 8192 (14336 x 4096) back to back for ~2 s with the
+    clocks sampled meanwhile: the GEMM's rate once the 1 kW power cap holds
+    the clocks down, next to the cuBLAS GEMM's sustained figure."""
+    import torch
+    from xwfes_b200 import ftc
+    n, k, m = 14336, 4096, 8192
+    ws = [torch.from_numpy(S.weight(F.Q4_K, n, k, seed=c, name=f"p.{n}x{k}")).to(dev)
+          for c in range(copies)]
+    x = torch.from_numpy(S.activations_bf16(m, k, seed=0, name=f"p.{m}")).to(dev).view(
+        torch.bfloat16)
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    for c in range(copies):
+        ftc.gemm(ws[c], F.Q4_K, n, k, x, y=y, y_dtype=F.BF16)
+    torch.cuda.synchronize()
+    clk = ClockSampler(bus)
+    clk.__enter__()
+    launches = 0
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def batch():
+        nonlocal launches
+        for c in range(copies * 4):
+            ftc.gemm(ws[c % copies], F.Q4_K, n, k, x, y=y, y_dtype=F.BF16)
+        launches += copies * 4
+        torch.cuda.synchronize()
+
+    try:
+        ev0.record()
+        clk.load_window(batch, seconds)
+        ev1.record()
+        torch.cuda.synchronize()
+    finally:
+        clk.__exit__(None, None, None)
+    us = ev0.elapsed_time(ev1) * 1e3 / launches
+    c = clk.summary()
+    return {"tflops": round(2.0 * m * n * k / (us * 1e-6) / 1e12, 1), "us_per_launch": round(us, 1),
+            "launches": launches, "sm_mhz": c["sm_mhz"], "power_w_median": c["power_w_median"],
+            "reasons": c["reasons"], "clock_samples": c["samples"]}
+
+
 def prefill_summary(prefill, status):
     if "error" in prefill:
         return {**prefill, "device_status": status}
@@ -895,7 +946,7 @@ def prefill_summary(prefill, status):
             "dtype": "bf16 x bf16(dequantized Q4_K) -> fp32 accumulate -> bf16"}
 
 
-def gemm_roofline(prefill_sum, short=False):
+def gemm_roofline(prefill_sum, short=False, sustained_run=None):
     """The metric's second half as a roofline object: config 3's dequant-GEMM
     (gemm_q4k_tc) at M = 8192, mean of both shapes, against the measured
     dense bf16 peak; per-M figures beside it."""
@@ -910,6 +961,14 @@ def gemm_roofline(prefill_sum, short=False):
            "achieved": prefill_sum["value"], "peak": prefill_sum["peak"], "unit": "TFLOP/s",
            "frac": prefill_sum["frac_of_peak"], "tflops_per_M": per_m}
     if not short:
+        sustained = peaks_sustained()
+        if sustained:
+            # the same number against the cuBLAS GEMM measured back to back for
+            # seconds (power-capped clocks), for context; `frac` stays on burst
+            out["frac_of_sustained"] = round(prefill_sum["value"] / sustained, 3)
+            out["peak_sustained"] = sustained
+        if sustained_run:
+            out["sustained_2s"] = sustained_run
         out.update({"peak_kind": prefill_sum["peak_kind"], "traffic": gemm_traffic_from_profiles(),
                     "traffic_case": "14336x4096, M=8192 (one ncu capture, profiles/gemm_q4k_prefill.md)",
                     "flops_per_launch": "2*M*N*K (M=8192: 962.1 GFLOP per shape)",

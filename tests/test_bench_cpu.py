@@ -39,7 +39,8 @@ def test_warmup_below_three_is_refused():
 
 def test_clock_summary_keeps_the_load_window():
     """Samples outside the marked replay window (idle clocks before and
-    after it) are left out; without a window, only samples under load."""
+    after it) are left out, and so are idle samples inside it; without a
+    window, every sample under load counts."""
     import time
     import bench
     c = bench.ClockSampler("00000000:e5:00.0")
@@ -51,6 +52,6 @@ def test_clock_summary_keeps_the_load_window():
     assert s["samples"] == 20 and s["sm_mhz"] == 1965.0 and s["reasons"] == []
     c.window = (t + 1.0, t + 3.0)
     s = c.summary()
-    assert s["samples"] == s["samples_all"] == 19
+    assert s["samples_all"] == 19 and s["samples"] == 18  # the idle sample at the end is left out
     assert s["sm_mhz"] == 1965.0 and s["reasons"] == []
     assert s["gpu"] == "00000000:e5:00.0" and "replays" in s["window"]
