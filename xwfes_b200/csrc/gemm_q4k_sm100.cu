@@ -335,6 +335,13 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     const int G = grp.G;
     const int n_tiles = (N + BM - 1) / BM;
     const int n_all = n_tiles * grp.n_sets;
+    // Programmatic dependent launch: this grid may start while the preceding
+    // kernel on the stream still runs.  Grouped launches read device counts
+    // for their tile schedule, so every thread waits here; dense launches let
+    // the raw-weight producer, the dequant and the MMA warps start at once and
+    // wait only where the preceding kernel's outputs are read (activations)
+    // or its inputs may still be read (Y, row scales, split-K scratch).
+    if (grp.counts) grid_dependency_wait();
     for (int g = threadIdx.x; g < G; g += blockDim.x) {
         const int base = grp.counts ? min(max(grp.offsets[g], 0), M) : 0;
         s_base[g] = base;
@@ -379,6 +386,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    grid_launch_dependents();  // the next kernel's prologue may overlap this grid
 
     const int tiles = s_start[G];
     const int nsb = K / 256;
@@ -400,6 +408,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         // ---------------------------------------------------------- TMA
         if (lane == 0) {
             for (int i = 0; i < kXMaps; ++i) prefetch_tensormap(&tm_x.m[i]);
+            grid_dependency_wait();  // X may be the preceding kernel's output
             const uint64_t pol_x = policy_evict_last();
             uint32_t kc = 0;
             for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
@@ -522,6 +531,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         // warp counts on its own (no barrier between the epilogue warps).
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int nl = 32 * q + lane;  // column of the tile this lane holds
+        grid_dependency_wait();  // Y, row scales and split-K scratch of earlier kernels
         int i = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
             const int b = i & 1;
@@ -773,7 +783,19 @@ int launch(const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx, int M
                                "cudaFuncSetAttribute(gemm_q4k_tc)");
     if (rc) return rc;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(max_units, sms));
-    gemm_q4k_tc<C, OP><<<grid, C::THREADS, C::SMEM, st>>>(tw, tw2, tx, M, N, K, y, ytype, grp);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e =
+        cudaLaunchKernelEx(&cfg, gemm_q4k_tc<C, OP>, tw, tw2, tx, M, N, K, y, ytype, grp);
+    if (e != cudaSuccess) return cuda_error(e, "launch gemm_q4k_tc");
     return FTC_OK;
 }
 

@@ -32,6 +32,7 @@
 
 #include "common.cuh"
 #include "gemv_batch.cuh"
+#include "sm100.cuh"
 
 namespace ftc {
 
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(kRouteThreads)
 moe_route(const float* __restrict__ logits, int T, int E, int U, int32_t* __restrict__ idx,
           float* __restrict__ wts, int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
           int32_t* __restrict__ rank, int32_t* __restrict__ pos, int32_t* __restrict__ row_token) {
+    grid_launch_dependents();  // the next launch may start its prologue
     __shared__ int s_count[kMaxExperts];
     __shared__ int s_first[kMaxExperts];
     __shared__ int s_off[kMaxExperts];
@@ -209,6 +211,7 @@ moe_route(const float* __restrict__ logits, int T, int E, int U, int32_t* __rest
 template <typename TI>
 __global__ void moe_gather_scale(const TI* __restrict__ x, const int32_t* __restrict__ row_token,
                                  int K, __half* __restrict__ xg, int32_t* __restrict__ xs) {
+    grid_launch_dependents();  // the next launch may start its prologue
     __shared__ float red[32];
     const int row = blockIdx.x;
     const TI* src = x + (int64_t)(row_token ? row_token[row] : row) * K;
@@ -227,6 +230,7 @@ __global__ void moe_gather_scale(const TI* __restrict__ x, const int32_t* __rest
 // max pass and the store pass.
 __global__ void moe_silu_scale(const float* __restrict__ gu, const int32_t* __restrict__ xs,
                                int n_ff, __half* __restrict__ h, int32_t* __restrict__ hs) {
+    grid_launch_dependents();  // the next launch may start its prologue
     extern __shared__ float sh[];
     __shared__ float red[32];
     const int row = blockIdx.x;
@@ -289,6 +293,7 @@ __global__ void moe_combine(const float* __restrict__ yd, const int32_t* __restr
 // xf = fp32 copy of x (exact for bf16 / fp16)
 template <typename TI>
 __global__ void moe_to_f32(const TI* __restrict__ x, int64_t n, float* __restrict__ xf) {
+    grid_launch_dependents();  // the next launch may start its prologue
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
         xf[i] = to_f(x[i]);
@@ -297,6 +302,7 @@ __global__ void moe_to_f32(const TI* __restrict__ x, int64_t n, float* __restric
 // h[r][i] = silu(gu[r][i]) * gu[r][n_ff + i], all fp32
 __global__ void moe_silu_f32(const float* __restrict__ gu, int rows, int n_ff,
                              float* __restrict__ h) {
+    grid_launch_dependents();  // the next launch may start its prologue
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)rows * n_ff;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / n_ff, c = i - r * n_ff;

@@ -53,6 +53,7 @@ __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float
 template <typename TI>
 __global__ void rows_to_f16_kernel(const TI* __restrict__ x, int64_t ld, int K,
                                    __half* __restrict__ out, int32_t* __restrict__ row_exp) {
+    grid_launch_dependents();  // a following GEMM / GEMV may start its prologue
     __shared__ float red[32];
     const TI* src = x + (int64_t)blockIdx.x * ld;
     float amax = 0.f;
@@ -74,6 +75,7 @@ __global__ void rows_to_f16_kernel(const TI* __restrict__ x, int64_t ld, int K,
 
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                 int64_t n, float* __restrict__ h) {
+    grid_launch_dependents();  // a following GEMM / GEMV may start its prologue
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float gv = g[i];
@@ -85,6 +87,7 @@ __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __rest
 // elements (decode-sized M has too few rows for one CTA per row).
 __global__ void silu_mul_rows_f32(const float* __restrict__ gu, int64_t ld, int64_t rows, int n,
                                   float* __restrict__ h) {
+    grid_launch_dependents();  // a following GEMM / GEMV may start its prologue
     const int64_t total = rows * n;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -101,6 +104,7 @@ template <bool kCache>
 __global__ void __launch_bounds__(1024)
 silu_mul_rows_f16(const float* __restrict__ gu, int64_t ld, int n, __half* __restrict__ out16,
                   int32_t* __restrict__ row_exp) {
+    grid_launch_dependents();  // a following GEMM / GEMV may start its prologue
     extern __shared__ float hs[];
     __shared__ float red[32];
     const float* g = gu + (int64_t)blockIdx.x * ld;
