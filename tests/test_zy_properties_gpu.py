@@ -1,11 +1,15 @@
 """Size-independent properties at the BASELINE configs' full sizes, where the
-CPU oracle would be slow, checked bit for bit:
+CPU oracle would be slow:
 
 * token permutation: every output row depends on its own token only (per-row
-  fp16 scales, row-independent MMAs, split-K partials summed in split order,
-  top-2 combine of two terms), so permuting the tokens of the config-5 MoE
-  layer, the config-3 GEMM or a batch-8 config-2 GEMV permutes the outputs
-  and changes no bit;
+  fp16 scales, row-independent MMAs, top-2 combine of two terms), so
+  permuting the tokens of a batch-8 config-2 GEMV permutes the outputs and
+  changes no bit.  The tensor-core GEMM (config 3, and the config-5 MoE
+  layer's expert GEMMs) schedules stream-K: a tile cut by a CTA's range
+  boundary sums fp32 partials of its k pieces, and which tiles are cut
+  depends on their place in the schedule, so a token moved to another tile
+  may see its k sum split differently -- there the permuted output must
+  match within 1e-5 of the output scale (the order of fp32 additions);
 * scaling by two: the decode GEMV's activation blocks carry power-of-two
   scales, so y(2x) == 2 y(x) exactly (batch 1, dp4a kernel; batch 4, fp32).
 
@@ -45,7 +49,13 @@ def test_moe_config5_token_permutation(ftc, T):
     yp = layer(logits[perm].contiguous(), x[perm].contiguous())
     torch.cuda.synchronize()
     assert ftc.device_status() == 0
-    assert torch.equal(yp, y[perm])
+    assert close_rows(yp, y[perm])
+
+
+def close_rows(a, b, tol=1e-5):
+    """max |a - b| within tol of max |b| (fp32 summation order only)."""
+    a, b = a.float(), b.float()
+    return float((a - b).abs().max()) <= tol * float(b.abs().max())
 
 
 def test_gemm_config3_row_permutation(ftc):
@@ -57,7 +67,7 @@ def test_gemm_config3_row_permutation(ftc):
     yp = ftc.gemm(w, F.Q4_K, n, k, x[perm].contiguous(), y_dtype=F.F32)
     torch.cuda.synchronize()
     assert ftc.device_status() == 0
-    assert torch.equal(yp, y[perm])
+    assert close_rows(yp, y[perm])
 
 
 def test_gemv_batch8_token_permutation(ftc):

@@ -39,6 +39,13 @@
 // fewer tokens than BN issues a narrower MMA (N rounded up to 16) and loads a
 // shorter activation box (32, 64, ... rows).
 //
+// Schedule.  Full waves of whole tiles (CTA b: tiles b, b + G, ...), then
+// the tiles of the last, partial wave stream-K: their tiles x K/256
+// super-block steps cut into one equal contiguous range per CTA, so every SM
+// gets the same work (224 tiles on 148 SMs would otherwise be 1.5 waves); a
+// tile cut by a range boundary gets fp32 partials from each piece, summed in
+// range order by the piece that arrives last.
+//
 // Row scales.  With row_exp set, output row m is multiplied by 2^row_exp[m]
 // in the epilogue (exact): callers feed fp16 rows scaled by 2^-row_exp into
 // fp16's range (ftc_rows_to_f16) and get unscaled results.
@@ -67,12 +74,9 @@ struct GemmGroups {
     int n_sets;              // weight tensors sharing the tokens (1, or 2 for gate + up)
     int64_t ldy;             // Y row pitch in elements
     const int32_t* row_exp;  // optional: Y row m is multiplied by 2^row_exp[m] (exact)
-    // split-K (set by the launcher): K is cut into `splits` super-block
-    // ranges; each (range, tile) unit writes an fp32 partial and the last
-    // unit of a tile to finish sums them in range order
-    int splits;
-    uint32_t* counters;  // [tiles][kEpiWarps] arrivals (zero between launches)
-    float* part;         // [tiles * splits][BN][BM] fp32 partials
+    // stream-K scratch (set by the launcher; nullptr: whole tiles only)
+    uint32_t* counters;  // [CTAs][kEpiWarps] arrivals of cut tiles (zero between launches)
+    float* part;         // [2 * CTAs][BN][BM] fp32 partials of cut tiles
 };
 
 namespace {
@@ -340,7 +344,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     // for their tile schedule, so every thread waits here; dense launches let
     // the raw-weight producer, the dequant and the MMA warps start at once and
     // wait only where the preceding kernel's outputs are read (activations)
-    // or its inputs may still be read (Y, row scales, split-K scratch).
+    // or its inputs may still be read (Y, row scales, stream-K scratch).
     if (grp.counts) grid_dependency_wait();
     for (int g = threadIdx.x; g < G; g += blockDim.x) {
         const int base = grp.counts ? min(max(grp.offsets[g], 0), M) : 0;
@@ -390,19 +394,59 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
 
     const int tiles = s_start[G];
     const int nsb = K / 256;
-    const int S = grp.splits;
-    const int units = tiles * S;  // split-major: concurrent CTAs share k ranges
     auto tile_at = [&](int tile) {
         return tile_ref<BN>(tile, s_start, s_base, s_cnt, G, n_tiles, n_all);
     };
-    // unit u: tile and its super-block range [sb0, sb1) (never empty: the
-    // host keeps at least two super-blocks per split)
-    auto unit_at = [&](int u, int& split, int& sb0, int& sb1) {
-        split = u / tiles;
-        sb0 = split * nsb / S;
-        sb1 = (split + 1) * nsb / S;
-        return u - split * tiles;
+    // Work schedule.  Whole tiles b, b + G, ... for every full wave of G
+    // CTAs (consecutive CTAs on consecutive tiles, so a wave shares its
+    // activation and weight tiles in L2); the tiles of the last, partial
+    // wave (all of them when there are fewer tiles than CTAs) go stream-K,
+    // given the scratch: their tiles x nsb super-block steps are cut into one
+    // equal contiguous range per CTA, [b*W/G, (b+1)*W/G), which meets tiles
+    // in segments (a tile and a super-block range), whole in the middle and
+    // partial at the two ends.  A tile cut by range boundaries is finished by
+    // the last of its pieces to arrive, adding the pieces' fp32 partials in
+    // range order.  Without the scratch every tile runs whole.
+    // (the launcher keeps tiles x nsb below 2^31 for stream-K)
+    const int Gl = (int)gridDim.x;
+    const int b_cta = (int)blockIdx.x;
+    // CTAs that share the stream-K steps: at most one per kMinPiece steps (a
+    // piece's pipeline fill and its share of the fix-up, 128 KB of fp32
+    // partial per piece on the 256-token tile, outweigh the balance below
+    // that), the rest idle; with W >= Gc every range is non-empty, which the
+    // piece bookkeeping relies on.  The tail goes stream-K only when that
+    // shortens the schedule by 5 % or more (in super-block steps, counting
+    // ~2 for a cut tile's fix-up): a last wave that is nearly full, or one
+    // of many waves, gains less than the cut tiles cost.
+    constexpr int kMinPiece = BN >= 256 ? 4 : 2;
+    const int waves = tiles / Gl, rem = tiles - waves * Gl;
+    const int w_rem = rem * nsb;
+    const int g_rem = min(Gl, max(1, w_rem / kMinPiece));
+    const int span_whole = (waves + (rem ? 1 : 0)) * nsb;
+    const int span_sk = waves * nsb + (w_rem + g_rem - 1) / g_rem + 2;
+    const bool sk = grp.part != nullptr && rem > 0 && 20 * span_sk < 19 * span_whole;
+    const int t_full = sk ? waves * Gl : tiles;  // tiles run whole, round robin
+    const int n_whole = b_cta < t_full ? (t_full - 1 - b_cta) / Gl + 1 : 0;
+    const int W = sk ? w_rem : 0;                // stream-K steps
+    const int Gc = sk ? g_rem : 0;
+    const int it0 = b_cta < Gc ? (int)((int64_t)b_cta * W / Gc) : 0;
+    const int it1 = b_cta < Gc ? (int)((int64_t)(b_cta + 1) * W / Gc) : 0;  // empty unless sk
+    const int nseg = n_whole + (it1 > it0 ? (it1 - 1) / nsb - it0 / nsb + 1 : 0);
+    // segment k of this CTA: its tile and super-block range [sb0, sb1)
+    auto seg_at = [&](int k, int& sb0, int& sb1) -> int {
+        if (k < n_whole) {
+            sb0 = 0;
+            sb1 = nsb;
+            return b_cta + k * Gl;
+        }
+        const int t = it0 / nsb + (k - n_whole);
+        const int t0 = t * nsb;
+        sb0 = max(it0, t0) - t0;
+        sb1 = min(it1, t0 + nsb) - t0;
+        return t_full + t;
     };
+    // the CTA whose stream-K range holds step q (W > 0)
+    auto owner = [&](int q) { return (int)(((int64_t)(q + 1) * Gc + W - 1) / W - 1); };
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA
@@ -411,9 +455,9 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             grid_dependency_wait();  // X may be the preceding kernel's output
             const uint64_t pol_x = policy_evict_last();
             uint32_t kc = 0;
-            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-                int split, sb0, sb1;
-                const TileRef t = tile_at(unit_at(u, split, sb0, sb1));
+            for (int k = 0; k < nseg && !*abort_flag; ++k) {
+                int sb0, sb1;
+                const TileRef t = tile_at(seg_at(k, sb0, sb1));
                 int xb = 0;  // smallest box covering the tile's rows
                 while (xb < kXMaps - 1 && xbox_rows(xb, BN) < t.rows) ++xb;
                 const CUtensorMap* xm = &tm_x.m[xb];
@@ -443,9 +487,9 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             prefetch_tensormap(&tm_w2);
             const uint64_t pol_w = policy_evict_last();  // weights are re-read per token tile
             uint32_t rc = 0;
-            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-                int split, sb0, sb1;
-                const TileRef t = tile_at(unit_at(u, split, sb0, sb1));
+            for (int k = 0; k < nseg && !*abort_flag; ++k) {
+                int sb0, sb1;
+                const TileRef t = tile_at(seg_at(k, sb0, sb1));
                 const CUtensorMap* wm = t.set ? &tm_w2 : &tm_w;
                 for (int sb = sb0; sb < sb1; ++sb) {
                     const RingPos<C> rp(rc, 0);
@@ -475,10 +519,10 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             uint32_t kc = 0, last_kc = 0;
             bool any = false;
             int i = 0;
-            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++i) {
+            for (int k = 0; k < nseg && !*abort_flag; ++k, ++i) {
                 const int b = i & 1;
-                int split, sb0, sb1;
-                const int tile = unit_at(u, split, sb0, sb1);
+                int sb0, sb1;
+                const int tile = seg_at(k, sb0, sb1);
                 // MMA N = the tile's tokens rounded up to 16
                 const uint32_t idesc = idesc_f16(fmt, BM, (uint32_t)min(BN, (tile_at(tile).rows + 15) & ~15));
                 if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1, C::SLEEP_NS)) {
@@ -524,19 +568,19 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         }
     } else if (warp < 2 + kEpiWarps) {
         // ---------------------------------------------------------- epilogue
-        // Split-K: every unit stores its fp32 partial (this warp's 32 columns
-        // of the tile); the warp whose arrival completes the tile's count
-        // re-reads its own accumulator and sums all partials in split order,
-        // so the result does not depend on which unit finished last.  Each
-        // warp counts on its own (no barrier between the epilogue warps).
+        // A cut tile (stream-K): every piece stores its fp32 partial (this
+        // warp's 32 columns of the tile); the warp whose arrival completes the
+        // tile's count sums all partials in range order, so the result does
+        // not depend on which piece finished last.  Each warp counts on its
+        // own (no barrier between the epilogue warps).
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int nl = 32 * q + lane;  // column of the tile this lane holds
-        grid_dependency_wait();  // Y, row scales and split-K scratch of earlier kernels
+        grid_dependency_wait();  // Y, row scales and stream-K scratch of earlier kernels
         int i = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+        for (int k = 0; k < nseg; ++k, ++i) {
             const int b = i & 1;
-            int split, sb0, sb1;
-            const int tile = unit_at(u, split, sb0, sb1);
+            int sb0, sb1;
+            const int tile = seg_at(k, sb0, sb1);
             const TileRef t = tile_at(tile);
             if (!mbar_wait_warp(&acc_full[b], (i >> 1) & 1, C::SLEEP_NS)) {
                 *abort_flag = 1;
@@ -561,9 +605,18 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 }
             };
             bool last = true;
-            if (S > 1) {
-                // partial slot (tile, split): [quadrant][row][32 columns] fp32
-                float* mine = grp.part + (size_t)(tile * S + split) * (BM * BN) + q * (BN * 32) + lane;
+            if (sb0 != 0 || sb1 != nsb) {
+                // a piece of a tile cut by range boundaries: pieces come from
+                // CTAs first .. last_cta in range order; CTA c keeps the piece of
+                // its first tile in partial slot 2c and of its last tile in
+                // 2c + 1 ([quadrant][row][32 columns] fp32 each); the tile's
+                // arrival count sits in row `first` of the counters (no other
+                // cut tile has its first piece in CTA `first`)
+                const int ts = tile - t_full;  // the tile in the stream-K range
+                const int first = owner(ts * nsb);
+                const int npieces = owner(ts * nsb + nsb - 1) - first + 1;
+                float* mine = grp.part + (size_t)(2 * b_cta + (k == n_whole ? 0 : 1)) * (BM * BN) +
+                              q * (BN * 32) + lane;
 #pragma unroll 1
                 for (int c0 = 0; c0 < t.rows; c0 += 32) {
                     uint32_t r[32];
@@ -576,40 +629,49 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                 __threadfence();
                 __syncwarp();
                 uint32_t old = 0;
-                uint32_t* cnt = grp.counters + tile * kEpiWarps + q;
+                uint32_t* cnt = grp.counters + first * kEpiWarps + q;
                 if (lane == 0) old = atomicAdd(cnt, 1u);
                 old = __shfl_sync(0xffffffffu, old, 0);
-                last = old == (uint32_t)(S - 1);
+                last = old == (uint32_t)(npieces - 1);
                 if (last) {
                     if (lane == 0) atomicExch(cnt, 0u);  // ready for the next launch
                     __threadfence();
-                    // Sum the S partials of this quadrant in split order.  A
-                    // lane takes 4 columns (c4..c4+3) of rows 4g + rr; loads
-                    // go out 16 at a time (4 splits x 4 row groups) so the
-                    // fix-up costs one L2 round trip per 16 rows and 4 splits.
+                    // Sum the pieces' partials of this quadrant in range
+                    // order.  A lane takes 4 columns (c4..c4+3) of rows
+                    // 4g + rr; loads go out 16 at a time (4 pieces x 4 row
+                    // groups) so the fix-up costs one L2 round trip per 16
+                    // rows and 4 pieces.
                     const int rr = lane >> 3, c4 = 4 * (lane & 7);
-                    const float* qb = grp.part + (size_t)tile * S * (BM * BN) + q * (BN * 32) + c4;
+                    // partial slot of piece p (CTA first + p): the tile is the
+                    // first tile of every later piece's CTA (slot 2c) and the
+                    // last tile of CTA `first` unless its range starts here
+                    const int e0 = (int)((int64_t)first * W / Gc) != ts * nsb ? 1 : 0;
+                    auto piece_slot = [&](int p) {
+                        return (size_t)(2 * (first + p) + (p == 0 ? e0 : 0));
+                    };
+                    const float* qb = grp.part + q * (BN * 32) + c4;
                     const int nq = t.nt * BM + 32 * q + c4;  // first of the lane's 4 columns
                     const int64_t cq = (int64_t)t.set * N + nq;
 #pragma unroll 1
                     for (int rb = 0; rb < t.rows; rb += 16) {
                         float4 acc[4];
 #pragma unroll 1
-                        for (int s0 = 0; s0 < S; s0 += 4) {
+                        for (int s0 = 0; s0 < npieces; s0 += 4) {
                             float4 v[4][4];
 #pragma unroll
                             for (int u2 = 0; u2 < 4; ++u2)
 #pragma unroll
                                 for (int g = 0; g < 4; ++g) {
                                     const int row = rb + 4 * g + rr;
-                                    v[u2][g] = (s0 + u2 < S && row < t.rows)
+                                    v[u2][g] = (s0 + u2 < npieces && row < t.rows)
                                                    ? __ldcg(reinterpret_cast<const float4*>(
-                                                         qb + (size_t)(s0 + u2) * (BM * BN) + row * 32))
+                                                         qb + piece_slot(s0 + u2) * (BM * BN) +
+                                                         row * 32))
                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
                                 }
 #pragma unroll
                             for (int u2 = 0; u2 < 4; ++u2) {
-                                if (s0 + u2 >= S) break;
+                                if (s0 + u2 >= npieces) break;
 #pragma unroll
                                 for (int g = 0; g < 4; ++g) {
                                     if (s0 + u2 == 0) {
@@ -683,9 +745,9 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                              : 16 * wi + 8 * (lane >> 4) + (lane & 7);  // weight row in tile
         const int swz = r & 7;
         uint32_t rc = 0;  // super-blocks in kernel order; this team takes rc % DT == team
-        for (int u = blockIdx.x; u < units; u += gridDim.x) {
-            int split, sb0, sb1;
-            unit_at(u, split, sb0, sb1);
+        for (int k = 0; k < nseg; ++k) {
+            int sb0, sb1;
+            seg_at(k, sb0, sb1);
             for (int sb = sb0; sb < sb1; ++sb, ++rc) {
                 if ((int)(rc % C::DT) != team) continue;
                 const RingPos<C> rp0(rc, 0);
@@ -838,16 +900,14 @@ int act_maps(XMaps* mx, const void* x, int x_dtype, int64_t rows, int64_t K, int
     return FTC_OK;
 }
 
-// ------------------------------------------------------------- split-K
+// ------------------------------------------------------------- stream-K
 
-// Units (tiles x splits) of one launch are capped at kUnitsPerSm per SM; the
-// per-device scratch holds the partials and arrival counters of that many.
-constexpr int kUnitsPerSm = 4;
-constexpr int kMaxSplits = 16;
-constexpr int kMinSbPerSplit = 2;
+// Scratch of the stream-K schedule: two partial slots (a CTA's first and
+// last tile) and one row of arrival counters per CTA, one CTA per SM.
+constexpr int kSlotsPerSm = 2;
 
 struct SplitScratch {
-    int units = 0;  // capacity in units (0: none)
+    int units = 0;  // capacity in partial slots (0: none)
     uint32_t* counters = nullptr;
     float* part = nullptr;
 };
@@ -855,14 +915,14 @@ struct SplitScratch {
 std::mutex g_split_mu;
 SplitScratch g_split[64];  // per device
 
-// The device's split-K scratch, allocated on first use (never freed, never
+// The device's stream-K scratch, allocated on first use (never freed, never
 // moved: graphs that captured its address stay valid).  Inside a stream
 // capture nothing can be allocated; *out stays empty and the caller runs
-// without splits.
+// whole tiles.
 int split_scratch(cudaStream_t st, int sms, SplitScratch* out) {
     int dev = 0;
     FTC_CUDA(cudaGetDevice(&dev));
-    FTC_REQUIRE(dev >= 0 && dev < 64, FTC_E_CUDA, "gemm split-K: device index out of range");
+    FTC_REQUIRE(dev >= 0 && dev < 64, FTC_E_CUDA, "gemm stream-K: device index out of range");
     std::lock_guard<std::mutex> lk(g_split_mu);
     SplitScratch& sc = g_split[dev];
     if (!sc.units) {
@@ -872,7 +932,7 @@ int split_scratch(cudaStream_t st, int sms, SplitScratch* out) {
             *out = SplitScratch{};
             return FTC_OK;
         }
-        const int units = kUnitsPerSm * sms;
+        const int units = kSlotsPerSm * sms;
         const size_t cnt_bytes = ((size_t)units * kEpiWarps * 4 + 255) & ~size_t(255);
         const size_t part_bytes = (size_t)units * BM * 256 * 4;
         void* p = nullptr;
@@ -880,7 +940,7 @@ int split_scratch(cudaStream_t st, int sms, SplitScratch* out) {
         const cudaError_t e = cudaMemset(p, 0, cnt_bytes);
         if (e != cudaSuccess) {
             cudaFree(p);
-            return cuda_error(e, "cudaMemset(gemm split-K counters)");
+            return cuda_error(e, "cudaMemset(gemm stream-K counters)");
         }
         sc.counters = static_cast<uint32_t*>(p);
         sc.part = reinterpret_cast<float*>(static_cast<uint8_t*>(p) + cnt_bytes);
@@ -890,47 +950,26 @@ int split_scratch(cudaStream_t st, int sms, SplitScratch* out) {
     return FTC_OK;
 }
 
-// Splits for `tiles` output tiles of nsb super-blocks and up to tile_rows
-// token rows each on `sms` SMs: the one that minimizes, in units of one
-// super-block step (~2 us), waves x (super-blocks per unit + one for the
-// pipeline fill and epilogue) plus the fix-up of the last unit of a tile
-// (one L2 round trip, ~1/4 step, per 16 rows and 4 splits).
-int choose_splits(int64_t tiles, int nsb, int tile_rows, int sms) {
-    auto cost = [&](int S) {
-        const int64_t waves = (tiles * S + sms - 1) / sms;
-        const double fix = S > 1 ? 0.5 + 0.25 * ((S + 3) / 4) * ((tile_rows + 15) / 16) : 0.0;
-        return (double)waves * ((nsb + S - 1) / S + 1) + fix;
-    };
-    int best = 1;
-    double best_cost = cost(1);
-    for (int S = 2; S <= kMaxSplits; ++S) {
-        if (nsb < kMinSbPerSplit * S || tiles * S > (int64_t)kUnitsPerSm * sms) break;
-        const double c = cost(S);
-        if (c < best_cost) best = S, best_cost = c;
-    }
-    return best;
-}
-
 int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2, const XMaps& tx,
              int M, int N, int K, void* y, int y_dtype, GemmGroups grp, int64_t max_tiles,
              int tile_rows, cudaStream_t st) {
     const bool bf = x_dtype == FTC_BF16;
     const int sms = device_sms();
-    const int S = choose_splits(max_tiles, K / 256, std::min(tile_rows, BN), sms);
-    grp.splits = 1;
+    (void)tile_rows;
+    // stream-K over all SMs when the scratch exists (two partial slots and
+    // one counter row per CTA); otherwise whole tiles, one CTA per tile
     grp.counters = nullptr;
     grp.part = nullptr;
-    if (S > 1) {
-        SplitScratch sc;
-        const int rc = split_scratch(st, sms, &sc);
-        if (rc != FTC_OK) return rc;
-        if (sc.units >= max_tiles * S) {
-            grp.splits = S;
-            grp.counters = sc.counters;
-            grp.part = sc.part;
-        }
+    SplitScratch sc;
+    const int src = split_scratch(st, sms, &sc);
+    if (src != FTC_OK) return src;
+    if (sc.units >= 2 * sms) {
+        grp.counters = sc.counters;
+        grp.part = sc.part;
     }
-    const int64_t units = max_tiles * grp.splits;
+    if (max_tiles * (K / 256) > INT32_MAX) grp.counters = nullptr, grp.part = nullptr;
+    // launch size: every step of the grid's range scheme needs a CTA
+    const int64_t units = grp.part ? max_tiles * (K / 256) : max_tiles;
     // up to 64 tokens: two MMA issuers (their accumulators and the A stages
     // all in tensor memory); up to 128: A stages in tensor memory (no
     // shared-memory A stores or A reads by the MMA); larger: the 256-token
@@ -957,7 +996,7 @@ int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2,
 }  // namespace
 
 // Status reader of this file's kernels.  Clearing a recorded timeout also
-// zeroes the split-K arrival counters, which a launch that gave up part way
+// zeroes the stream-K arrival counters, which a launch that gave up part way
 // may have left uneven.
 int devstat_gemm_q4k(int clear) {
     int v = 0;
@@ -1005,7 +1044,7 @@ int gemm_q4k(const void* w, int64_t N, int64_t K, int64_t row_stride, const void
     if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm"))) return rc;
     if ((rc = act_maps(&tx, x, x_dtype, M, K, BN, "ftc_gemm"))) return rc;
     if (inject_fail("ftc_gemm")) return set_error(FTC_E_INJECTED, "ftc_gemm: injected failure");
-    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, nullptr, 1, nullptr, nullptr};
+    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, nullptr, nullptr, nullptr};
     const int64_t tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
     return dispatch(BN, x_dtype, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles,
                     (int)std::min<int64_t>(M, BN), st);
@@ -1031,7 +1070,7 @@ int gemm_q4k_rowscaled(const void* w, int64_t N, int64_t K, int64_t row_stride, 
     if ((rc = weight_map(&tw, w, N, K, row_stride, 1, N * row_stride, "ftc_gemm_rowscaled")))
         return rc;
     if ((rc = act_maps(&tx, x16, FTC_F16, M, K, BN, "ftc_gemm_rowscaled"))) return rc;
-    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, row_exp, 1, nullptr, nullptr};
+    const GemmGroups grp = {nullptr, nullptr, 1, 1, N, row_exp, nullptr, nullptr};
     const int64_t tiles = ((N + BM - 1) / BM) * ((M + BN - 1) / BN);
     return dispatch(BN, FTC_F16, tw, tw, tx, (int)M, (int)N, (int)K, y, y_dtype, grp, tiles,
                     (int)std::min<int64_t>(M, BN), st);
@@ -1070,7 +1109,7 @@ int gemm_q4k_grouped(const void* w, const void* w2, int n_sets, int64_t G, int64
         (rc = weight_map(&tw2, w2, N, K, row_stride, G, plane_stride, "gemm_q4k_grouped")))
         return rc;
     if ((rc = act_maps(&tx, x, x_dtype, rows, K, BN, "gemm_q4k_grouped"))) return rc;
-    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy, row_exp, 1, nullptr, nullptr};
+    const GemmGroups grp = {counts, offsets, (int)G, n_sets, ldy, row_exp, nullptr, nullptr};
     // upper bound on tiles: every non-empty group adds at most one partial token tile
     const int64_t tok_tiles = (rows + BN - 1) / BN + std::min<int64_t>(G, rows);
     const int64_t tiles = tok_tiles * ((N + BM - 1) / BM) * n_sets;
