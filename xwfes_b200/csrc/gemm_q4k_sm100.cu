@@ -137,9 +137,10 @@ struct Cfg {
     // barriers: a_full[NA] a_empty[NA] b_full[NB] b_empty[NB] raw_full[RAW]
     // raw_empty[RAW] acc_full[2] acc_empty[2]
     static constexpr int N_BARS = 2 * NA + 2 * NB + 2 * RAW + 4;
-    // tile schedule: first tile, first row and row count of each group
+    // tile schedule: first tile, first row and row count of each group, then
+    // the CTA's work ranges (8 ints)
     static constexpr int OFF_SCHED = OFF_BAR + N_BARS * 8 + 16;
-    static constexpr int SMEM = OFF_SCHED + (3 * kGemmMaxGroups + 1) * 4 + 1024;  // +1024: alignment slack
+    static constexpr int SMEM = OFF_SCHED + (3 * kGemmMaxGroups + 1 + 8) * 4 + 1024;  // +1024: alignment slack
     static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -166,6 +167,59 @@ struct RingPos {
 struct TileRef {
     int g, set, nt, row0, rows;
 };
+
+// Cut of the last, partial wave of whole tiles, computed alike by the
+// kernel and by the launcher (which sizes a launch with fewer tiles than SMs
+// to the CTAs that get work).  Given the scratch, the tail's W = rem x nsb
+// super-block steps are cut one of two ways.  Aligned: S CTAs per tail
+// tile, each on nsb/S of its steps, so no range crosses a tile boundary (the
+// fewest S with the shortest range that fits the grid).  Stream-K: one CTA
+// per kMinPiece steps or more, up to the grid, ranges crossing tile
+// boundaries (such a CTA drains its pipeline and runs an epilogue twice).
+// With W >= Gc every range is non-empty, which the piece bookkeeping relies
+// on.  Each is charged its longest range plus an estimate, in super-block
+// steps, of its fix-up (128 KB of fp32 partial per piece on the 256-token
+// tile) and, for stream-K, the second epilogue; the cheaper runs when it
+// shortens the schedule by 5 % or more, else every tile runs whole (a last
+// wave that is nearly full, or one of many waves, gains less than the cut
+// tiles cost).  Any grid size gives a valid plan.
+struct TailPlan {
+    int t_full;  // tiles run whole, round robin over the grid
+    int W;       // steps of the cut tail (0: none)
+    int Gc;      // CTAs sharing them, ranges [b*W/Gc, (b+1)*W/Gc)
+};
+
+template <int BN>
+__host__ __device__ inline TailPlan plan_tail(int tiles, int nsb, int Gl, bool scratch) {
+    constexpr int kMinPiece = BN >= 256 ? 4 : 2;
+    constexpr int kCostAligned = BN >= 256 ? 4 : 2;
+    constexpr int kCostStreamK = BN >= 256 ? 8 : 3;
+    const int waves = tiles / Gl, rem = tiles - waves * Gl;
+    const int w_rem = rem * nsb;
+    const int span_whole = (waves + (rem ? 1 : 0)) * nsb;
+    int s_al = 0;
+    if (rem) {
+        s_al = Gl / rem < nsb / kMinPiece ? Gl / rem : nsb / kMinPiece;
+        if (s_al >= 2) {
+            const int len = (nsb + s_al - 1) / s_al;
+            s_al = (nsb + len - 1) / len;
+        }
+    }
+    const int span_al = s_al >= 2 ? waves * nsb + (nsb + s_al - 1) / s_al + kCostAligned : (1 << 30);
+    const int per = w_rem / kMinPiece > 1 ? w_rem / kMinPiece : 1;
+    const int g_sk = Gl < per ? Gl : per;
+    const int span_sk = waves * nsb + (w_rem + g_sk - 1) / g_sk + kCostStreamK;
+    const bool aligned = span_al <= span_sk;
+    const int span_cut = aligned ? span_al : span_sk;
+    // (W x (Gl + 1) below 2^31: the range and owner arithmetic is 32-bit)
+    const bool cut = scratch && rem > 0 && 20 * span_cut < 19 * span_whole &&
+                     (long long)w_rem * (Gl + 1) < 0x7fffffffLL;
+    TailPlan p;
+    p.t_full = cut ? waves * Gl : tiles;
+    p.W = cut ? w_rem : 0;
+    p.Gc = cut ? (aligned ? rem * s_al : g_sk) : 0;
+    return p;
+}
 
 template <int BN>
 __device__ __forceinline__ TileRef tile_ref(int tile, const int* s_start, const int* s_base,
@@ -336,6 +390,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     int* s_start = reinterpret_cast<int*>(smem + C::OFF_SCHED);  // [G + 1]
     int* s_base = s_start + kGemmMaxGroups + 1;                  // [G]
     int* s_cnt = s_base + kGemmMaxGroups;                        // [G]
+    int* s_plan = s_cnt + kGemmMaxGroups;                        // [8] this CTA's schedule
     const int G = grp.G;
     const int n_tiles = (N + BM - 1) / BM;
     const int n_all = n_tiles * grp.n_sets;
@@ -381,6 +436,20 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
             acc += (s_cnt[g] + BN - 1) / BN * n_all;
         }
         s_start[G] = acc;
+        // this CTA's share (one thread: the divisions, issued by every warp,
+        // cost ~0.4 us of issue slots per launch)
+        const int Gl = (int)gridDim.x, b = (int)blockIdx.x, nsb = K / 256;
+        const TailPlan pl = plan_tail<BN>(acc, nsb, Gl, grp.part != nullptr);
+        const int it0 = b < pl.Gc ? b * pl.W / pl.Gc : 0;
+        const int it1 = b < pl.Gc ? (b + 1) * pl.W / pl.Gc : 0;
+        const int n_whole = b < pl.t_full ? (pl.t_full - 1 - b) / Gl + 1 : 0;
+        s_plan[0] = pl.t_full;
+        s_plan[1] = pl.W;
+        s_plan[2] = pl.Gc;
+        s_plan[3] = n_whole;
+        s_plan[4] = it0;
+        s_plan[5] = it1;
+        s_plan[6] = n_whole + (it1 > it0 ? (it1 - 1) / nsb - it0 / nsb + 1 : 0);
     }
     if (warp == 0) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -392,7 +461,6 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     const uint32_t tmem_base = *tmem_slot;
     grid_launch_dependents();  // the next kernel's prologue may overlap this grid
 
-    const int tiles = s_start[G];
     const int nsb = K / 256;
     auto tile_at = [&](int tile) {
         return tile_ref<BN>(tile, s_start, s_base, s_cnt, G, n_tiles, n_all);
@@ -400,38 +468,20 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
     // Work schedule.  Whole tiles b, b + G, ... for every full wave of G
     // CTAs (consecutive CTAs on consecutive tiles, so a wave shares its
     // activation and weight tiles in L2); the tiles of the last, partial
-    // wave (all of them when there are fewer tiles than CTAs) go stream-K,
-    // given the scratch: their tiles x nsb super-block steps are cut into one
-    // equal contiguous range per CTA, [b*W/G, (b+1)*W/G), which meets tiles
-    // in segments (a tile and a super-block range), whole in the middle and
-    // partial at the two ends.  A tile cut by range boundaries is finished by
-    // the last of its pieces to arrive, adding the pieces' fp32 partials in
-    // range order.  Without the scratch every tile runs whole.
-    // (the launcher keeps tiles x nsb below 2^31 for stream-K)
+    // wave (all of them when there are fewer tiles than CTAs) may be cut
+    // (plan_tail): their W = tiles x nsb super-block steps split into one
+    // equal contiguous range per CTA, [b*W/Gc, (b+1)*W/Gc) for the first Gc
+    // CTAs, which meets tiles in segments (a tile and a super-block range).
+    // A tile cut by range boundaries is finished by the last of its pieces
+    // to arrive, adding the pieces' fp32 partials in range order.
     const int Gl = (int)gridDim.x;
     const int b_cta = (int)blockIdx.x;
-    // CTAs that share the stream-K steps: at most one per kMinPiece steps (a
-    // piece's pipeline fill and its share of the fix-up, 128 KB of fp32
-    // partial per piece on the 256-token tile, outweigh the balance below
-    // that), the rest idle; with W >= Gc every range is non-empty, which the
-    // piece bookkeeping relies on.  The tail goes stream-K only when that
-    // shortens the schedule by 5 % or more (in super-block steps, counting
-    // ~2 for a cut tile's fix-up): a last wave that is nearly full, or one
-    // of many waves, gains less than the cut tiles cost.
-    constexpr int kMinPiece = BN >= 256 ? 4 : 2;
-    const int waves = tiles / Gl, rem = tiles - waves * Gl;
-    const int w_rem = rem * nsb;
-    const int g_rem = min(Gl, max(1, w_rem / kMinPiece));
-    const int span_whole = (waves + (rem ? 1 : 0)) * nsb;
-    const int span_sk = waves * nsb + (w_rem + g_rem - 1) / g_rem + 2;
-    const bool sk = grp.part != nullptr && rem > 0 && 20 * span_sk < 19 * span_whole;
-    const int t_full = sk ? waves * Gl : tiles;  // tiles run whole, round robin
-    const int n_whole = b_cta < t_full ? (t_full - 1 - b_cta) / Gl + 1 : 0;
-    const int W = sk ? w_rem : 0;                // stream-K steps
-    const int Gc = sk ? g_rem : 0;
-    const int it0 = b_cta < Gc ? (int)((int64_t)b_cta * W / Gc) : 0;
-    const int it1 = b_cta < Gc ? (int)((int64_t)(b_cta + 1) * W / Gc) : 0;  // empty unless sk
-    const int nseg = n_whole + (it1 > it0 ? (it1 - 1) / nsb - it0 / nsb + 1 : 0);
+    const int t_full = s_plan[0];   // tiles run whole, round robin
+    const int W = s_plan[1];        // steps of the cut tail
+    const int Gc = s_plan[2];       // CTAs sharing them
+    const int n_whole = s_plan[3];  // this CTA's whole tiles
+    const int it0 = s_plan[4], it1 = s_plan[5];  // its range of the tail (empty unless W)
+    const int nseg = s_plan[6];
     // segment k of this CTA: its tile and super-block range [sb0, sb1)
     auto seg_at = [&](int k, int& sb0, int& sb1) -> int {
         if (k < n_whole) {
@@ -446,7 +496,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
         return t_full + t;
     };
     // the CTA whose stream-K range holds step q (W > 0)
-    auto owner = [&](int q) { return (int)(((int64_t)(q + 1) * Gc + W - 1) / W - 1); };
+    auto owner = [&](int q) { return ((q + 1) * Gc + W - 1) / W - 1; };
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA
@@ -645,7 +695,7 @@ gemm_q4k_tc(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CU
                     // partial slot of piece p (CTA first + p): the tile is the
                     // first tile of every later piece's CTA (slot 2c) and the
                     // last tile of CTA `first` unless its range starts here
-                    const int e0 = (int)((int64_t)first * W / Gc) != ts * nsb ? 1 : 0;
+                    const int e0 = first * W / Gc != ts * nsb ? 1 : 0;
                     auto piece_slot = [&](int p) {
                         return (size_t)(2 * (first + p) + (p == 0 ? e0 : 0));
                     };
@@ -968,8 +1018,19 @@ int dispatch(int BN, int x_dtype, const CUtensorMap& tw, const CUtensorMap& tw2,
         grp.part = sc.part;
     }
     if (max_tiles * (K / 256) > INT32_MAX) grp.counters = nullptr, grp.part = nullptr;
-    // launch size: every step of the grid's range scheme needs a CTA
-    const int64_t units = grp.part ? max_tiles * (K / 256) : max_tiles;
+    // launch size: with the tile count known on the host (no device-side
+    // groups) and under one wave, the CTAs the kernel's plan gives work to
+    // (the kernel recomputes it for that grid); otherwise every SM (grouped
+    // counts are only known on the device)
+    int64_t units = grp.part ? max_tiles * (K / 256) : max_tiles;
+    if (!grp.counts && max_tiles < sms) {
+        const int t = (int)max_tiles, nsb = K / 256;
+        const bool scr = grp.part != nullptr;
+        const TailPlan pl = BN == 64    ? plan_tail<64>(t, nsb, sms, scr)
+                            : BN == 128 ? plan_tail<128>(t, nsb, sms, scr)
+                                        : plan_tail<256>(t, nsb, sms, scr);
+        units = std::max(pl.t_full, pl.Gc);
+    }
     // up to 64 tokens: two MMA issuers (their accumulators and the A stages
     // all in tensor memory); up to 128: A stages in tensor memory (no
     // shared-memory A stores or A reads by the MMA); larger: the 256-token
