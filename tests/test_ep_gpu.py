@@ -3,13 +3,18 @@ sizes).  With one rank the layer is routing + grouped expert GEMMs + combine
 and must reproduce ftc_moe_ffn's grouped path; across two GPUs (NCCL) the rows
 exchanged between ranks must give the same result again.
 
-Each output row depends only on its own token and experts, except for the
-GEMMs' split-K: a launch with few output tiles cuts K into ranges whose fp32
-partials are summed in a fixed order, and the number of ranges follows the
-launch's tile count, which differs between one GPU holding all experts and a
-rank holding some.  Only that fp32 summation order differs, so the results
-agree to a few fp32 ulps of the output scale (bound 1e-5 relative to the
-largest output)."""
+Each output row depends only on its own token and experts, but the two
+layers tile their GEMMs differently: the token tile follows the caller's
+bound on rows per expert (all tokens on one GPU, the rank's capacity under
+EP), and a launch with few output tiles cuts K into ranges whose fp32
+partials are summed in a fixed order that follows the launch's tile count.
+So gate/up agree to fp32 summation order only (~1e-6 relative), and where
+h = silu(gate) * up lies next to an fp16 rounding boundary its 16-bit copy
+for the down GEMM can differ by one fp16 ulp (2^-11 relative).  A few such
+elements per row move the output by ~1e-5 of its scale (measured up to
+~2e-5 of an element on two B200s), so the bound is 1e-4 relative to the
+largest output; the one-token case below compares different paths
+altogether and keeps the GEMM tolerance."""
 import os
 import socket
 import subprocess
@@ -45,7 +50,7 @@ def to_dev(logits, xbits):
 
 def close(got, want):  # bound: see the module docstring
     return got.shape == want.shape and \
-        float(np.max(np.abs(got - want))) <= 1e-5 * float(np.max(np.abs(want)))
+        float(np.max(np.abs(got - want))) <= 1e-4 * float(np.max(np.abs(want)))
 
 
 def single_gpu(T):
