@@ -815,7 +815,7 @@ def time_ep(dev, world, rank):
         x = torch.from_numpy(S.activations_bf16(T, K, seed=0, name="moe.x")[t0:t1].view(
             np.int16)).to(dev).view(torch.bfloat16)
         with torch.cuda.stream(cs):
-            for _ in range(3):  # eager warm-up (NCCL, workspaces, split-K scratch)
+            for _ in range(3):  # eager warm-up (NCCL, workspaces, GEMM partial-sum scratch)
                 layer.forward(logits, x)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -1060,10 +1060,11 @@ def run_ncu_gemm_probe():
 
 
 def run_ncu_gemm_split_probe():
-    """Three split-K dequant-GEMM launches on a tensor-parallel rank's shape
-    (the stacked q/k/v shard of config 4 at 8 GPUs: 1280 x 8192 Q4_K, 16
-    tokens, fp16 row-scaled operands): 10 output tiles, so K is split over
-    the SMs and the partials are summed by the last unit of each tile."""
+    """Three dequant-GEMM launches on a tensor-parallel rank's shape (the
+    stacked q/k/v shard of config 4 at 8 GPUs: 1280 x 8192 Q4_K, 16 tokens,
+    fp16 row-scaled operands): 10 output tiles, so each tile's K range is cut
+    into pieces on several SMs and the partials are summed by the last piece
+    of each tile."""
     import torch
     from xwfes_b200 import ftc
     dev = torch.device("cuda", 0)
@@ -1075,7 +1076,7 @@ def run_ncu_gemm_split_probe():
     for _ in range(3):
         ftc.gemm_rowscaled(w, F.Q4_K, n, k, x16, e, y=y)
     torch.cuda.synchronize()
-    print(json.dumps({"probe": "gemm_q4k_tc split-K 1280x8192 M=16 x3",
+    print(json.dumps({"probe": "gemm_q4k_tc cut tiles 1280x8192 M=16 x3",
                       "status": ftc.device_status()}))
     return 0
 
@@ -1272,7 +1273,7 @@ def main():
                     help="profiling mode: three batch-4 grouped gate+up launches of the integer "
                          "tensor-core GEMV (2 x 14336x4096), no timing")
     ap.add_argument("--ncu-gemm-split", action="store_true",
-                    help="profiling mode: three split-K dequant-GEMM launches on a TP rank's "
+                    help="profiling mode: three dequant-GEMM launches with cut tiles on a TP rank's "
                          "q/k/v shard (1280x8192, M=16), no timing")
     ap.add_argument("--ncu-gemm", action="store_true",
                     help="profiling mode: three launches of the config-3 dequant-GEMM "

@@ -167,9 +167,30 @@ def test_gemm_config3(ftc, oracle, n, k, m):
 @pytest.mark.parametrize("m,n,k", [(16, 128, 8192), (77, 384, 14336), (300, 256, 4096)])
 def test_gemm_split_k(ftc, oracle, m, n, k):
     """Shapes with fewer output tiles than SMs: the K range is split over
-    several CTAs and the partials are summed in a fixed order, so the result
-    matches the reference and repeats bit for bit, also when replayed from a
-    CUDA graph."""
+    several CTAs (on 148 SMs each of these tiles is cut into aligned pieces,
+    none crossing a tile) and the partials are summed in a fixed order, so
+    the result matches the reference and repeats bit for bit, also when
+    replayed from a CUDA graph."""
+    _check_cut_tiles(ftc, oracle, m, n, k)
+
+
+# The tail plans of the tile schedule on a 148-SM B200 (whole waves, then
+# the last partial wave run whole, cut into aligned pieces, or cut stream-K
+# with ranges that cross tile boundaries); every plan must give the same
+# arithmetic per tile up to the fp32 order of its pieces.
+@pytest.mark.parametrize("m,n,k", [
+    (16, 10240, 4096),    # 80 tiles: stream-K over all SMs, ranges crossing tiles
+    (16, 21504, 4096),    # 168 tiles: a whole wave, then 20 tiles in aligned pieces
+    (16, 29440, 4096),    # 230 tiles: a whole wave, then a stream-K tail
+    (100, 10240, 4096),   # 128-token tile (A in tensor memory), stream-K
+    (300, 10240, 4096),   # 256-token tile, a whole wave, then aligned pieces
+    (2048, 4096, 14336),  # 256-token tile, a whole wave, then a stream-K tail
+])
+def test_gemm_tail_plans(ftc, oracle, m, n, k):
+    _check_cut_tiles(ftc, oracle, m, n, k)
+
+
+def _check_cut_tiles(ftc, oracle, m, n, k):
     w = S.weight(F.Q4_K, n, k, seed=5, name="gemm.split")
     x16 = to16(S.activations_f32(m, k, seed=5), F.BF16).cuda()
     wd = torch.from_numpy(w).cuda()

@@ -23,9 +23,10 @@ expert planes, uploaded only there) and a shard of the tokens:
   6. the weighted sum in expert first-use order (ftc_moe_combine).
 
 Every token's result is the arithmetic of the single-GPU layer
-(ftc_moe_ffn's grouped path) on the same rows; only the GEMMs' split-K
-choice, which follows the launch's tile count, may order the fp32 partial
-sums differently.
+(ftc_moe_ffn's grouped path) on the same rows, up to the GEMMs' tiling:
+the token tile follows the bound on rows per expert and the cut of the last
+wave of tiles follows the launch's tile count, so fp32 partial sums may be
+ordered differently (and an fp16 rounding of h may then differ by one ulp).
 
 The compute is injected (``ops``): :class:`CudaEPOps` runs the library's
 kernels, the CPU tests run the same orchestration with the oracle under gloo.
