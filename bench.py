@@ -14,8 +14,10 @@ Inputs are seeded synthetic tensors with the config's distributions.
                CUDA events on the launching stream.
 * e2e       -- the same pass through the reference-facing C ABI
                (ftc_backend_matmul, the ft::IBackend::matmul equivalent):
-               host x in, host y out, per call; weights resident (uploaded
-               once, as at Engine::load).
+               host x in, host y out, per call, the step's calls issued by
+               a native loop as the engine's C++ decode loop issues them
+               (e2e_python: the same calls from a Python loop); weights
+               resident (uploaded once, as at Engine::load).
 * roofline  -- the dominant kernel (gate/up shape 14336x4096) timed alone.
 * cpu_baseline -- the CPU port of the reference's CpuBackend::matmul on a
                bounded sample (N=1, rank 0).
@@ -359,6 +361,22 @@ def run_ours(args, rank, world, local_rank):
     ext = torch.cuda.ExternalStream(be.stream(), device=dev)
     yh = {name: np.empty((1, n), dtype=np.float32) for name, n, _ in LAYER}
 
+    # the step's 56 calls in engine order, issued from native code (the
+    # reference's engine is a C++ loop over IBackend::matmul)
+    seq = be.matmul_sequence([(xs_host[X_OF[name]], 1, k, hosts[(li, name)], yh[name])
+                              for li in range(N_LAYERS) for name, n, k in LAYER])
+    seq.run(3)
+    e2e_steps = max(20, min(args.steps, 200))
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record(ext)
+    seq.run(e2e_steps)
+    ev1.record(ext)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+
+    # the same calls one by one from Python (CudaBackend.matmul per call)
     def e2e_step():
         for li in range(N_LAYERS):
             for name, n, k in LAYER:
@@ -366,7 +384,6 @@ def run_ours(args, rank, world, local_rank):
 
     for _ in range(3):
         e2e_step()
-    e2e_steps = max(20, min(args.steps, 200))
     barrier()
     torch.cuda.synchronize()
     ev0.record(ext)
@@ -375,7 +392,7 @@ def run_ours(args, rank, world, local_rank):
     ev1.record(ext)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+    e2e_py_ms = ev0.elapsed_time(ev1) / e2e_steps
     h2d = N_LAYERS * sum(4 * k for _, _, k in LAYER)
     d2h = N_LAYERS * sum(4 * n for _, n, _ in LAYER)
     e2e_direct = side_measurement(
@@ -392,10 +409,10 @@ def run_ours(args, rank, world, local_rank):
     clk.__exit__(None, None, None)
 
     # max over ranks
-    t = torch.tensor([ms, e2e_ms, k_ms], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms, e2e_ms, k_ms, e2e_py_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, k_ms = t.tolist()
+    ms, e2e_ms, k_ms, e2e_py_ms = t.tolist()
 
     del graph, g2
     be.close()
@@ -454,9 +471,17 @@ def run_ours(args, rank, world, local_rank):
             "steps": e2e_steps,
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "api": "ftc_backend_matmul (ft::IBackend::matmul): host x copied into pinned "
-                   "staging, one cached CUDA graph per (weight, shape) replayed per call (copy "
-                   "kernel in, GEMV storing y into pinned memory), sync per call",
+            "api": "ftc_backend_matmul (ft::IBackend::matmul) called 56 times per step, in "
+                   "engine order, from a native loop (MatmulSequence, host/call_loop.c): host x "
+                   "copied into pinned staging, one cached CUDA graph per (weight, shape) "
+                   "replayed per call (copy kernel in, GEMV storing y into pinned memory), sync "
+                   "per call",
+        },
+        "e2e_python": {
+            "value": round(step_bytes / (e2e_py_ms * 1e-3) / 1e9 * world, 2),
+            "unit": "GB/s",
+            "ms_per_step": round(e2e_py_ms, 4),
+            "api": "the same 56 calls one by one from Python (CudaBackend.matmul, ctypes)",
         },
         "decode_batched": decode_extras["batched"],
         "q6_k_head": decode_extras["q6_k_head"],
@@ -493,27 +518,22 @@ def time_e2e_direct(dev, local_rank, hosts, xs_host, steps, step_bytes):
         for T in hosts.values():
             be.upload(T)
         yh = {name: np.empty((1, n), dtype=np.float32) for name, n, _ in LAYER}
-
-        def step():
-            for li in range(N_LAYERS):
-                for name, n, k in LAYER:
-                    be.matmul(xs_host[X_OF[name]], 1, k, hosts[(li, name)], yh[name])
-
-        for _ in range(3):
-            step()
+        seq = be.matmul_sequence([(xs_host[X_OF[name]], 1, k, hosts[(li, name)], yh[name])
+                                  for li in range(N_LAYERS) for name, n, k in LAYER])
+        seq.run(3)
         ext = torch.cuda.ExternalStream(be.stream(), device=dev)
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         ev0.record(ext)
-        for _ in range(steps):
-            step()
+        seq.run(steps)
         ev1.record(ext)
         torch.cuda.synchronize()
         ms = ev0.elapsed_time(ev1) / steps
         return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(ms, 4), "steps": steps,
                 "api": "ftc_backend_matmul with FTC_BACKEND_GRAPHS=0 (copy kernel, GEMV and "
-                       "any copy issued per call), pinned staging, sync per call"}
+                       "any copy issued per call), pinned staging, sync per call; the 56 calls "
+                       "from the native loop, as e2e"}
     finally:
         be.close()
 

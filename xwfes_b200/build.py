@@ -4,7 +4,8 @@
 
 Every .cu under csrc/ is compiled by nvcc with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`` and linked into
-xwfes_b200/libftcuda.so (static CUDA runtime).  Objects go to
+xwfes_b200/libftcuda.so (static CUDA runtime); host/call_loop.c (plain C,
+no CUDA) becomes xwfes_b200/libftcloop.so.  Objects go to
 xwfes_b200/_build/; a source newer than its object (or any header newer
 than the library) triggers a rebuild.
 """
@@ -20,6 +21,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libftcuda.so")
+LOOP_SRC = os.path.join(PKG, "host", "call_loop.c")
+LOOP_LIB = os.path.join(PKG, "libftcloop.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -64,6 +67,13 @@ def build(verbose=False, force=False):
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    # the native caller loop used by the end-to-end benchmark (plain C)
+    if _stale(LOOP_LIB, [LOOP_SRC]):
+        cmd = ["gcc", "-O2", "-std=c11", "-Wall", "-Wextra", "-Werror", "-shared", "-fPIC",
+               "-o", LOOP_LIB, LOOP_SRC]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"gcc failed for {LOOP_SRC}:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 

@@ -499,6 +499,57 @@ class HostTensor:
 
 # ------------------------------------------------------------ backend
 
+LOOP_PATH = os.path.join(PKG, "libftcloop.so")
+_loop = None
+
+
+def loop_lib():
+    """Load libftcloop.so (host/call_loop.c): the native caller loop."""
+    global _loop
+    if _loop is None:
+        if not os.path.exists(LOOP_PATH):
+            raise FileNotFoundError(
+                f"{LOOP_PATH} is missing: build it with `python -m xwfes_b200.build`")
+        L = C.CDLL(LOOP_PATH)
+        L.ftc_call_loop.restype = C.c_int
+        L.ftc_call_loop.argtypes = [_p, _p, C.c_int, C.POINTER(_p), C.POINTER(_i64),
+                                    C.POINTER(_i64), C.POINTER(_p), C.POINTER(C.c_int),
+                                    C.POINTER(_i64), C.POINTER(_p), C.c_int]
+        _loop = L
+    return _loop
+
+
+class MatmulSequence:
+    """A fixed list of IBackend::matmul calls on one backend, replayed by
+    ``run(reps)`` from native code: each call is ftc_backend_matmul with
+    host buffers, synchronous, in list order -- what an engine's decode loop
+    does per step -- with no interpreter between the calls.  The arrays are
+    checked and their addresses taken once, here; they must stay alive and
+    in place while the sequence is used (it keeps references)."""
+
+    def __init__(self, backend, calls):
+        n = len(calls)
+        self._be = backend
+        self._keep = [c for c in calls]
+        xs, ws, ys = (_p * n)(), (_p * n)(), (_p * n)()
+        ms, ks, ns = (_i64 * n)(), (_i64 * n)(), (_i64 * n)()
+        dts = (C.c_int * n)()
+        for i, (x, M, K, W, y) in enumerate(calls):
+            N = W.ne[1]
+            assert x.dtype == np.float32 and x.flags.c_contiguous and x.size >= M * K
+            assert y.dtype == np.float32 and y.flags.c_contiguous and y.size >= M * N
+            xs[i], ws[i], ys[i] = x.ctypes.data, W._base, y.ctypes.data
+            ms[i], ks[i], ns[i], dts[i] = M, K, N, W.dtype
+        self._args = (n, xs, ms, ks, ws, dts, ns, ys)
+        self._fn = C.cast(lib().ftc_backend_matmul, _p)
+
+    def run(self, reps=1):
+        n, xs, ms, ks, ws, dts, ns, ys = self._args
+        rc = loop_lib().ftc_call_loop(self._fn, self._be._h, n, xs, ms, ks, ws, dts, ns, ys, reps)
+        if rc:
+            raise FtcError("ftc_backend_matmul", rc, last_error())
+
+
 class CudaBackend:
     """Python mirror of the ft::IBackend a CUDA build plugs in
     (ft/include/ft/backend.h:21-40), over the ftc_backend_* C ABI.  Host
@@ -568,6 +619,12 @@ class CudaBackend:
                                      y.ctypes.data)
         if rc:
             raise FtcError("ftc_backend_matmul", rc, last_error())
+
+    def matmul_sequence(self, calls):
+        """A fixed list of ``matmul`` calls, ``calls`` = [(x, M, K, W, y), ...]
+        with the same argument rules, replayed from native code (see
+        MatmulSequence)."""
+        return MatmulSequence(self, calls)
 
     def matmul_down_axpy(self, x, M, n_in, W, y):
         """ft::matmul_down_axpy: y[m] += x_m . W over the first ``n_in`` rows of
