@@ -13,6 +13,8 @@
  *   - row-parallel matmul: ft/src/cpu_backend.cpp:39-58, 90-104
  *   - expert chunk:    ft/src/cpu_backend.cpp:106-149
  *   - MoE routing:     ft/src/engine.cpp:62-72 (softmax), 179-241 (moe_ffn)
+ *   - attention:       ft/src/engine.cpp:137-177 (Engine::Impl::attn), 43-60 and
+ *                      545-551 (RoPE)
  *
  * Q4_K and Q6_K do not exist in the reference (ft/include/ft/types.h:20-27,
  * ft/src/gguf.cpp:129-137).  Their decoders below are written from the
@@ -553,4 +555,105 @@ int ftor_moe_ffn(const float* x, const float* logits, int64_t T, int64_t K, int6
     }
     free(idx); free(w); free(order); free(list); free(xe); free(acb);
     return rc;
+}
+
+/* ---------------------------------------------------------- attention */
+
+/* ft/src/engine.cpp:62-72 (softmax_inplace): max, exp of the shifted
+ * scores in float, their sum in double, one float reciprocal applied. */
+static void softmax_ref(float* p, int64_t n) {
+    float mx = p[0];
+    for (int64_t i = 1; i < n; ++i) mx = p[i] > mx ? p[i] : mx;
+    double sum = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        p[i] = expf(p[i] - mx);
+        sum += p[i];
+    }
+    const float inv = (float)(1.0 / sum);
+    for (int64_t i = 0; i < n; ++i) p[i] *= inv;
+}
+
+struct attn_ctx {
+    const float *q, *kc, *vc, *kb, *vb;
+    float* out;
+    int64_t nh, gqa, hd, dk, base;
+    float scale;
+};
+
+/* ft/src/engine.cpp:137-177 (Engine::Impl::attn), one (row, head) item:
+ * causal length base + m + 1; positions below base from the cache, the rest
+ * from the current block; scores d * scale with d summed in k order;
+ * output summed in position order, positions of weight zero skipped. */
+static void attn_items(void* vctx, int64_t b, int64_t e) {
+    const struct attn_ctx* c = (const struct attn_ctx*)vctx;
+    float* sc = NULL;
+    int64_t cap = 0;
+    for (int64_t idx = b; idx < e; ++idx) {
+        const int64_t m = idx / c->nh, h = idx % c->nh, kvh = h / c->gqa;
+        const float* qs = c->q + (m * c->nh + h) * c->hd;
+        const int64_t len = c->base + m + 1;
+        if (len > cap) {
+            free(sc);
+            sc = (float*)malloc((size_t)len * sizeof(float));
+            cap = len;
+            if (!sc) return;
+        }
+        for (int64_t p = 0; p < len; ++p) {
+            const float* kp = (p < c->base ? c->kc + p * c->dk : c->kb + (p - c->base) * c->dk) +
+                              kvh * c->hd;
+            float d = 0.f;
+            for (int64_t t = 0; t < c->hd; ++t) d += qs[t] * kp[t];
+            sc[p] = d * c->scale;
+        }
+        softmax_ref(sc, len);
+        float* o = c->out + (m * c->nh + h) * c->hd;
+        for (int64_t t = 0; t < c->hd; ++t) o[t] = 0.f;
+        for (int64_t p = 0; p < len; ++p) {
+            const float w = sc[p];
+            if (w == 0.f) continue;
+            const float* vp = (p < c->base ? c->vc + p * c->dk : c->vb + (p - c->base) * c->dk) +
+                              kvh * c->hd;
+            for (int64_t t = 0; t < c->hd; ++t) o[t] += w * vp[t];
+        }
+    }
+    free(sc);
+}
+
+int ftor_attention(const float* q, int64_t M, int64_t n_head, int64_t n_head_kv,
+                   int64_t head_dim, const float* k_cache, const float* v_cache, int64_t base,
+                   const float* k_blk, const float* v_blk, float* out, int threads) {
+    if (M <= 0 || n_head <= 0 || n_head_kv <= 0 || head_dim <= 0 || n_head % n_head_kv || base < 0)
+        return -1;
+    struct attn_ctx c = {q, k_cache, v_cache, k_blk, v_blk, out, n_head, n_head / n_head_kv,
+                         head_dim, n_head_kv * head_dim, base,
+                         1.f / sqrtf((float)head_dim)};
+    parallel_for(M * n_head, threads, attn_items, &c);
+    return 0;
+}
+
+/* ft/src/engine.cpp:43-60 (rope_vec): frequency and angle in double, cos and
+ * sin rounded to float, the rotation in float (pairs (i, i + hd/2) for NeoX,
+ * (2i, 2i + 1) otherwise). */
+void ftor_rope_vec(float* v, int64_t hd, int64_t pos, double theta, int neox) {
+    for (int64_t i = 0; i < hd / 2; ++i) {
+        const double f = pow(theta, -2.0 * (double)i / (double)hd);
+        const double ang = (double)pos * f;
+        const float c = (float)cos(ang);
+        const float s = (float)sin(ang);
+        const int64_t i0 = neox ? i : 2 * i, i1 = neox ? i + hd / 2 : 2 * i + 1;
+        const float a = v[i0], b = v[i1];
+        v[i0] = a * c - b * s;
+        v[i1] = a * s + b * c;
+    }
+}
+
+/* ft/src/engine.cpp:545-551: every head of rows m = 0..M-1 at position
+ * base + m; x is [M][heads][hd]. */
+int ftor_rope(float* x, int64_t M, int64_t heads, int64_t hd, int64_t base, double theta,
+              int neox) {
+    if (M < 0 || heads <= 0 || hd <= 0 || hd % 2) return -1;
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t h = 0; h < heads; ++h)
+            ftor_rope_vec(x + (m * heads + h) * hd, hd, base + m, theta, neox);
+    return 0;
 }

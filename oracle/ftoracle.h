@@ -35,6 +35,12 @@ int ftor_route_topk(const float* logits, const float* bias, int64_t T, int64_t E
 int ftor_moe_ffn(const float* x, const float* logits, int64_t T, int64_t K, int64_t n_ff,
                  int64_t E, int64_t U, const uint8_t* gate_exps, const uint8_t* up_exps,
                  const uint8_t* down_exps, int dtype, float* out, int threads);
+int ftor_attention(const float* q, int64_t M, int64_t n_head, int64_t n_head_kv,
+                   int64_t head_dim, const float* k_cache, const float* v_cache, int64_t base,
+                   const float* k_blk, const float* v_blk, float* out, int threads);
+void ftor_rope_vec(float* v, int64_t hd, int64_t pos, double theta, int neox);
+int ftor_rope(float* x, int64_t M, int64_t heads, int64_t hd, int64_t base, double theta,
+              int neox);
 
 #ifdef __cplusplus
 }

@@ -3,6 +3,8 @@
 * ``liboracle.so`` -- ftoracle.c, the C restatement of the reference path.
 * ``_ref/libftref.so`` -- the reference's own ``ft/src/cpu_backend.cpp``
   compiled from its sources (oracle/Makefile), reached through ref_shim.cpp.
+* ``_ref/libftref_engine.so`` -- the reference engine's attention and RoPE
+  (``ft/src/engine.cpp``), reached through ref_engine_shim.cpp.
 
 Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use
 this module; the product path never does.
@@ -16,6 +18,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB = os.path.join(HERE, "liboracle.so")
 _REF = os.path.join(HERE, "_ref", "libftref.so")
+_REF_ENGINE = os.path.join(HERE, "_ref", "libftref_engine.so")
 
 _f = C.c_float
 _i64 = C.c_int64
@@ -72,6 +75,9 @@ def lib():
         _lib.ftor_route_topk.argtypes = [_p, _p, _i64, _i64, _i64, _p, _p]
         _lib.ftor_moe_ffn.argtypes = [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
                                       C.c_int, _p, C.c_int]
+        _lib.ftor_attention.argtypes = [_p, _i64, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _p,
+                                        C.c_int]
+        _lib.ftor_rope.argtypes = [_p, _i64, _i64, _i64, _i64, C.c_double, C.c_int]
         for fn in ("ftor_block_elems", "ftor_block_bytes", "ftor_row_bytes"):
             getattr(_lib, fn).restype = _i64
         _lib.ftor_row_bytes.argtypes = [C.c_int, _i64]
@@ -99,6 +105,24 @@ def ref():
         r.ftref_matmul_down_axpy.argtypes = [_p, _i64, _i64, _p, C.c_uint32, _i64, _p]
         _ref = r
     return _ref
+
+
+_ref_engine = None
+
+
+def ref_engine():
+    """The reference engine's own attention and RoPE (None when
+    _ref/libftref_engine.so was never built)."""
+    global _ref_engine
+    if _ref_engine is None and os.path.exists(_REF_ENGINE):
+        r = _load(_REF_ENGINE)
+        r.ftref_attn.argtypes = [_p, _i64, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _p, C.c_int]
+        r.ftref_rope_vec.restype = None
+        r.ftref_rope_vec.argtypes = [_p, _i64, _i64, C.c_double, C.c_int]
+        r.ftref_softmax.restype = None
+        r.ftref_softmax.argtypes = [_p, _i64]
+        _ref_engine = r
+    return _ref_engine
 
 
 def _ptr(a):
@@ -247,3 +271,31 @@ def ref_matmul_down_axpy(x, w, dtype, n, y):
     _check(ref().ftref_matmul_down_axpy(_ptr(x), x.shape[0], w.shape[0], _ptr(w), dtype, n,
                                         _ptr(y)), "ftref_matmul_down_axpy")
     return y
+
+
+# -------------------------------------------------------------- attention
+
+def attention(q, n_head, n_head_kv, head_dim, k_cache, v_cache, base, k_blk, v_blk, threads=1):
+    """Engine::Impl::attn (ft/src/engine.cpp:137-177) restated: q fp32
+    ``[M, n_head*head_dim]`` after RoPE, cache rows ``[base, dk]`` (rows
+    below ``base`` are read), the block's rows ``[M, dk]``; returns the
+    attention output ``[M, n_head*head_dim]``."""
+    q = _c(q, np.float32)
+    M = q.shape[0]
+    dk = n_head_kv * head_dim
+    kc = _c(k_cache, np.float32) if base else np.zeros((1, dk), np.float32)
+    vc = _c(v_cache, np.float32) if base else np.zeros((1, dk), np.float32)
+    kb, vb = _c(k_blk, np.float32), _c(v_blk, np.float32)
+    out = np.empty((M, n_head * head_dim), dtype=np.float32)
+    _check(lib().ftor_attention(_ptr(q), M, n_head, n_head_kv, head_dim, _ptr(kc), _ptr(vc), base,
+                                _ptr(kb), _ptr(vb), _ptr(out), threads), "ftor_attention")
+    return out
+
+
+def rope(x, heads, head_dim, base, theta, neox):
+    """RoPE of rows m at positions base + m (ft/src/engine.cpp:43-60, 545-551),
+    on a copy of x ``[M, heads*head_dim]``."""
+    x = np.array(x, dtype=np.float32, order="C", copy=True)
+    _check(lib().ftor_rope(_ptr(x), x.shape[0], heads, head_dim, base, theta, 1 if neox else 0),
+           "ftor_rope")
+    return x
