@@ -405,6 +405,7 @@ def run_ours(args, rank, world, local_rank):
     gemm_status = ftc.device_status()
     tp_block = time_tp(dev, world, rank)
     moe = side_measurement("moe", lambda: time_moe(dev), None) if world == 1 else None
+    attn = side_measurement("attention", lambda: time_attention(dev), None)
     ep_layer = time_ep(dev, world, rank)
     clk.__exit__(None, None, None)
 
@@ -490,6 +491,7 @@ def run_ours(args, rank, world, local_rank):
         "prefill_dequant_gemm": prefill_sum,
         "tp_block": tp_block,
         "moe": moe,
+        "attention": attn,
         "ep_moe": ep_layer,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
@@ -745,6 +747,90 @@ def time_tp(dev, world, rank, seed=0):
             "kernels": "M<=8: decode GEMV (fp32); M>8: tcgen05 GEMM on row-scaled fp16",
             **({"note": peer_note} if peer_note else {}),
             "per_M": out}
+
+
+ATTN_CTX = [512, 4096, 32768]
+
+
+def time_attention(dev, reps=50):
+    """The engine's attention on the device (ftc_attention, ft/src/engine.cpp:
+    137-177) at Llama-3-8B's heads (32 query heads, 8 KV heads, head_dim
+    128): one decode row over a context of n positions, fp32 KV rows as
+    ft::KvCache keeps them.  Enough layer copies are rotated (about 512 MB)
+    that every call reads its K and V from HBM.  Beside it, the reference's
+    own CPU attention (Engine::Impl::attn) on this host's cores at 4096."""
+    import torch
+    from xwfes_b200 import ftc
+    nh, nkv, hd = 32, 8, 128
+    dk = nkv * hd
+    hbm, _, _ = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    out = {}
+    st = torch.cuda.Stream(device=dev)
+    for n in ATTN_CTX:
+        base = n - 1
+        row_bytes = n * dk * 4
+        copies = max(2, (512 << 20) // (2 * row_bytes))
+        ks = [torch.randn((n, dk), device=dev, generator=g) for _ in range(copies)]
+        vs = [torch.randn((n, dk), device=dev, generator=g) for _ in range(copies)]
+        q = torch.randn((1, nh * hd), device=dev, generator=g)
+        o = torch.empty((1, nh * hd), device=dev)
+        need = int(ftc.lib().ftc_attention_workspace_bytes(1, nh, nkv, hd, base))
+        ws = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+        with torch.cuda.stream(st):
+            def call(i):
+                k, v = ks[i % copies], vs[i % copies]
+                ftc.attention(q, nh, nkv, hd, k[base:], v[base:], base=base, k_cache=k,
+                              v_cache=v, out=o, ws=ws, stream=st)
+            for i in range(copies):
+                call(i)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                for i in range(copies):
+                    call(i)
+            for _ in range(3):
+                graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            r = max(1, reps // copies)
+            e0.record(st)
+            for _ in range(r):
+                graph.replay()
+            e1.record(st)
+            e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (r * copies)
+        kv_bytes = 2 * row_bytes
+        gbs = kv_bytes / (us * 1e-6) / 1e9
+        out[str(n)] = {"us": round(us, 2), "kv_bytes": kv_bytes, "GBps": round(gbs, 1),
+                       "frac_of_hbm": round(gbs / hbm, 3),
+                       "layer_copies": copies}
+        del graph, ks, vs
+    ref = None
+    try:
+        from oracle import oracle as O
+        R = O.ref_engine()
+        if R is not None:
+            n, threads = 4096, os.cpu_count() or 1
+            rng = np.random.default_rng(0)
+            qh = rng.standard_normal((1, nh * hd), dtype=np.float32)
+            kh = rng.standard_normal((n, dk), dtype=np.float32)
+            vh = rng.standard_normal((n, dk), dtype=np.float32)
+            oh = np.empty_like(qh)
+            p = lambda a: a.ctypes.data_as(O._p)  # noqa: E731
+            ts = []
+            for _ in range(5):
+                t0 = time.perf_counter()
+                R.ftref_attn(p(qh), 1, nh, nkv, hd, p(kh), p(vh), n - 1, p(kh[n - 1:]),
+                             p(vh[n - 1:]), p(oh), threads)
+                ts.append(time.perf_counter() - t0)
+            ref = {"ctx": n, "us": round(statistics.median(ts) * 1e6, 1), "cores": threads,
+                   "kind": "reference (Engine::Impl::attn compiled from its sources)"}
+    except Exception as e:  # the checker library is optional on a box
+        ref = {"error": str(e)[:200]}
+    return {"workload": "Llama-3-8B attention heads (32 q, 8 kv, head_dim 128), one decode row, "
+                        "fp32 KV cache",
+            "api": "ftc_attention (split positions, cp.async K/V staging, split combine)",
+            "per_ctx": out, "reference_cpu_4096": ref, "status": ftc.device_status()}
 
 
 MOE_T = [1, 64, 1024]

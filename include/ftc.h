@@ -444,6 +444,55 @@ int ftc_mul_mat_vec_silu(ftc_peer_ar* ar, int dtype, const void* w, int64_t N, i
                          int64_t row_stride, const float* gu, int64_t up_offset, float* y,
                          void* stream);
 
+/* ------------------------------------------------------------ attention */
+
+/* Bytes of workspace ftc_attention needs for this shape (0: none). */
+size_t ftc_attention_workspace_bytes(int64_t M, int64_t n_head, int64_t n_head_kv,
+                                     int64_t head_dim, int64_t base);
+
+/* Causal grouped-query attention on DEVICE buffers, Engine::Impl::attn
+ * (ft/src/engine.cpp:137-177): query row m (position base + m) of head h
+ * attends positions 0 .. base + m of KV head h / (n_head / n_head_kv), with
+ * scores q . k / sqrt(head_dim) and a softmax over them.  q and out are fp32
+ * [M][n_head][head_dim]; K and V rows are fp32 [position][kv_stride] with the
+ * head's head_dim values at kv_head * head_dim.  Positions below base are
+ * read from k_cache / v_cache (row p at p * kv_stride; may be NULL when base
+ * is 0), the rest from k_blk / v_blk (position p at (p - base) * kv_stride),
+ * which is the cache itself at row base when the caller stored the block
+ * there first (the engine's write_kv path, ft/src/engine.cpp:553-565).
+ * head_dim 64, 128 or 256; kv_stride >= n_head_kv * head_dim, a multiple of
+ * 4; every buffer 16-byte aligned; ws at least
+ * ftc_attention_workspace_bytes (may be NULL when that is 0). */
+int ftc_attention(const float* q, int64_t M, int64_t n_head, int64_t n_head_kv, int64_t head_dim,
+                  const float* k_cache, const float* v_cache, int64_t kv_stride, int64_t base,
+                  const float* k_blk, const float* v_blk, float* out, void* ws, size_t ws_bytes,
+                  void* stream);
+
+/* Rotary position embedding in place on DEVICE fp32 x [M][heads][head_dim],
+ * row m at position base + m: rope_vec (ft/src/engine.cpp:43-60) as the
+ * engine applies it to q and k (ft/src/engine.cpp:545-551); neox != 0 rotates
+ * the pairs (i, i + head_dim/2), else (2i, 2i + 1).  Angles in double, the
+ * rotation in float with separately rounded products, as the reference. */
+int ftc_rope(float* x, int64_t M, int64_t heads, int64_t head_dim, int64_t base, double theta,
+             int neox, void* stream);
+
+/* The engine's KV cache in this backend's HBM: ft::KvCache::alloc
+ * (ft/include/ft/kv_cache.h:12-20), n_layers x capacity rows of dim fp32 for
+ * K and for V, zero-filled; replaces any cache the backend held. */
+int ftc_backend_kv_alloc(ftc_backend* be, int64_t n_layers, int64_t capacity, int64_t dim);
+
+/* The engine's per-layer attention step with HOST buffers: q [M][n_head *
+ * head_dim] and the block's k_new / v_new [M][n_head_kv * head_dim] (all fp32,
+ * after RoPE), out [M][n_head * head_dim].  With write_kv the block's rows
+ * are stored into the device cache at rows [base, base + M) of `layer` first
+ * (ft/src/engine.cpp:553-559), else they are used for this call only.  Then
+ * ftc_attention over the cache's rows [0, base) and the block.  Synchronous,
+ * like the engine's CPU attention.  Requires ftc_backend_kv_alloc with dim =
+ * n_head_kv * head_dim and base + M <= capacity. */
+int ftc_backend_attention(ftc_backend* be, int64_t layer, int64_t base, int64_t M, int64_t n_head,
+                          int64_t n_head_kv, int64_t head_dim, const float* q,
+                          const float* k_new, const float* v_new, int write_kv, float* out);
+
 #ifdef __cplusplus
 }
 #endif

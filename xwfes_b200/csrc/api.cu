@@ -122,6 +122,16 @@ int moe_experts(const ftc_moe_desc* d, const void* x, int x_dtype, int64_t rows,
                 void* ws, size_t ws_bytes, cudaStream_t st);
 int moe_ffn(const ftc_moe_desc* d, const float* logits, const void* x, int x_dtype, int64_t T,
             float* out, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t attention_workspace_bytes(int64_t M, int64_t n_head, int64_t n_head_kv, int64_t head_dim,
+                                 int64_t base);
+int attention(const float* q, int64_t M, int64_t n_head, int64_t n_head_kv, int64_t head_dim,
+              const float* k_cache, const float* v_cache, int64_t kv_stride, int64_t base,
+              const float* k_blk, const float* v_blk, float* out, void* ws, size_t ws_bytes,
+              cudaStream_t st);
+int attention_check(int64_t M, int64_t n_head, int64_t n_head_kv, int64_t head_dim, int64_t base,
+                    const char* who);
+int rope(float* x, int64_t M, int64_t heads, int64_t head_dim, int64_t base, double theta,
+         int neox, cudaStream_t st);
 
 // status readers of the translation units whose kernels use bounded waits
 int devstat_gemv_q4k(int clear);
@@ -184,6 +194,13 @@ struct ftc_backend {
     DevBuf pin_in{nullptr, 0, true}, pin_out{nullptr, 0, true};
     DevBuf dx, dy, dwin, dtmp;
     std::mutex mu;
+
+    // the engine's KV cache in HBM (ftc_backend_kv_alloc): K of all layers,
+    // then V, each [layer][capacity][dim] fp32; dattn stages one attention
+    // call's q, block rows, workspace and output
+    float* kv = nullptr;
+    int64_t kv_layers = 0, kv_cap = 0, kv_dim = 0;
+    DevBuf dattn;
 
     // ftc_backend_matmul's per-call work (copy in, GEMV or GEMM, copy out)
     // captured once per (weight, shape) and replayed as a CUDA graph: one
@@ -320,6 +337,8 @@ void ftc_backend_destroy(ftc_backend* be) {
     be->dy.release();
     be->dwin.release();
     be->dtmp.release();
+    be->dattn.release();
+    if (be->kv) cudaFree(be->kv);
     if (be->stream) cudaStreamDestroy(be->stream);
     delete be;
 }
@@ -522,6 +541,94 @@ int ftc_backend_run_expert_chunk(ftc_backend* be, const ftc_expert_chunk_job* jo
     return ok();
 }
 
+int ftc_backend_kv_alloc(ftc_backend* be, int64_t n_layers, int64_t capacity, int64_t dim) {
+    int rc = bind(be);
+    if (rc) return rc;
+    FTC_REQUIRE(n_layers > 0 && capacity > 0 && dim > 0 && dim % 4 == 0, FTC_E_INVALID,
+                "ftc_backend_kv_alloc: empty shape or dim not a multiple of 4");
+    FTC_REQUIRE(n_layers <= (1 << 20) && capacity <= (1 << 28) && dim <= (1 << 20) &&
+                    n_layers * capacity <= ((int64_t)1 << 40) / dim,
+                FTC_E_INVALID, "ftc_backend_kv_alloc: cache too large");
+    std::lock_guard<std::mutex> lk(be->mu);
+    FTC_CUDA(cudaStreamSynchronize(be->stream));  // no call may still read the old cache
+    if (be->kv) cudaFree(be->kv);
+    be->kv = nullptr;
+    be->kv_layers = be->kv_cap = be->kv_dim = 0;
+    const size_t bytes = (size_t)(2 * n_layers * capacity * dim) * sizeof(float);
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess)
+        return set_error(FTC_E_NOMEM, std::string("ftc_backend_kv_alloc: ") + cudaGetErrorString(e));
+    const cudaError_t z = cudaMemsetAsync(p, 0, bytes, be->stream);  // KvCache::alloc zero-fills
+    if (z != cudaSuccess) {
+        cudaFree(p);
+        return cuda_error(z, "ftc_backend_kv_alloc: cudaMemsetAsync");
+    }
+    be->kv = static_cast<float*>(p);
+    be->kv_layers = n_layers;
+    be->kv_cap = capacity;
+    be->kv_dim = dim;
+    return ok();
+}
+
+int ftc_backend_attention(ftc_backend* be, int64_t layer, int64_t base, int64_t M, int64_t n_head,
+                          int64_t n_head_kv, int64_t head_dim, const float* q,
+                          const float* k_new, const float* v_new, int write_kv, float* out) {
+    int rc = bind(be);
+    if (rc) return rc;
+    if ((rc = attention_check(M, n_head, n_head_kv, head_dim, base, "ftc_backend_attention")))
+        return rc;
+    FTC_REQUIRE(q && k_new && v_new && out, FTC_E_INVALID, "ftc_backend_attention: null pointer");
+    if (inject_fail("ftc_backend_attention"))
+        return set_error(FTC_E_INJECTED, "ftc_backend_attention: injected failure");
+    std::lock_guard<std::mutex> lk(be->mu);
+    FTC_REQUIRE(be->kv, FTC_E_INVALID, "ftc_backend_attention: no KV cache (ftc_backend_kv_alloc)");
+    const int64_t dk = n_head_kv * head_dim;
+    FTC_REQUIRE(dk == be->kv_dim, FTC_E_INVALID,
+                "ftc_backend_attention: n_head_kv * head_dim differs from the cache's dim");
+    FTC_REQUIRE(layer >= 0 && layer < be->kv_layers, FTC_E_INVALID,
+                "ftc_backend_attention: layer out of range");
+    FTC_REQUIRE(base + M <= be->kv_cap, FTC_E_INVALID,
+                "ftc_backend_attention: base + M exceeds the cache capacity");
+    // staging: [q | k_new | v_new | out | workspace], each 256-byte aligned
+    auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+    const size_t qb = (size_t)(M * n_head * head_dim) * 4, rb = (size_t)(M * dk) * 4;
+    const size_t wsb = attention_workspace_bytes(M, n_head, n_head_kv, head_dim, base);
+    const size_t in_b = up(qb) + 2 * up(rb);
+    if ((rc = be->pin_in.ensure(in_b)) || (rc = be->pin_out.ensure(qb)) ||
+        (rc = be->dattn.ensure(in_b + up(qb) + up(wsb))))
+        return rc;
+    uint8_t* hp = static_cast<uint8_t*>(be->pin_in.p);
+    std::memcpy(hp, q, qb);
+    std::memcpy(hp + up(qb), k_new, rb);
+    std::memcpy(hp + up(qb) + up(rb), v_new, rb);
+    uint8_t* dp = static_cast<uint8_t*>(be->dattn.p);
+    cudaStream_t st = be->stream;
+    FTC_CUDA(cudaMemcpyAsync(dp, hp, in_b, cudaMemcpyHostToDevice, st));
+    const float* dq = reinterpret_cast<const float*>(dp);
+    const float* dkn = reinterpret_cast<const float*>(dp + up(qb));
+    const float* dvn = reinterpret_cast<const float*>(dp + up(qb) + up(rb));
+    float* dout = reinterpret_cast<float*>(dp + in_b);
+    void* dws = wsb ? dp + in_b + up(qb) : nullptr;
+    float* kc = be->kv + layer * be->kv_cap * dk;
+    float* vc = be->kv + (be->kv_layers + layer) * be->kv_cap * dk;
+    const float* kb = dkn;
+    const float* vb = dvn;
+    if (write_kv) {  // the block joins the cache (ft/src/engine.cpp:553-559)
+        FTC_CUDA(cudaMemcpyAsync(kc + base * dk, dkn, rb, cudaMemcpyDeviceToDevice, st));
+        FTC_CUDA(cudaMemcpyAsync(vc + base * dk, dvn, rb, cudaMemcpyDeviceToDevice, st));
+        kb = kc + base * dk;
+        vb = vc + base * dk;
+    }
+    if ((rc = attention(dq, M, n_head, n_head_kv, head_dim, kc, vc, dk, base, kb, vb, dout, dws,
+                        wsb, st)))
+        return rc;
+    FTC_CUDA(cudaMemcpyAsync(be->pin_out.p, dout, qb, cudaMemcpyDeviceToHost, st));
+    FTC_CUDA(cudaStreamSynchronize(st));
+    std::memcpy(out, be->pin_out.p, qb);
+    return ok();
+}
+
 int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int64_t n_in,
                                  const void* w_host, int dtype, int64_t N, float* y) {
     int rc = bind(be);
@@ -696,6 +803,28 @@ int ftc_matmul_down_axpy(int dtype, const void* w, int64_t n_in, int64_t N, int6
                          const float* x, int64_t M, float* y, void* ws, size_t ws_bytes,
                          void* stream) {
     int rc = down_axpy(dtype, w, n_in, N, row_stride, x, M, y, ws, ws_bytes, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+size_t ftc_attention_workspace_bytes(int64_t M, int64_t n_head, int64_t n_head_kv,
+                                     int64_t head_dim, int64_t base) {
+    return attention_workspace_bytes(M, n_head, n_head_kv, head_dim, base);
+}
+
+int ftc_attention(const float* q, int64_t M, int64_t n_head, int64_t n_head_kv, int64_t head_dim,
+                  const float* k_cache, const float* v_cache, int64_t kv_stride, int64_t base,
+                  const float* k_blk, const float* v_blk, float* out, void* ws, size_t ws_bytes,
+                  void* stream) {
+    if (inject_fail("ftc_attention"))
+        return set_error(FTC_E_INJECTED, "ftc_attention: injected failure");
+    int rc = attention(q, M, n_head, n_head_kv, head_dim, k_cache, v_cache, kv_stride, base, k_blk,
+                       v_blk, out, ws, ws_bytes, (cudaStream_t)stream);
+    return rc ? rc : ok();
+}
+
+int ftc_rope(float* x, int64_t M, int64_t heads, int64_t head_dim, int64_t base, double theta,
+             int neox, void* stream) {
+    int rc = rope(x, M, heads, head_dim, base, theta, neox, (cudaStream_t)stream);
     return rc ? rc : ok();
 }
 

@@ -71,6 +71,13 @@ SIGNATURES = {
     "ftc_peer_ar_destroy": (C.c_int, [_p]),
     "ftc_mul_mat_vec_allreduce": (C.c_int, [_p, C.c_int, _p, _i64, _i64, _i64, _p, _p, _p]),
     "ftc_mul_mat_vec_silu": (C.c_int, [_p, C.c_int, _p, _i64, _i64, _i64, _p, _i64, _p, _p]),
+    "ftc_attention_workspace_bytes": (C.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
+    "ftc_attention": (C.c_int, [_p, _i64, _i64, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p,
+                                C.c_size_t, _p]),
+    "ftc_rope": (C.c_int, [_p, _i64, _i64, _i64, _i64, C.c_double, C.c_int, _p]),
+    "ftc_backend_kv_alloc": (C.c_int, [_p, _i64, _i64, _i64]),
+    "ftc_backend_attention": (C.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
+                                        C.c_int, _p]),
 }
 
 
@@ -215,6 +222,37 @@ def mul_mat_vec_multi(ws, dtype, ns, k, x, ys=None, row_stride=None, stream=None
     check(lib().ftc_mul_mat_vec_multi(t, P, wa, na, k, rs, x2.data_ptr(), m, ya, _stream(stream)),
           "ftc_mul_mat_vec_multi")
     return ys
+
+
+def attention(q, n_head, n_head_kv, head_dim, k_blk, v_blk, base=0, k_cache=None, v_cache=None,
+              kv_stride=None, out=None, ws=None, stream=None):
+    """Causal grouped-query attention on the GPU (ftc_attention): q fp32 CUDA
+    [M, n_head*head_dim] at positions base .. base+M-1; K/V rows [pos,
+    kv_stride] -- rows below ``base`` from k_cache / v_cache, the block's
+    from k_blk / v_blk.  Returns out [M, n_head*head_dim]."""
+    import torch
+    q2 = q.reshape(q.shape[0], -1)
+    M = q2.shape[0]
+    ks = kv_stride if kv_stride is not None else n_head_kv * head_dim
+    if out is None:
+        out = torch.empty((M, n_head * head_dim), dtype=torch.float32, device=q.device)
+    need = int(lib().ftc_attention_workspace_bytes(M, n_head, n_head_kv, head_dim, base))
+    if need and (ws is None or ws.numel() < need):
+        ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    check(lib().ftc_attention(q2.data_ptr(), M, n_head, n_head_kv, head_dim, ptr(k_cache),
+                              ptr(v_cache), ks, base, k_blk.data_ptr(), v_blk.data_ptr(),
+                              out.data_ptr(), ptr(ws) if need else None, need, _stream(stream)),
+          "ftc_attention")
+    return out
+
+
+def rope(x, heads, head_dim, base, theta, neox, stream=None):
+    """RoPE in place on fp32 CUDA x [M, heads*head_dim], row m at position
+    base + m (ftc_rope); returns x."""
+    check(lib().ftc_rope(x.data_ptr(), x.shape[0], heads, head_dim, base, float(theta),
+                         1 if neox else 0, _stream(stream)), "ftc_rope")
+    return x
 
 
 _TORCH_OUT = {F.F32: "float32", F.BF16: "bfloat16", F.F16: "float16"}
@@ -619,6 +657,30 @@ class CudaBackend:
                                      y.ctypes.data)
         if rc:
             raise FtcError("ftc_backend_matmul", rc, last_error())
+
+    def kv_alloc(self, n_layers, capacity, dim):
+        """The engine's KV cache in this backend's HBM (ftc_backend_kv_alloc)."""
+        check(lib().ftc_backend_kv_alloc(self._h, n_layers, capacity, dim), "ftc_backend_kv_alloc")
+
+    def attention(self, layer, base, q, k_new, v_new, n_head, n_head_kv, head_dim, write_kv=True,
+                  out=None):
+        """One layer's attention with host arrays (ftc_backend_attention): q
+        fp32 [M, n_head*head_dim], k_new / v_new [M, n_head_kv*head_dim];
+        returns out [M, n_head*head_dim]."""
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        k_new = np.ascontiguousarray(k_new, dtype=np.float32)
+        v_new = np.ascontiguousarray(v_new, dtype=np.float32)
+        M = q.shape[0]
+        assert q.size == M * n_head * head_dim
+        assert k_new.size == v_new.size == M * n_head_kv * head_dim
+        if out is None:
+            out = np.empty((M, n_head * head_dim), dtype=np.float32)
+        assert out.dtype == np.float32 and out.flags.c_contiguous and out.size >= q.size
+        check(lib().ftc_backend_attention(self._h, layer, base, M, n_head, n_head_kv, head_dim,
+                                          q.ctypes.data, k_new.ctypes.data, v_new.ctypes.data,
+                                          1 if write_kv else 0, out.ctypes.data),
+              "ftc_backend_attention")
+        return out
 
     def matmul_sequence(self, calls):
         """A fixed list of ``matmul`` calls, ``calls`` = [(x, M, K, W, y), ...]
