@@ -10,16 +10,19 @@
 // fp32, as ft::KvCache keeps them (ft/include/ft/kv_cache.h:12-20).
 //
 // Decode reads every cached K and V row once per KV head, so the kernel is
-// HBM-bound: the positions of a row are cut into splits of L (32 or 64)
-// positions, one CTA per (KV head, group of G query heads, row, split).  A
-// CTA brings its split's K and V rows into shared memory with 16-byte
-// cp.async copies (all in flight at once), computes the G x L scores from
-// shared memory, a partial softmax (split maximum, exponentials, their sum)
-// and the weighted V sum.  A row with one split is finished in place; else a
-// second kernel combines the splits in split order (deterministic):
+// HBM-bound: the positions of a row are cut into splits of L positions (a
+// multiple of 32), one CTA per (KV head, group of G query heads, row,
+// split), with as many splits as fill one wave of resident CTAs.  A CTA
+// walks its split in chunks of 32 positions whose K and V rows it brings
+// into shared memory with 16-byte cp.async copies, one chunk ahead of the
+// one it computes on:
+// G x 32 scores from shared memory, an online softmax (running maximum and
+// sum, the accumulator rescaled when the maximum grows) and the weighted V
+// sum.  A row with one split is finished in place; else a second kernel
+// combines the splits in split order (deterministic):
 //   out = sum_s acc_s * exp(max_s - max) / sum_s sum_s * exp(max_s - max).
 // The reference normalises before the V sum (w = e / sum) and sums in
-// position order; the results agree to fp32 rounding (~1e-6 relative).
+// position order; the results agree to fp32 rounding.
 //
 // RoPE (ft/src/engine.cpp:43-60, applied at 545-551): frequencies, angles,
 // cos and sin in double as the reference computes them, rounded to float,
@@ -58,21 +61,38 @@ struct AttnArgs {
     float scale;
 };
 
-// Shared layout: K [L][HD + 4] (padded: the 16-byte loads of 8 lanes reading
-// 8 consecutive positions at the same k hit 8 different bank quads), V
-// [L][HD], q [G][HD], scores [G][L], split statistics [G][2]; the V-sum
-// reduction reuses the K area.
+// A CTA walks its split in chunks of 32 positions, two chunk buffers in
+// shared memory: while chunk c is scored and summed, chunk c + 1 is in
+// flight.  Buffer layout: K [32][HD + 4] (padded: the 16-byte loads of 8
+// lanes reading 8 consecutive positions at the same k hit 8 different bank
+// quads), V [32][HD].  Then q [G][HD], the chunk's exponentials [G][32] and
+// per head the running maximum, running sum and this chunk's rescale factor
+// (online softmax: the accumulator is multiplied by exp(old max - new max)
+// whenever the maximum grows).  The final cross-group V-sum reduction reuses
+// buffer 0 (512 G floats, within 32 (2 HD + 4) for every HD and G <= 8).
+constexpr int kChunk = 32;
+static_assert(512 * 8 <= kChunk * (2 * 64 + 4), "V-sum reduction fits a chunk buffer");
+
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 template <int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_split(const AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
-    constexpr int KP = HD + 4;
-    const int L = a.L;
-    float* ks = sm;
-    float* vs = ks + L * KP;
-    float* qs = vs + L * HD;
-    float* sc = qs + G * HD;
-    float* st = sc + G * L;
+    constexpr int KP = HD + 4, C4 = HD / 4, BUF = kChunk * (KP + HD);
+    constexpr int NGRP = kAttnThreads / C4;  // position groups of the V sum
+    float* qs = sm + 2 * BUF;
+    float* es = qs + G * HD;
+    float* mrun = es + G * kChunk;
+    float* lrun = mrun + G;
+    float* alpha = lrun + G;
 
     const int ngrp = a.gqa / G;
     const int kvh = blockIdx.x / ngrp;
@@ -80,92 +100,117 @@ attn_split(const AttnArgs a) {
     const int m = blockIdx.y;
     const int s = blockIdx.z;
     const int64_t len = a.base + m + 1;
-    const int64_t p0 = (int64_t)s * L;
+    const int64_t p0 = (int64_t)s * a.L;
     if (p0 >= len) return;  // this row has fewer splits
-    const int n = (int)(len - p0 < L ? len - p0 : L);
-    const int S_m = (int)((len + L - 1) / L);
+    const int n = (int)(len - p0 < a.L ? len - p0 : a.L);
+    const int nch = (n + kChunk - 1) / kChunk;
+    const int S_m = (int)((len + a.L - 1) / a.L);
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
 
-    // K and V rows of the split -> shared memory, all copies in flight
-    constexpr int C4 = HD / 4;  // 16-byte pieces per row
-    for (int i = t; i < n * C4; i += kAttnThreads) {
-        const int r = i / C4, c = i - r * C4;
-        const int64_t p = p0 + r;
-        const int64_t off = (p < a.base ? p : p - a.base) * a.kv_stride + (int64_t)kvh * HD + 4 * c;
-        const float* kr = (p < a.base ? a.kc : a.kb) + off;
-        const float* vr = (p < a.base ? a.vc : a.vb) + off;
-        cp_async16(ks + r * KP + 4 * c, kr);
-        cp_async16(vs + r * HD + 4 * c, vr);
-    }
+    // chunk c (rows [32c, 32c + rows) of the split) -> buffer c & 1
+    auto issue = [&](int c) {
+        float* ks = sm + (c & 1) * BUF;
+        float* vs = ks + kChunk * KP;
+        const int rows = min(kChunk, n - kChunk * c);
+        for (int i = t; i < rows * C4; i += kAttnThreads) {
+            const int r = i / C4, cc = i - r * C4;
+            const int64_t p = p0 + kChunk * c + r;
+            const int64_t off =
+                (p < a.base ? p : p - a.base) * a.kv_stride + (int64_t)kvh * HD + 4 * cc;
+            cp_async16(ks + r * KP + 4 * cc, (p < a.base ? a.kc : a.kb) + off);
+            cp_async16(vs + r * HD + 4 * cc, (p < a.base ? a.vc : a.vb) + off);
+        }
+        cp_async_commit();
+    };
+    issue(0);
     for (int i = t; i < G * HD; i += kAttnThreads)
         qs[i] = a.q[((int64_t)m * a.n_head + h0) * HD + i];
-    cp_async_wait_all();
-    __syncthreads();
+    if (t < G) {
+        mrun[t] = -INFINITY;
+        lrun[t] = 0.f;
+    }
+    const int d4 = t % C4, grp = t / C4;
+    float4 acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
 
-    // scores: lane j of warp w takes position j of each 32-position tile and
-    // heads w, w + 4, ...
-    for (int r0 = 0; r0 < n; r0 += 32) {
-        const int r = r0 + lane;
-        if (r < n) {
-            const float4* kr = reinterpret_cast<const float4*>(ks + r * KP);
+    for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch) {
+            issue(c + 1);
+            cp_async_wait<1>();  // chunk c has landed (c + 1 may still fly)
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float* ks = sm + (c & 1) * BUF;
+        const float* vs = ks + kChunk * KP;
+        const int rows = min(kChunk, n - kChunk * c);
+
+        // scores: lane j takes position j, warp w heads w, w + 4, ...
+        if (lane < rows) {
+            const float4* kr = reinterpret_cast<const float4*>(ks + lane * KP);
             for (int g = warp; g < G; g += 4) {
                 const float4* qg = reinterpret_cast<const float4*>(qs + g * HD);
                 float d0 = 0.f, d1 = 0.f;
 #pragma unroll 8
-                for (int c = 0; c < C4; ++c) {
-                    const float4 k4 = kr[c], q4 = qg[c];
+                for (int cc = 0; cc < C4; ++cc) {
+                    const float4 k4 = kr[cc], q4 = qg[cc];
                     d0 = fmaf(q4.x, k4.x, d0);
                     d1 = fmaf(q4.y, k4.y, d1);
                     d0 = fmaf(q4.z, k4.z, d0);
                     d1 = fmaf(q4.w, k4.w, d1);
                 }
-                sc[g * L + r] = (d0 + d1) * a.scale;
+                es[g * kChunk + lane] = (d0 + d1) * a.scale;
             }
         }
-    }
-    __syncthreads();
+        __syncthreads();
 
-    // partial softmax of each head's n scores (warp w: heads w, w + 4, ...)
-    for (int g = warp; g < G; g += 4) {
-        float mx = -INFINITY;
-        for (int r = lane; r < n; r += 32) mx = fmaxf(mx, sc[g * L + r]);
+        // online softmax: new maximum, this chunk's exponentials, rescale
+        for (int g = warp; g < G; g += 4) {
+            const float sv = lane < rows ? es[g * kChunk + lane] : -INFINITY;
+            float cm = sv;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.f;
-        for (int r = lane; r < n; r += 32) {
-            const float e = expf(sc[g * L + r] - mx);
-            sc[g * L + r] = e;
-            sum += e;
-        }
+            for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+            const float mo = mrun[g], mn = fmaxf(mo, cm);
+            const float e = lane < rows ? expf(sv - mn) : 0.f;
+            es[g * kChunk + lane] = e;
+            float se = e;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) {
-            st[2 * g] = mx;
-            st[2 * g + 1] = sum;
+            for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
+            if (lane == 0) {
+                const float al = expf(mo - mn);  // 0 on the first chunk (mo = -inf)
+                alpha[g] = al;
+                lrun[g] = lrun[g] * al + se;
+                mrun[g] = mn;
+            }
         }
-    }
-    __syncthreads();
+        __syncthreads();
 
-    // weighted V sum: thread t takes 4 dimensions (d4) of every NGRP-th
-    // position; the NGRP partial sums are added in group order
-    constexpr int NGRP = kAttnThreads / C4;
-    const int d4 = t % C4, grp = t / C4;
-    float4 acc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r = grp; r < n; r += NGRP) {
-        const float4 v4 = reinterpret_cast<const float4*>(vs + r * HD)[d4];
+        // weighted V sum: thread t takes 4 dimensions (d4) of every NGRP-th row
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const float e = sc[g * L + r];
-            acc[g].x = fmaf(e, v4.x, acc[g].x);
-            acc[g].y = fmaf(e, v4.y, acc[g].y);
-            acc[g].z = fmaf(e, v4.z, acc[g].z);
-            acc[g].w = fmaf(e, v4.w, acc[g].w);
+            const float al = alpha[g];
+            acc[g].x *= al;
+            acc[g].y *= al;
+            acc[g].z *= al;
+            acc[g].w *= al;
         }
+        for (int r = grp; r < rows; r += NGRP) {
+            const float4 v4 = reinterpret_cast<const float4*>(vs + r * HD)[d4];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float e = es[g * kChunk + r];
+                acc[g].x = fmaf(e, v4.x, acc[g].x);
+                acc[g].y = fmaf(e, v4.y, acc[g].y);
+                acc[g].z = fmaf(e, v4.z, acc[g].z);
+                acc[g].w = fmaf(e, v4.w, acc[g].w);
+            }
+        }
+        __syncthreads();  // buffer c & 1 is refilled by the next iteration's copies
     }
-    float4* red = reinterpret_cast<float4*>(ks);  // [NGRP][G][C4] over K (and V): no longer read
-    __syncthreads();
+
+    // add the NGRP group sums in group order
+    float4* red = reinterpret_cast<float4*>(sm);  // [NGRP][G][C4] over buffer 0
 #pragma unroll
     for (int g = 0; g < G; ++g) red[(grp * G + g) * C4 + d4] = acc[g];
     __syncthreads();
@@ -181,34 +226,60 @@ attn_split(const AttnArgs a) {
         }
         const int64_t row = (int64_t)m * a.n_head + h0 + g;
         if (S_m == 1) {
-            const float inv = 1.f / st[2 * g + 1];
+            const float inv = 1.f / lrun[g];
             reinterpret_cast<float4*>(a.out + row * HD)[c] =
                 make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
         } else {
             reinterpret_cast<float4*>(a.part + (row * a.S + s) * HD)[c] = v;
-            if (c == 0) a.stat[row * a.S + s] = make_float2(st[2 * g], st[2 * g + 1]);
+            if (c == 0) a.stat[row * a.S + s] = make_float2(mrun[g], lrun[g]);
         }
     }
 }
 
-// Rows with more than one split: combine the splits in split order.
+// Rows with more than one split: combine the splits in split order.  The
+// split weights exp(max_s - max) go to shared memory once; thread (d, sg)
+// sums the splits s = sg, sg + SG, ... of dimension d, and the SG partial
+// sums are added in sg order (deterministic).
 __global__ void __launch_bounds__(256)
 attn_combine(const AttnArgs a, int HD) {
+    extern __shared__ float wsm[];  // [S] split weights, then [SG][HD] partial sums
+    __shared__ float red[32];
     const int h = blockIdx.x, m = blockIdx.y;
     const int64_t len = a.base + m + 1;
     const int S_m = (int)((len + a.L - 1) / a.L);
     if (S_m == 1) return;  // finished by the split kernel
     const int64_t row = (int64_t)m * a.n_head + h;
     const float2* st = a.stat + row * a.S;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
     float mx = -INFINITY;
-    for (int s = 0; s < S_m; ++s) mx = fmaxf(mx, st[s].x);
-    float tot = 0.f;
-    for (int s = 0; s < S_m; ++s) tot += st[s].y * expf(st[s].x - mx);
-    const float inv = 1.f / tot;
-    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-        float v = 0.f;
-        for (int s = 0; s < S_m; ++s) v += a.part[(row * a.S + s) * HD + d] * expf(st[s].x - mx);
-        a.out[row * HD + d] = v * inv;
+    for (int s = t; s < S_m; s += blockDim.x) mx = fmaxf(mx, st[s].x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < nw; ++w) mx = fmaxf(mx, red[w]);
+    for (int s = t; s < S_m; s += blockDim.x) wsm[s] = expf(st[s].x - mx);
+    __syncthreads();
+    if (t == 0) {
+        float tot = 0.f;
+        for (int s = 0; s < S_m; ++s) tot += st[s].y * wsm[s];
+        red[0] = tot;  // every thread has read red[] above
+    }
+    const int SG = (int)blockDim.x / HD;
+    const int d = t % HD, sg = t / HD;
+    float v = 0.f;
+    if (sg < SG) {
+#pragma unroll 8
+        for (int s = sg; s < S_m; s += SG) v = fmaf(a.part[(row * a.S + s) * HD + d], wsm[s], v);
+    }
+    float* psum = wsm + a.S;
+    if (sg < SG) psum[sg * HD + d] = v;
+    __syncthreads();
+    if (sg == 0) {
+        float o = psum[d];
+        for (int k = 1; k < SG; ++k) o += psum[k * HD + d];
+        a.out[row * HD + d] = o / red[0];
     }
 }
 
@@ -237,28 +308,54 @@ struct AttnPlan {
     int G, L, S;
 };
 
-// Query heads per CTA (a power of two dividing gqa, at most 8) and the split
-// length: 64 positions, or 32 when the launch would otherwise leave SMs idle.
-AttnPlan attn_plan(int64_t M, int64_t n_head_kv, int64_t gqa, int64_t base) {
+// two chunk buffers, q, the chunk's exponentials, three floats per head
+size_t attn_smem(int HD, int G) {
+    return (size_t)(2 * kChunk * (2 * HD + 4) + G * HD + G * kChunk + 3 * G) * sizeof(float);
+}
+
+template <int HD, int G>
+int resident_ctas() {
+    int n = 0;
+    const size_t smem = attn_smem(HD, G);
+    const int rc = opt_in_smem(reinterpret_cast<const void*>(attn_split<HD, G>), (int)smem,
+                               "cudaFuncSetAttribute(attn_split)");
+    if (rc) return 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_split<HD, G>, kAttnThreads, smem) !=
+            cudaSuccess ||
+        n < 1)
+        return 1;
+    return n;
+}
+
+template <int HD>
+int resident_ctas_g(int G) {
+    return G == 8 ? resident_ctas<HD, 8>() : G == 4 ? resident_ctas<HD, 4>()
+         : G == 2 ? resident_ctas<HD, 2>() : resident_ctas<HD, 1>();
+}
+
+// Query heads per CTA (a power of two dividing gqa, at most 8) and the
+// split length L, a whole number of 32-position chunks: the longest row's
+// chunks shared out over as many splits as fit one wave of resident CTAs
+// (a CTA per SM slot), so every CTA of a decode launch runs at once.
+AttnPlan attn_plan(int64_t M, int64_t n_head_kv, int64_t gqa, int64_t base, int64_t head_dim) {
     AttnPlan p;
     p.G = gqa % 8 == 0 ? 8 : gqa % 4 == 0 ? 4 : gqa % 2 == 0 ? 2 : 1;
+    const int res = head_dim == 64 ? resident_ctas_g<64>(p.G)
+                  : head_dim == 128 ? resident_ctas_g<128>(p.G) : resident_ctas_g<256>(p.G);
     const int64_t ctas_per_split = n_head_kv * (gqa / p.G) * M;
     const int64_t len_max = base + M;
-    p.L = ctas_per_split * ((len_max + 63) / 64) < 2 * (int64_t)device_sms() ? 32 : 64;
+    const int64_t chunks = (len_max + kChunk - 1) / kChunk;
+    const int64_t slots = (int64_t)res * device_sms();
+    const int64_t splits = std::max<int64_t>(1, std::min<int64_t>(chunks, slots / ctas_per_split));
+    const int64_t per = (chunks + splits - 1) / splits;  // chunks per split
+    p.L = (int)(per * kChunk);
     p.S = (int)((len_max + p.L - 1) / p.L);
     return p;
 }
 
-// The V-sum reduction ([512 / HD groups][G][HD] floats) reuses the K and V
-// areas (L (2 HD + 4) floats), which it fits for every HD, G <= 8, L >= 32.
-size_t attn_smem(int HD, int G, int L) {
-    return (size_t)(L * (HD + 4) + L * HD + G * HD + G * L + 2 * G) * sizeof(float);
-}
-static_assert(512 * 8 <= 32 * (2 * 64 + 4), "V-sum reduction fits the K and V areas");
-
 template <int HD, int G>
 int launch_split(const AttnArgs& a, int64_t M, int64_t n_head_kv, cudaStream_t st) {
-    const size_t smem = attn_smem(HD, G, a.L);
+    const size_t smem = attn_smem(HD, G);
     const int rc = opt_in_smem(reinterpret_cast<const void*>(attn_split<HD, G>), (int)smem,
                                "cudaFuncSetAttribute(attn_split)");
     if (rc) return rc;
@@ -297,7 +394,7 @@ size_t attention_workspace_bytes(int64_t M, int64_t n_head, int64_t n_head_kv, i
                                  int64_t base) {
     if (attention_check(M, n_head, n_head_kv, head_dim, base, "ftc_attention_workspace_bytes"))
         return 0;
-    const AttnPlan p = attn_plan(M, n_head_kv, n_head / n_head_kv, base);
+    const AttnPlan p = attn_plan(M, n_head_kv, n_head / n_head_kv, base, head_dim);
     if (p.S == 1) return 0;
     // split statistics (float2 each), padded to 16 bytes, then the split sums
     const size_t stats = ((size_t)(M * n_head) * (size_t)p.S * sizeof(float2) + 15) & ~size_t(15);
@@ -318,7 +415,7 @@ int attention(const float* q, int64_t M, int64_t n_head, int64_t n_head_kv, int6
     FTC_REQUIRE(a16(q) && a16(out) && a16(k_cache) && a16(v_cache) && a16(k_blk) && a16(v_blk),
                 FTC_E_INVALID, "ftc_attention: buffers must be 16-byte aligned");
     const int64_t gqa = n_head / n_head_kv;
-    const AttnPlan p = attn_plan(M, n_head_kv, gqa, base);
+    const AttnPlan p = attn_plan(M, n_head_kv, gqa, base, head_dim);
     const size_t need = attention_workspace_bytes(M, n_head, n_head_kv, head_dim, base);
     FTC_REQUIRE(ws_bytes >= need && (need == 0 || (ws && a16(ws))), FTC_E_INVALID,
                 "ftc_attention: workspace smaller than ftc_attention_workspace_bytes");
@@ -344,8 +441,8 @@ int attention(const float* q, int64_t M, int64_t n_head, int64_t n_head_kv, int6
     else rc = launch_split_g<256>(p.G, a, M, n_head_kv, st);
     if (rc) return rc;
     if (p.S > 1) {
-        attn_combine<<<dim3((unsigned)n_head, (unsigned)M), (unsigned)std::min<int64_t>(head_dim, 256),
-                       0, st>>>(a, (int)head_dim);
+        const size_t csm = (size_t)(p.S + 256) * sizeof(float);  // split weights + partial sums
+        attn_combine<<<dim3((unsigned)n_head, (unsigned)M), 256, csm, st>>>(a, (int)head_dim);
         FTC_CUDA(cudaGetLastError());
     }
     return FTC_OK;
