@@ -332,6 +332,56 @@ static void test_gguf_model(CudaBackend& be, const char* path) {
     for (const auto& kv : model.tensors()) be.evict(kv.second);
 }
 
+// ft::CudaBackend::kv_alloc + attention as the engine's layer loop uses them
+// (ft/src/engine.cpp:553-566): a prefill block written into the device cache,
+// decode steps after it, and a look-ahead call without write_kv; each output
+// against the oracle's restatement of Engine::Impl::attn over the same rows.
+static void test_attention(CudaBackend& be) {
+    const int64_t nh = 16, nkv = 4, hd = 64, dk = nkv * hd, layers = 2, cap = 96;
+    be.kv_alloc(layers, cap, dk);
+    std::vector<std::vector<float>> kc(layers), vc(layers);
+    int64_t base = 0;
+    for (int64_t M : {9, 1, 1, 4}) {
+        for (int64_t l = 0; l < layers; ++l) {
+            for (int pass = 0; pass < 2; ++pass) {  // pass 0: look-ahead, not written
+                const bool write = pass == 1;
+                const int64_t rows = write ? M : 1;
+                std::vector<float> q((size_t)(rows * nh * hd)), k((size_t)(rows * dk)),
+                    v((size_t)(rows * dk)), out(q.size()), ref(q.size());
+                for (auto& x : q) x = rnd();
+                for (auto& x : k) x = rnd();
+                for (auto& x : v) x = rnd();
+                be.attention(l, base, rows, nh, nkv, hd, q.data(), k.data(), v.data(), write,
+                             out.data());
+                const float* kp = kc[l].empty() ? k.data() : kc[l].data();
+                const float* vp = vc[l].empty() ? v.data() : vc[l].data();
+                CHECK(ftor_attention(q.data(), rows, nh, nkv, hd, kp, vp, base, k.data(),
+                                     v.data(), ref.data(), 4) == 0,
+                      "oracle attention");
+                double num = 0, den = 0;
+                for (size_t i = 0; i < out.size(); ++i) {
+                    num += (double)(out[i] - ref[i]) * (out[i] - ref[i]);
+                    den += (double)ref[i] * ref[i];
+                }
+                CHECK(std::sqrt(num / den) < 5e-5, "attention vs oracle (normwise)");
+                if (write) {
+                    kc[l].insert(kc[l].end(), k.begin(), k.end());
+                    vc[l].insert(vc[l].end(), v.begin(), v.end());
+                }
+            }
+        }
+        base += M;
+    }
+    bool threw = false;
+    try {  // beyond the cache's capacity
+        std::vector<float> q((size_t)(nh * hd)), k((size_t)dk), v((size_t)dk), o(q.size());
+        be.attention(0, cap, 1, nh, nkv, hd, q.data(), k.data(), v.data(), true, o.data());
+    } catch (const std::runtime_error&) {
+        threw = true;
+    }
+    CHECK(threw, "attention past the capacity throws");
+}
+
 int main(int argc, char** argv) {
     test_down_layout();
     const char* mode = argc > 1 ? argv[1] : "";
@@ -339,6 +389,22 @@ int main(int argc, char** argv) {
         try {
             CudaBackend be(0);
             test_gguf_model(be, argv[2]);
+            be.sync();
+        } catch (const std::exception& e) {
+            std::printf("FAIL exception: %s\n", e.what());
+            ++g_fails;
+        }
+        if (g_fails) {
+            std::printf("%d checks FAILED\n", g_fails);
+            return 1;
+        }
+        std::printf("all tests passed\n");
+        return 0;
+    }
+    if (std::strcmp(mode, "--attention") == 0) {
+        try {
+            CudaBackend be(0);
+            test_attention(be);
             be.sync();
         } catch (const std::exception& e) {
             std::printf("FAIL exception: %s\n", e.what());

@@ -118,6 +118,18 @@ bool CudaBackend::moe_ffn(const float* xn, const float* router, const std::vecto
     return true;
 }
 
+void CudaBackend::kv_alloc(int64_t n_layers, int64_t capacity, int64_t dim) {
+    check(ftc_backend_kv_alloc(be_, n_layers, capacity, dim), "kv_alloc");
+}
+
+void CudaBackend::attention(int64_t layer, int64_t base, int64_t M, int64_t n_head,
+                            int64_t n_head_kv, int64_t head_dim, const float* q, const float* k,
+                            const float* v, bool write_kv, float* attout) {
+    check(ftc_backend_attention(be_, layer, base, M, n_head, n_head_kv, head_dim, q, k, v,
+                                write_kv ? 1 : 0, attout),
+          "attention");
+}
+
 void CudaBackend::upload(const HostTensor& t) {
     const size_t n = t.nbytes ? t.nbytes
                               : t.slice_bytes() * (size_t)t.ne[2] * (size_t)t.ne[3];

@@ -81,6 +81,19 @@ public:
     static bool moe_supported(const HostTensor& gexps, const HostTensor& uexps,
                               const HostTensor& dexps);
 
+    // The engine's KV cache in HBM (ft::KvCache::alloc, ft/include/ft/
+    // kv_cache.h:12-20): n_layers x capacity rows of dim floats for K and V.
+    void kv_alloc(int64_t n_layers, int64_t capacity, int64_t dim);
+    // One layer of the engine's attention step (ft/src/engine.cpp:553-566):
+    // with write_kv the block's k / v rows ([M][n_head_kv * head_dim], after
+    // RoPE) are stored into the device cache at rows [base, base + M), then
+    // Engine::Impl::attn's causal grouped-query attention of q ([M][n_head *
+    // head_dim], after RoPE) over rows [0, base + M) writes attout.  Host
+    // buffers, synchronous; head_dim 64, 128 or 256.
+    void attention(int64_t layer, int64_t base, int64_t M, int64_t n_head, int64_t n_head_kv,
+                   int64_t head_dim, const float* q, const float* k, const float* v,
+                   bool write_kv, float* attout);
+
     // Load a tensor's blocks into HBM once (call at Engine::load time).  The
     // host blocks must stay mapped and unchanged until evict() or the
     // backend's destruction; tensors never uploaded are copied per call.
