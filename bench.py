@@ -1165,6 +1165,27 @@ def run_ncu_gemm_probe():
     return 0
 
 
+def run_ncu_attention_probe():
+    """Three ftc_attention launches (split kernel + combine each): one decode
+    row of Llama-3-8B heads over 32768 positions, K and V 134 MB each on the
+    device: the case for ncu captures of attn_split."""
+    import torch
+    from xwfes_b200 import ftc
+    dev = torch.device("cuda", 0)
+    nh, nkv, hd, n = 32, 8, 128, 32768
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    k = torch.randn((n, nkv * hd), device=dev, generator=g)
+    v = torch.randn((n, nkv * hd), device=dev, generator=g)
+    q = torch.randn((1, nh * hd), device=dev, generator=g)
+    for _ in range(3):
+        ftc.attention(q, nh, nkv, hd, k[n - 1:], v[n - 1:], base=n - 1, k_cache=k, v_cache=v)
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": "attn_split 32 q / 8 kv heads x 128, 32768 positions x3",
+                      "status": ftc.device_status()}))
+    return 0
+
+
 def run_ncu_gemm_split_probe():
     """Three dequant-GEMM launches on a tensor-parallel rank's shape (the
     stacked q/k/v shard of config 4 at 8 GPUs: 1280 x 8192 Q4_K, 16 tokens,
@@ -1383,7 +1404,10 @@ def main():
                          "q/k/v shard (1280x8192, M=16), no timing")
     ap.add_argument("--ncu-gemm", action="store_true",
                     help="profiling mode: three launches of the config-3 dequant-GEMM "
-                         "(14336x4096, M=2048, bf16), no timing")
+                         "(14336x4096, M=8192, bf16), no timing")
+    ap.add_argument("--ncu-attention", action="store_true",
+                    help="profiling mode: three ftc_attention launches, one decode row over a "
+                         "32768-position fp32 KV cache (Llama-3-8B heads), no timing")
     ap.add_argument("--down-axpy", action="store_true",
                     help="time the neuron-major down projection (ftc_matmul_down_axpy) alone "
                          "and print one JSON line; also the case for ncu captures of rows_axpy")
@@ -1402,6 +1426,8 @@ def main():
         return run_ncu_gemm_probe()
     if args.ncu_gemm_split:
         return run_ncu_gemm_split_probe()
+    if args.ncu_attention:
+        return run_ncu_attention_probe()
     if args.down_axpy:
         return run_down_axpy()
 
