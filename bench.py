@@ -827,6 +827,14 @@ def time_attention(dev, reps=50):
                    "kind": "reference (Engine::Impl::attn compiled from its sources)"}
     except Exception as e:  # the checker library is optional on a box
         ref = {"error": str(e)[:200]}
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "attention_decode_32k.md")
+    if os.path.exists(prof):
+        for ln in open(prof):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                traffic = int(ln.split(":", 1)[1].strip())
+    if "32768" in out:
+        out["32768"]["traffic"] = traffic  # ncu dram bytes of one split launch at this size
     return {"workload": "Llama-3-8B attention heads (32 q, 8 kv, head_dim 128), one decode row, "
                         "fp32 KV cache",
             "api": "ftc_attention (split positions, cp.async K/V staging, split combine)",
