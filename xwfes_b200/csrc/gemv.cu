@@ -371,6 +371,8 @@ int launch_staged(const uint8_t* W, int64_t stride, int N, int nblk, const float
 
 int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
                   float* y, cudaStream_t st);
+int gemv_q6k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
+                  float* y, cudaStream_t st);
 int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y,
                         int64_t stride, int64_t K, const float* x, cudaStream_t st, int n_next,
                         const uint8_t* const* next_w, const int64_t* next_bytes);
@@ -401,6 +403,10 @@ int launch_m(int dtype, const uint8_t* W, int64_t stride, int N, int64_t K, cons
              float* y, cudaStream_t st) {
     if (M == 1 && dtype == FTC_Q4_K) {
         const int rc = gemv_q4k_fast(W, stride, N, K, x, y, st);
+        if (rc != FTC_E_UNSUPPORTED) return rc;
+    }
+    if (M == 1 && dtype == FTC_Q6_K) {
+        const int rc = gemv_q6k_fast(W, stride, N, K, x, y, st);
         if (rc != FTC_E_UNSUPPORTED) return rc;
     }
     if (M > 1 && dtype == FTC_Q4_K) {

@@ -63,6 +63,9 @@ struct GemvSpec {
     // silu_gate(gate[k], up[k]) -- the SiLU product folded into the
     // activation load, bit for bit what a separate silu kernel would give.
     int64_t x_up;
+    // 1: the weights are Q6_K super-blocks (210 bytes, one matrix per x,
+    // no allreduce, no SiLU activation); 0: Q4_K.
+    int q6k;
 };
 
 constexpr int64_t kGemvPrefetchWindow = 24ll << 20;

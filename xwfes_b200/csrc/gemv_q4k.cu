@@ -228,6 +228,75 @@ __device__ __forceinline__ float q4k_row_partial(const uint8_t* blk, int t, uint
     return X.scale * fmaf(-dmin, um, d * sq);
 }
 
+// d = a (signed bytes) . b (unsigned bytes) + c
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// N words of the bytes at p, which is only 2-byte aligned (Q6_K super-blocks
+// are 210 bytes): N + 1 aligned shared-memory words and a funnel shift.
+template <int N>
+__device__ __forceinline__ void lds_words_a2(const uint8_t* p, uint32_t (&w)[N]) {
+    const uint32_t* a =
+        reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(reinterpret_cast<uintptr_t>(p) & 3) * 8;
+    uint32_t prev = a[0];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const uint32_t nx = a[i + 1];
+        w[i] = __funnelshift_r(prev, nx, sh);
+        prev = nx;
+    }
+}
+
+// One Q6_K row: this lane's 64 weights [64t, 64t + 64) of the super-block
+// against its activations (the same x range as a Q4_K lane).  Q6_K keeps
+// 256 weights as two halves of 128 (ql 64 bytes, qh 32, then 16 int8 scales
+// and d): in half h, weight 32q + l (quad q, l < 32) is
+//   q6 = (ql[l + 32 (q & 1)] nibble q >> 1) | (qh[l] bits 2q, 2q + 1) << 4,
+// value d * scale[8h + 2q + l / 16] * (q6 - 32).  Lane t takes half t >> 1,
+// quads 2 (t & 1) and 2 (t & 1) + 1.  q6 - 32 is formed per byte as a signed
+// byte: (q6 ^ 32) read as a 6-bit two's complement number, sign-extended
+// (+ 0xC0 where bit 5 is set; no carry leaves a byte), so three dp4a per
+// four weights give exact integer sums per activation digit plane; each
+// 16-weight group's sums are multiplied by its scale in int32 (|.| < 2^27).
+__device__ __forceinline__ float q6k_row_partial(const uint8_t* blk, int t, const LaneX& X) {
+    const int h = t >> 1, qq = t & 1;
+    uint32_t ql[16], qh[8], scw[1];
+    lds_words_a2<16>(blk + 64 * h, ql);
+    lds_words_a2<8>(blk + 128 + 32 * h, qh);
+    lds_words_a2<1>(blk + 192 + 8 * h + 4 * qq, scw);
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
+    const int sh_lo = 4 * qq;
+    int ph = 0, pm = 0, pl = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {      // quad 2qq + j: ql bytes 32j.., qh bits 4qq + 2j
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {  // 16-weight group: scale byte 2j + g of the lane's 4
+            int sh = 0, sm = 0, sl = 0;
+#pragma unroll
+            for (int uu = 0; uu < 4; ++uu) {
+                const int u = 4 * g + uu;  // weights 4u .. 4u + 3 of the quad
+                const uint32_t lo = (ql[8 * j + u] >> sh_lo) & 0x0F0F0F0Fu;
+                const uint32_t hx = ((qh[u] >> (sh_lo + 2 * j)) & 0x03030303u) ^ 0x02020202u;
+                const uint32_t s6 = lo + hx * 16u;                  // q6 ^ 32
+                const uint32_t q = s6 + (s6 & 0x20202020u) * 6u;   // q6 - 32, signed bytes
+                sh = __dp4a((int)q, (int)X.h[8 * j + u], sh);
+                sm = dp4a_su(q, X.m[8 * j + u], sm);
+                sl = dp4a_su(q, X.l[8 * j + u], sl);
+            }
+            const int sc = (int)(int8_t)(uint8_t)(scw[0] >> (8 * (2 * j + g)));
+            ph += sc * sh;
+            pm += sc * sm;
+            pl += sc * sl;
+        }
+    }
+    const float sq = fmaf(65536.f, (float)ph, fmaf(256.f, (float)pm, (float)pl));
+    return X.scale * (d * sq);
+}
+
 // Sum each of R per-lane values over the warp.  Halving steps exchange half
 // of the values with the partner lane (xor 1, 2, ...), so after log2(R)
 // steps each lane holds one row; the remaining steps are a plain butterfly.
@@ -368,7 +437,7 @@ __device__ __noinline__ void fused_allreduce_tail(const GemvBatch& B, const Chun
     if (threadIdx.x == 0) peer_call_done(P.ctr, epoch);
 }
 
-template <int RPW, bool kSilu>
+template <int RPW, bool kSilu, bool kQ6 = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int WK, int WR,
               int RC) {
@@ -531,14 +600,15 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
         if (!mbar_wait_warp(&full[s], (it / kStages) & 1)) break;
         const int p = chunk_matrix(B, c);
         const int rows = min(RC, B.N[p] - (c - B.first_chunk[p]) * RC);
-        const uint8_t* base = stg + s * stage_bytes + sb_ld * 144 + wr * stride;
+        const uint8_t* base = stg + s * stage_bytes + sb_ld * (kQ6 ? 210 : 144) + wr * stride;
         float acc[RPW];
 #pragma unroll
         for (int i = 0; i < RPW; ++i) {
             acc[i] = 0.f;
             if (wr + WR * i < rows) {
-                const float v = q4k_row_partial(base + (WR * i) * stride, t, use_s2, sh0, mask_a,
-                                                mask_b, X);
+                const float v = kQ6 ? q6k_row_partial(base + (WR * i) * stride, t, X)
+                                    : q4k_row_partial(base + (WR * i) * stride, t, use_s2, sh0,
+                                                      mask_a, mask_b, X);
                 acc[i] = valid ? v : 0.f;
             }
         }
@@ -628,6 +698,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     if (g.peer && (P != 1 || g.per_matrix_x || g.sel || g.N[0] > g.peer->max_elems))
         return FTC_E_UNSUPPORTED;
     if (g.x_up < 0 || g.x_up % 4) return FTC_E_UNSUPPORTED;  // up half 16-byte aligned
+    if (g.q6k && (g.peer || g.x_up || g.sel || g.per_matrix_x)) return FTC_E_UNSUPPORTED;
     Q4kPlan p;
     if (!plan_q4k(ntot, g.K, g.stride, p)) return FTC_E_UNSUPPORTED;
     const int sms = device_sms();
@@ -709,7 +780,11 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
         return FTC_OK;
     };
     int rc;
-    if (g.x_up == 0)
+    if (g.q6k)
+        rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, false, true>, 8)
+           : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, false, true>, 7)
+                        : launch(gemv_q4k_dp4a<1, false, true>, 6);
+    else if (g.x_up == 0)
         rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, false>, 2)
            : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, false>, 1)
                         : launch(gemv_q4k_dp4a<1, false>, 0);
@@ -750,6 +825,22 @@ int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float*
 int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
                   float* y, cudaStream_t st) {
     return gemv_q4k_fast_multi(1, &W, &N, &y, stride, K, x, st);
+}
+
+// The same persistent kernel on Q6_K rows (batch 1): the config-2 output
+// head.  FTC_E_UNSUPPORTED when the shape or alignment does not fit.
+int gemv_q6k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
+                  float* y, cudaStream_t st) {
+    GemvSpec g = {};
+    g.P = 1;
+    g.K = K;
+    g.stride = stride;
+    g.x[0] = x;
+    g.W[0] = W;
+    g.N[0] = N;
+    g.y[0] = y;
+    g.q6k = 1;
+    return gemv_q4k_batch(g, st);
 }
 
 }  // namespace ftc
