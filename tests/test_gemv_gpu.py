@@ -120,29 +120,33 @@ def test_q4_k_batch1_one_hot_exact(ftc, oracle, k):
         assert np.array_equal(y, deq[:, kk]), f"k={kk}"
 
 
-@pytest.mark.parametrize("k", [4096, 2048, 6144])
-def test_q6_k_batch1_one_hot_exact(ftc, oracle, k):
-    """Batch-1 Q6_K takes the same dp4a kernel (signed 6-bit codes, int8
-    scales per 16 weights): one-hot inputs give the dequantized column
-    exactly, every position of a super-block and both halves."""
+@pytest.mark.parametrize("t,k", [(F.Q6_K, 4096), (F.Q6_K, 2048), (F.Q6_K, 6144),
+                                 (F.Q8_0, 4096), (F.Q8_0, 2048), (F.Q8_0, 6144)])
+def test_kq_batch1_one_hot_exact(ftc, oracle, t, k):
+    """Batch-1 Q6_K and Q8_0 take the same dp4a kernel (signed codes as bytes;
+    Q6_K's int8 scales per 16 weights, Q8_0's fp16 scale per 32): one-hot
+    inputs give the dequantized column exactly, every position of a 256-weight
+    stretch included."""
     n = 40
-    w = S.weight(F.Q6_K, n, k, seed=16)
-    deq = oracle.dequant_rows(w, F.Q6_K, k)
+    w = S.weight(t, n, k, seed=16)
+    deq = oracle.dequant_rows(w, t, k)
     rng = np.random.default_rng(2)
     for kk in np.concatenate([np.arange(0, 256, 5), rng.integers(0, k, 12)]):
         x = np.zeros((1, k), dtype=np.float32)
         x[0, kk] = 1.0
-        y = run_gemv(ftc, w, F.Q6_K, n, k, x)[0]
+        y = run_gemv(ftc, w, t, n, k, x)[0]
         assert np.array_equal(y, deq[:, kk]), f"k={kk}"
 
 
+@pytest.mark.parametrize("t", [F.Q6_K, F.Q8_0])
 @pytest.mark.parametrize("n", [1, 7, 13, 300, 4099])
-def test_q6_k_batch1_row_counts(ftc, oracle, n):
-    """Row counts that leave partial chunks and idle CTAs, Q6_K batch 1."""
+def test_kq_batch1_row_counts(ftc, oracle, t, n):
+    """Row counts that leave partial chunks and idle CTAs, Q6_K and Q8_0 at
+    batch 1."""
     k = 4096
-    w = S.weight(F.Q6_K, n, k, seed=18)
+    w = S.weight(t, n, k, seed=18)
     x = S.activations_f32(1, k, seed=18) * np.float32(3.0)
-    assert rel_err(run_gemv(ftc, w, F.Q6_K, n, k, x), oracle.matmul(x, w, F.Q6_K, k)) <= TOL
+    assert rel_err(run_gemv(ftc, w, t, n, k, x), oracle.matmul(x, w, t, k)) <= TOL
     assert ftc.device_status() == 0
 
 

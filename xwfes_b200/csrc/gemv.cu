@@ -371,8 +371,8 @@ int launch_staged(const uint8_t* W, int64_t stride, int N, int nblk, const float
 
 int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
                   float* y, cudaStream_t st);
-int gemv_q6k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
-                  float* y, cudaStream_t st);
+int gemv_kq_fast(int wfmt, const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
+                 float* y, cudaStream_t st);
 int gemv_q4k_fast_multi(int P, const uint8_t* const* W, const int64_t* N, float* const* y,
                         int64_t stride, int64_t K, const float* x, cudaStream_t st, int n_next,
                         const uint8_t* const* next_w, const int64_t* next_bytes);
@@ -405,8 +405,9 @@ int launch_m(int dtype, const uint8_t* W, int64_t stride, int N, int64_t K, cons
         const int rc = gemv_q4k_fast(W, stride, N, K, x, y, st);
         if (rc != FTC_E_UNSUPPORTED) return rc;
     }
-    if (M == 1 && dtype == FTC_Q6_K) {
-        const int rc = gemv_q6k_fast(W, stride, N, K, x, y, st);
+    if (M == 1 && (dtype == FTC_Q6_K || dtype == FTC_Q8_0)) {
+        const int rc = gemv_kq_fast(dtype == FTC_Q6_K ? kGemvQ6K : kGemvQ80, W, stride, N, K, x,
+                                    y, st);
         if (rc != FTC_E_UNSUPPORTED) return rc;
     }
     if (M > 1 && dtype == FTC_Q4_K) {

@@ -63,10 +63,14 @@ struct GemvSpec {
     // silu_gate(gate[k], up[k]) -- the SiLU product folded into the
     // activation load, bit for bit what a separate silu kernel would give.
     int64_t x_up;
-    // 1: the weights are Q6_K super-blocks (210 bytes, one matrix per x,
-    // no allreduce, no SiLU activation); 0: Q4_K.
-    int q6k;
+    // Weight format: 0 Q4_K; kGemvQ6K / kGemvQ80: Q6_K super-blocks (210
+    // bytes) / Q8_0 blocks (34 bytes), one matrix per x, no allreduce, no
+    // SiLU activation, no expert selection.
+    int wfmt;
 };
+
+constexpr int kGemvQ6K = 1;
+constexpr int kGemvQ80 = 2;
 
 constexpr int64_t kGemvPrefetchWindow = 24ll << 20;
 

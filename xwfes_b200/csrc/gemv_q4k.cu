@@ -297,6 +297,30 @@ __device__ __forceinline__ float q6k_row_partial(const uint8_t* blk, int t, cons
     return X.scale * (d * sq);
 }
 
+// One Q8_0 row stretch of 256 weights (8 blocks of 34 bytes: fp16 d, 32
+// int8 codes): lane t takes blocks 2t and 2t + 1, weights [64t, 64t + 64)
+// (the same x range as a Q4_K lane).  The codes are signed bytes already:
+// three dp4a per four weights, exact per block; d applied per block.
+__device__ __forceinline__ float q80_row_partial(const uint8_t* unit, int t, const LaneX& X) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const uint8_t* blk = unit + 34 * (2 * t + j);
+        uint32_t q[8];
+        lds_words_a2<8>(blk + 2, q);
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
+        int sh = 0, sm = 0, sl = 0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            sh = __dp4a((int)q[u], (int)X.h[8 * j + u], sh);
+            sm = dp4a_su(q[u], X.m[8 * j + u], sm);
+            sl = dp4a_su(q[u], X.l[8 * j + u], sl);
+        }
+        acc = fmaf(d, fmaf(65536.f, (float)sh, fmaf(256.f, (float)sm, (float)sl)), acc);
+    }
+    return X.scale * acc;
+}
+
 // Sum each of R per-lane values over the warp.  Halving steps exchange half
 // of the values with the partner lane (xor 1, 2, ...), so after log2(R)
 // steps each lane holds one row; the remaining steps are a plain butterfly.
@@ -437,7 +461,7 @@ __device__ __noinline__ void fused_allreduce_tail(const GemvBatch& B, const Chun
     if (threadIdx.x == 0) peer_call_done(P.ctr, epoch);
 }
 
-template <int RPW, bool kSilu, bool kQ6 = false>
+template <int RPW, bool kSilu, int kFmt = 0>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int WK, int WR,
               int RC) {
@@ -600,15 +624,19 @@ gemv_q4k_dp4a(const __grid_constant__ GemvBatch B, int64_t stride, int nsb, int 
         if (!mbar_wait_warp(&full[s], (it / kStages) & 1)) break;
         const int p = chunk_matrix(B, c);
         const int rows = min(RC, B.N[p] - (c - B.first_chunk[p]) * RC);
-        const uint8_t* base = stg + s * stage_bytes + sb_ld * (kQ6 ? 210 : 144) + wr * stride;
+        // bytes per 256 weights: Q4_K 144, Q6_K 210, Q8_0 8 x 34
+        constexpr int kUnit = kFmt == kGemvQ6K ? 210 : kFmt == kGemvQ80 ? 272 : 144;
+        const uint8_t* base = stg + s * stage_bytes + sb_ld * kUnit + wr * stride;
         float acc[RPW];
 #pragma unroll
         for (int i = 0; i < RPW; ++i) {
             acc[i] = 0.f;
             if (wr + WR * i < rows) {
-                const float v = kQ6 ? q6k_row_partial(base + (WR * i) * stride, t, X)
-                                    : q4k_row_partial(base + (WR * i) * stride, t, use_s2, sh0,
-                                                      mask_a, mask_b, X);
+                const uint8_t* rb = base + (WR * i) * stride;
+                const float v = kFmt == kGemvQ6K ? q6k_row_partial(rb, t, X)
+                              : kFmt == kGemvQ80 ? q80_row_partial(rb, t, X)
+                                                 : q4k_row_partial(rb, t, use_s2, sh0, mask_a,
+                                                                   mask_b, X);
                 acc[i] = valid ? v : 0.f;
             }
         }
@@ -698,7 +726,7 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
     if (g.peer && (P != 1 || g.per_matrix_x || g.sel || g.N[0] > g.peer->max_elems))
         return FTC_E_UNSUPPORTED;
     if (g.x_up < 0 || g.x_up % 4) return FTC_E_UNSUPPORTED;  // up half 16-byte aligned
-    if (g.q6k && (g.peer || g.x_up || g.sel || g.per_matrix_x)) return FTC_E_UNSUPPORTED;
+    if (g.wfmt && (g.peer || g.x_up || g.sel || g.per_matrix_x)) return FTC_E_UNSUPPORTED;
     Q4kPlan p;
     if (!plan_q4k(ntot, g.K, g.stride, p)) return FTC_E_UNSUPPORTED;
     const int sms = device_sms();
@@ -780,10 +808,14 @@ int gemv_q4k_batch(const GemvSpec& g, cudaStream_t st) {
         return FTC_OK;
     };
     int rc;
-    if (g.q6k)
-        rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, false, true>, 8)
-           : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, false, true>, 7)
-                        : launch(gemv_q4k_dp4a<1, false, true>, 6);
+    if (g.wfmt == kGemvQ6K)
+        rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, false, kGemvQ6K>, 8)
+           : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, false, kGemvQ6K>, 7)
+                        : launch(gemv_q4k_dp4a<1, false, kGemvQ6K>, 6);
+    else if (g.wfmt == kGemvQ80)
+        rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, false, kGemvQ80>, 11)
+           : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, false, kGemvQ80>, 10)
+                        : launch(gemv_q4k_dp4a<1, false, kGemvQ80>, 9);
     else if (g.x_up == 0)
         rc = p.RPW == 4 ? launch(gemv_q4k_dp4a<4, false>, 2)
            : p.RPW == 2 ? launch(gemv_q4k_dp4a<2, false>, 1)
@@ -827,10 +859,11 @@ int gemv_q4k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const 
     return gemv_q4k_fast_multi(1, &W, &N, &y, stride, K, x, st);
 }
 
-// The same persistent kernel on Q6_K rows (batch 1): the config-2 output
-// head.  FTC_E_UNSUPPORTED when the shape or alignment does not fit.
-int gemv_q6k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
-                  float* y, cudaStream_t st) {
+// The same persistent kernel on Q6_K rows (the config-2 output head) or
+// Q8_0 rows (config 1), batch 1.  FTC_E_UNSUPPORTED when the shape or
+// alignment does not fit.
+int gemv_kq_fast(int wfmt, const uint8_t* W, int64_t stride, int64_t N, int64_t K, const float* x,
+                 float* y, cudaStream_t st) {
     GemvSpec g = {};
     g.P = 1;
     g.K = K;
@@ -839,7 +872,7 @@ int gemv_q6k_fast(const uint8_t* W, int64_t stride, int64_t N, int64_t K, const 
     g.W[0] = W;
     g.N[0] = N;
     g.y[0] = y;
-    g.q6k = 1;
+    g.wfmt = wfmt;
     return gemv_q4k_batch(g, st);
 }
 
