@@ -1173,6 +1173,24 @@ def run_ncu_gemm_probe():
     return 0
 
 
+def run_ncu_q6k_probe():
+    """Three batch-1 GEMVs of config 2's Q6_K output head (128256 x 4096,
+    431 MB on the device, larger than L2): the case for ncu captures of the
+    dp4a kernel on Q6_K rows."""
+    import torch
+    from xwfes_b200 import ftc
+    dev = torch.device("cuda", 0)
+    n, k = 128256, 4096
+    w = torch.from_numpy(S.weight(F.Q6_K, n, k, seed=0, name="q6k.head")).to(dev)
+    x = torch.from_numpy(S.activations_f32(1, k, seed=0, name="q6k.x")).to(dev)
+    y = torch.empty((1, n), dtype=torch.float32, device=dev)
+    for _ in range(3):
+        ftc.mul_mat_vec(w, F.Q6_K, n, k, x, y=y)
+    torch.cuda.synchronize()
+    print(json.dumps({"probe": "gemv_q4k_dp4a on Q6_K 128256x4096 x3", "status": ftc.device_status()}))
+    return 0
+
+
 def run_ncu_attention_probe():
     """Three ftc_attention launches (split kernel + combine each): one decode
     row of Llama-3-8B heads over 32768 positions, K and V 134 MB each on the
@@ -1413,6 +1431,9 @@ def main():
     ap.add_argument("--ncu-gemm", action="store_true",
                     help="profiling mode: three launches of the config-3 dequant-GEMM "
                          "(14336x4096, M=8192, bf16), no timing")
+    ap.add_argument("--ncu-q6k", action="store_true",
+                    help="profiling mode: three batch-1 GEMVs of config 2's Q6_K output head "
+                         "(128256x4096, 431 MB), no timing")
     ap.add_argument("--ncu-attention", action="store_true",
                     help="profiling mode: three ftc_attention launches, one decode row over a "
                          "32768-position fp32 KV cache (Llama-3-8B heads), no timing")
@@ -1436,6 +1457,8 @@ def main():
         return run_ncu_gemm_split_probe()
     if args.ncu_attention:
         return run_ncu_attention_probe()
+    if args.ncu_q6k:
+        return run_ncu_q6k_probe()
     if args.down_axpy:
         return run_down_axpy()
 

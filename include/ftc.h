@@ -493,6 +493,18 @@ int ftc_backend_attention(ftc_backend* be, int64_t layer, int64_t base, int64_t 
                           int64_t n_head_kv, int64_t head_dim, const float* q,
                           const float* k_new, const float* v_new, int write_kv, float* out);
 
+/* Rows [pos0, pos0 + n) of `layer` of the device KV cache to HOST k / v
+ * ([n][dim] fp32 each): the copies the engine's prefix cache makes when it
+ * stores a snapshot (ft/src/engine.cpp:630-645).  Synchronous. */
+int ftc_backend_kv_read(ftc_backend* be, int64_t layer, int64_t pos0, int64_t n, float* k,
+                        float* v);
+
+/* HOST k / v ([n][dim] fp32 each) into rows [pos0, pos0 + n) of `layer` of
+ * the device KV cache: the copies the engine makes when it restores a
+ * prefix-cache snapshot (ft/src/engine.cpp:608-616).  Synchronous. */
+int ftc_backend_kv_write(ftc_backend* be, int64_t layer, int64_t pos0, int64_t n, const float* k,
+                         const float* v);
+
 #ifdef __cplusplus
 }
 #endif

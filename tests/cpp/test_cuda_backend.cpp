@@ -372,6 +372,16 @@ static void test_attention(CudaBackend& be) {
         }
         base += M;
     }
+    // snapshot of layer 1 read back bit for bit, then written over and read again
+    std::vector<float> sk((size_t)(base * dk)), sv(sk.size());
+    be.kv_read(1, 0, base, sk.data(), sv.data());
+    CHECK(std::memcmp(sk.data(), kc[1].data(), sk.size() * sizeof(float)) == 0 &&
+              std::memcmp(sv.data(), vc[1].data(), sv.size() * sizeof(float)) == 0,
+          "kv_read returns the rows attention wrote");
+    be.kv_write(0, 0, base, sk.data(), sv.data());
+    std::vector<float> rk(sk.size()), rv(sk.size());
+    be.kv_read(0, 0, base, rk.data(), rv.data());
+    CHECK(rk == sk && rv == sv, "kv_write then kv_read");
     bool threw = false;
     try {  // beyond the cache's capacity
         std::vector<float> q((size_t)(nh * hd)), k((size_t)dk), v((size_t)dk), o(q.size());

@@ -44,3 +44,9 @@ def test_backend_entries_need_a_backend(lib):
     assert lib.ftc_backend_kv_alloc(None, 2, 16, 1024) != 0
     z = (C.c_float * 4)()
     assert lib.ftc_backend_attention(None, 0, 0, 1, 32, 8, 128, z, z, z, 1, z) != 0
+
+
+def test_kv_copies_need_a_backend(lib):
+    z = (C.c_float * 4)()
+    assert lib.ftc_backend_kv_read(None, 0, 0, 1, z, z) != 0
+    assert lib.ftc_backend_kv_write(None, 0, 0, 1, z, z) != 0

@@ -191,3 +191,40 @@ def test_backend_kv_cache_decode_sequence(ftc, oracle):
                          16, 4, hd)
     finally:
         be.close()
+
+
+def test_backend_kv_snapshot_and_restore(ftc, oracle):
+    """ftc_backend_kv_read / kv_write as the engine's prefix cache uses them
+    (ft/src/engine.cpp:605-645): rows written by attention calls read back
+    bit for bit, a snapshot restored into a fresh cache serves the next
+    attention call as if the prefix had been computed there."""
+    nh, nkv, hd, L = 8, 2, 128, 2
+    dk = nkv * hd
+    rng = np.random.default_rng(31)
+    a = ftc.CudaBackend(0)
+    b = ftc.CudaBackend(0)
+    try:
+        a.kv_alloc(L, 64, dk)
+        b.kv_alloc(L, 64, dk)
+        M = 20
+        ks = {l: rng.standard_normal((M, dk), dtype=np.float32) for l in range(L)}
+        vs = {l: rng.standard_normal((M, dk), dtype=np.float32) for l in range(L)}
+        for l in range(L):
+            q = rng.standard_normal((M, nh * hd), dtype=np.float32)
+            a.attention(l, 0, q, ks[l], vs[l], nh, nkv, hd, write_kv=True)
+        snap = {l: a.kv_read(l, 0, M, dk) for l in range(L)}
+        for l in range(L):
+            assert np.array_equal(snap[l][0], ks[l]) and np.array_equal(snap[l][1], vs[l])
+            b.kv_write(l, 0, *snap[l])
+        for l in range(L):
+            q = rng.standard_normal((1, nh * hd), dtype=np.float32)
+            kn = rng.standard_normal((1, dk), dtype=np.float32)
+            vn = rng.standard_normal((1, dk), dtype=np.float32)
+            got = b.attention(l, M, q, kn, vn, nh, nkv, hd, write_kv=True)
+            want = oracle.attention(q, nh, nkv, hd, ks[l], vs[l], M, kn, vn, threads=THR)
+            assert close(got, want)
+        with pytest.raises(ftc.FtcError):  # rows beyond the capacity
+            b.kv_read(0, 60, 8, dk)
+    finally:
+        a.close()
+        b.close()

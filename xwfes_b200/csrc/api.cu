@@ -629,6 +629,53 @@ int ftc_backend_attention(ftc_backend* be, int64_t layer, int64_t base, int64_t 
     return ok();
 }
 
+namespace {
+
+// rows [pos0, pos0 + n) of `layer`: K and V device pointers, or an error
+int kv_rows(ftc_backend* be, int64_t layer, int64_t pos0, int64_t n, float** k, float** v,
+            const char* who) {
+    FTC_REQUIRE(be->kv, FTC_E_INVALID, std::string(who) + ": no KV cache (ftc_backend_kv_alloc)");
+    FTC_REQUIRE(layer >= 0 && layer < be->kv_layers, FTC_E_INVALID,
+                std::string(who) + ": layer out of range");
+    FTC_REQUIRE(pos0 >= 0 && n >= 0 && pos0 + n <= be->kv_cap, FTC_E_INVALID,
+                std::string(who) + ": rows outside the cache");
+    *k = be->kv + (layer * be->kv_cap + pos0) * be->kv_dim;
+    *v = be->kv + ((be->kv_layers + layer) * be->kv_cap + pos0) * be->kv_dim;
+    return FTC_OK;
+}
+
+}  // namespace
+
+int ftc_backend_kv_read(ftc_backend* be, int64_t layer, int64_t pos0, int64_t n, float* k,
+                        float* v) {
+    int rc = bind(be);
+    if (rc) return rc;
+    FTC_REQUIRE(k && v, FTC_E_INVALID, "ftc_backend_kv_read: null pointer");
+    std::lock_guard<std::mutex> lk(be->mu);
+    float *dk, *dv;
+    if ((rc = kv_rows(be, layer, pos0, n, &dk, &dv, "ftc_backend_kv_read"))) return rc;
+    const size_t bytes = (size_t)(n * be->kv_dim) * sizeof(float);
+    FTC_CUDA(cudaMemcpyAsync(k, dk, bytes, cudaMemcpyDeviceToHost, be->stream));
+    FTC_CUDA(cudaMemcpyAsync(v, dv, bytes, cudaMemcpyDeviceToHost, be->stream));
+    FTC_CUDA(cudaStreamSynchronize(be->stream));
+    return ok();
+}
+
+int ftc_backend_kv_write(ftc_backend* be, int64_t layer, int64_t pos0, int64_t n, const float* k,
+                         const float* v) {
+    int rc = bind(be);
+    if (rc) return rc;
+    FTC_REQUIRE(k && v, FTC_E_INVALID, "ftc_backend_kv_write: null pointer");
+    std::lock_guard<std::mutex> lk(be->mu);
+    float *dk, *dv;
+    if ((rc = kv_rows(be, layer, pos0, n, &dk, &dv, "ftc_backend_kv_write"))) return rc;
+    const size_t bytes = (size_t)(n * be->kv_dim) * sizeof(float);
+    FTC_CUDA(cudaMemcpyAsync(dk, k, bytes, cudaMemcpyHostToDevice, be->stream));
+    FTC_CUDA(cudaMemcpyAsync(dv, v, bytes, cudaMemcpyHostToDevice, be->stream));
+    FTC_CUDA(cudaStreamSynchronize(be->stream));  // the host buffers may go after the call
+    return ok();
+}
+
 int ftc_backend_matmul_down_axpy(ftc_backend* be, const float* x, int64_t M, int64_t n_in,
                                  const void* w_host, int dtype, int64_t N, float* y) {
     int rc = bind(be);

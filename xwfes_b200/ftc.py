@@ -78,6 +78,8 @@ SIGNATURES = {
     "ftc_backend_kv_alloc": (C.c_int, [_p, _i64, _i64, _i64]),
     "ftc_backend_attention": (C.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
                                         C.c_int, _p]),
+    "ftc_backend_kv_read": (C.c_int, [_p, _i64, _i64, _i64, _p, _p]),
+    "ftc_backend_kv_write": (C.c_int, [_p, _i64, _i64, _i64, _p, _p]),
 }
 
 
@@ -681,6 +683,24 @@ class CudaBackend:
                                           1 if write_kv else 0, out.ctypes.data),
               "ftc_backend_attention")
         return out
+
+    def kv_read(self, layer, pos0, n, dim):
+        """Rows [pos0, pos0+n) of a layer of the device KV cache -> (k, v)
+        host arrays [n, dim] (the engine's prefix-cache snapshot copy)."""
+        k = np.empty((n, dim), dtype=np.float32)
+        v = np.empty((n, dim), dtype=np.float32)
+        check(lib().ftc_backend_kv_read(self._h, layer, pos0, n, k.ctypes.data, v.ctypes.data),
+              "ftc_backend_kv_read")
+        return k, v
+
+    def kv_write(self, layer, pos0, k, v):
+        """Host rows k, v [n, dim] into rows [pos0, pos0+n) of a layer of the
+        device KV cache (the engine's prefix-cache restore copy)."""
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        assert k.shape == v.shape and k.ndim == 2
+        check(lib().ftc_backend_kv_write(self._h, layer, pos0, k.shape[0], k.ctypes.data,
+                                         v.ctypes.data), "ftc_backend_kv_write")
 
     def matmul_sequence(self, calls):
         """A fixed list of ``matmul`` calls, ``calls`` = [(x, M, K, W, y), ...]

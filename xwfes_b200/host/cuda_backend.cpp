@@ -130,6 +130,15 @@ void CudaBackend::attention(int64_t layer, int64_t base, int64_t M, int64_t n_he
           "attention");
 }
 
+void CudaBackend::kv_read(int64_t layer, int64_t pos0, int64_t n, float* k, float* v) {
+    check(ftc_backend_kv_read(be_, layer, pos0, n, k, v), "kv_read");
+}
+
+void CudaBackend::kv_write(int64_t layer, int64_t pos0, int64_t n, const float* k,
+                           const float* v) {
+    check(ftc_backend_kv_write(be_, layer, pos0, n, k, v), "kv_write");
+}
+
 void CudaBackend::upload(const HostTensor& t) {
     const size_t n = t.nbytes ? t.nbytes
                               : t.slice_bytes() * (size_t)t.ne[2] * (size_t)t.ne[3];

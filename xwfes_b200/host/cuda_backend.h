@@ -93,6 +93,11 @@ public:
     void attention(int64_t layer, int64_t base, int64_t M, int64_t n_head, int64_t n_head_kv,
                    int64_t head_dim, const float* q, const float* k, const float* v,
                    bool write_kv, float* attout);
+    // Rows [pos0, pos0 + n) of a layer of the device cache to / from host
+    // [n][dim] buffers: the copies of the engine's prefix cache
+    // (ft/src/engine.cpp:608-616 restore, 630-645 snapshot).
+    void kv_read(int64_t layer, int64_t pos0, int64_t n, float* k, float* v);
+    void kv_write(int64_t layer, int64_t pos0, int64_t n, const float* k, const float* v);
 
     // Load a tensor's blocks into HBM once (call at Engine::load time).  The
     // host blocks must stay mapped and unchanged until evict() or the
