@@ -29,6 +29,7 @@
 // the rotation in float with every product and sum rounded separately (no
 // fused multiply-add), so it matches the reference's float arithmetic.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -313,8 +314,18 @@ size_t attn_smem(int HD, int G) {
     return (size_t)(2 * kChunk * (2 * HD + 4) + G * HD + G * kChunk + 3 * G) * sizeof(float);
 }
 
+// CTAs of attn_split<HD, G> one SM holds at once, queried once per device
+// (the attribute and the occupancy belong to the device's context).
 template <int HD, int G>
 int resident_ctas() {
+    static std::mutex mu;
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = -1;
+    if (dev >= 0) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (cached[dev]) return cached[dev];
+    }
     int n = 0;
     const size_t smem = attn_smem(HD, G);
     const int rc = opt_in_smem(reinterpret_cast<const void*>(attn_split<HD, G>), (int)smem,
@@ -324,6 +335,10 @@ int resident_ctas() {
             cudaSuccess ||
         n < 1)
         return 1;
+    if (dev >= 0) {
+        std::lock_guard<std::mutex> lk(mu);
+        cached[dev] = n;
+    }
     return n;
 }
 
