@@ -745,6 +745,12 @@ def time_tp(dev, world, rank, seed=0):
             "scaling": "strong (the whole block's work is split over the GPUs)",
             "weight_bytes": tp.weight_bytes(d), "weight_copies_rotated": copies,
             "kernels": "M<=8: decode GEMV (fp32); M>8: tcgen05 GEMM on row-scaled fp16",
+            "limits": {"1": "per-launch start-up of the rank's decode GEMVs (~3-4 us each, "
+                            "activation planes built after the dependency wait) and the "
+                            "allreduce waits fused into the o and down GEMVs",
+                       "16": "the small-M tcgen05 GEMM on the rank's shards (dequant-bound, "
+                             "cut tiles) and the one-shot peer allreduces",
+                       "1024": "two fp32 NCCL allreduces of 33.5 MB and mid-sized rank GEMMs"},
             **({"note": peer_note} if peer_note else {}),
             "per_M": out}
 
